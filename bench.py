@@ -1,0 +1,369 @@
+"""Benchmark: MoE decode µs/token over the 48-layer qwen4exp MoE stack.
+
+Default (N=1): BASELINE config 2 -- 48 independent seeded layers (hidden 2048,
+inter 512, 512 experts, top-10, shared expert, IQ4_XS; ~41 GB resident),
+batch-1 decode, one token per step, a fresh synthetic x per step.  A step is
+one replay of the CUDA graph of the whole stack.
+
+  value     device time per token (CUDA events around K steps, max over ranks),
+            inputs already in HBM
+  e2e       the same through the public API with host buffers: per step the
+            pinned host x is copied in, the stack runs, the fp32 output is read
+            back and the host waits for it
+  roofline  the dominant kernel (gate|up + SwiGLU): its algorithmic bytes per
+            launch / its average duration from CUDA events in this run
+  cpu_baseline  the CPU oracle (a restatement of reference/model.py:387-417
+            with cold IQ4_XS dequant) on a bounded sample of layers, scaled
+            to 48 layers
+
+N > 1 (torchrun): the stack sharded over N GPUs (--variant B by default:
+intermediate rows; A: expert ids), one NCCL all-reduce per layer inside the
+graph; the metric stays µs per token (total work fixed: "strong" scaling).
+
+`--impl reference` times the CPU oracle port with every host thread on the
+same metric (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE decode µs/token (48 layers, batch 1); achieved HBM GB/s vs 8 TB/s peak"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(f"/tmp/qmoe_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        if self.proc is None or not self.path.exists():
+            return None
+        rows = []
+        for line in self.path.read_text().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[5:9]))
+            except ValueError:
+                continue
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the oracle port; test infrastructure used only as the timed
+# CPU arm)
+
+def cpu_baseline(cfg, n_layers_sample: int, budget_s: float, seed: int = 0) -> dict:
+    import numpy as np
+
+    from oracle import moe_ref
+
+    pkg = load_pkg()
+    threads = moe_ref.threads()
+    hls = [pkg.synth_host_layer(cfg, layer=l, seed=seed) for l in range(n_layers_sample)]
+    srcs = [moe_ref.ExpertSource.from_host_layer(h) for h in hls]
+    x0 = pkg.synth_x(cfg, 1, seed=seed).float().numpy()
+    # untimed pass: generates the experts this input selects (weight setup)
+    x = x0
+    for s in srcs:
+        x = moe_ref.moe_forward(x, s, cfg.top_k)["out"]
+    per_layer = []
+    t_end = time.perf_counter() + budget_s
+    calls = 0
+    while time.perf_counter() < t_end or calls < 2:
+        x = x0
+        for s in srcs:
+            t0 = time.perf_counter()
+            x = moe_ref.moe_forward(x, s, cfg.top_k)["out"]   # cold: dequantises its 11 experts
+            per_layer.append(time.perf_counter() - t0)
+        calls += 1
+    us_layer = statistics.median(per_layer) * 1e6
+    return {
+        "value": us_layer * cfg.n_layers, "unit": "us/token", "cores": threads, "kind": "port",
+        "sample": f"{len(per_layer)} layer calls ({n_layers_sample} seeded layers x {calls}), batch 1, "
+                  f"cold IQ4_XS dequant of the selected experts each call, median per layer x {cfg.n_layers}",
+    }
+
+
+def physical_gpu(local_rank: int) -> int:
+    """nvidia-smi index of this process's GPU (CUDA_VISIBLE_DEVICES remaps)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in vis.split(",") if v.strip()]
+    if local_rank < len(ids) and ids[local_rank].isdigit():
+        return int(ids[local_rank])
+    return local_rank
+
+
+def load_pkg():
+    import __graft_entry__
+
+    return __graft_entry__.load_package()
+
+
+# ---------------------------------------------------------------------------
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--tokens", type=int, default=1, help="tokens per step (1 = decode; 4/8 = verify)")
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--variant", default="B", choices=["A", "B"])
+    ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline sampling")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+
+    pkg = load_pkg()
+    cfg = pkg.MoEConfig(n_layers=args.layers)
+    shard = pkg.Shard(args.variant, rank, world) if world > 1 else pkg.Shard()
+    M = args.tokens
+
+    layers = [pkg.synth_device_layer(cfg, l, seed=0, shard=shard, device=dev) for l in range(cfg.n_layers)]
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        from importlib import import_module
+
+        ShardedMoEStack = import_module(pkg.__name__ + ".dist").ShardedMoEStack
+        stack = ShardedMoEStack(layers, max_tokens=max(M, 1))
+        out_buf = stack.act
+    else:
+        stack = pkg.MoEStack(layers, max_tokens=max(M, 1))
+        out_buf = stack.out
+
+    n_x = args.warmup + args.steps
+    xs = torch.stack([pkg.synth_x(cfg, M, seed=1000 + i) for i in range(n_x)]).to(dev)   # [n, M, D] bf16
+    g = stack.graph(M)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    # ---- device-resident timing ----
+    for i in range(args.warmup):
+        stack.x_in[:M].copy_(xs[i])
+        g.replay()
+    barrier()
+    torch.cuda.synchronize(dev)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu(local_rank)) as clk:
+        barrier()
+        torch.cuda.synchronize(dev)
+        start.record()
+        for i in range(args.steps):
+            stack.x_in[:M].copy_(xs[args.warmup + i])
+            g.replay()
+        stop.record()
+        torch.cuda.synchronize(dev)
+        barrier()
+    ms = start.elapsed_time(stop)
+    clocks = clk.summary()
+
+    # ---- end to end: pinned host in, host read of the result each step ----
+    x_host = [xs[i].cpu().pin_memory() for i in range(n_x)]
+    out_host = torch.empty(M, cfg.hidden, dtype=torch.float32).pin_memory()
+    for i in range(args.warmup):
+        stack.x_in[:M].copy_(x_host[i], non_blocking=True)
+        g.replay()
+        out_host.copy_(out_buf[:M], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        stack.x_in[:M].copy_(x_host[args.warmup + i], non_blocking=True)
+        g.replay()
+        out_host.copy_(out_buf[:M], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms_e2e = e0.elapsed_time(e1)
+
+    # ---- per-kernel durations for the roofline (eager, events per stage) ----
+    stage = stage_timings(pkg, layers, xs[0], M, dev, reps=2)
+
+    if world > 1:
+        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = t.tolist()
+        stack.release()
+
+    if rank == 0:
+        hbm, hbm_kind = peaks()
+        ms_step = ms / args.steps
+        us_tok = ms_step * 1000.0 / M
+        bytes_tok = cfg.n_layers * cfg.layer_expert_bytes() / max(world, 1) if M == 1 else None
+        gu_bytes = (cfg.top_k + (1 if shard.has_shared() else 0)) * 2 * shard.dims(cfg).inter_local * cfg.gate_up_row_bytes
+        gu_gbs = gu_bytes / (stage["gateup_us"] * 1e-6) / 1e9
+        line = {
+            "metric": METRIC, "value": round(us_tok, 3), "unit": "us/token", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": False, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "iq4xs weights, bf16 activations, fp32 accumulate",
+            "data": "synthetic: seeded N(0,0.02) weights quantised to IQ4_XS, x ~ N(0,1) bf16, fresh x per step",
+            "config": {
+                "workload": f"BASELINE config {'2' if M == 1 else '3'}: {cfg.n_layers}-layer MoE stack, "
+                            f"{M} token(s)/step, hidden {cfg.hidden}, inter {cfg.inter}, {cfg.n_experts} experts, "
+                            f"top-{cfg.top_k} + shared",
+                "tokens_per_step": M, "layers": cfg.n_layers,
+                "parallelism": f"variant {args.variant} x{world}" if world > 1 else "1 GPU",
+                "l2": "inputs larger than L2: ~1.08 GB of weights read per token vs 126 MB L2",
+            },
+            "e2e": {"value": round(ms_e2e / args.steps * 1000.0 / M, 3), "unit": "us/token",
+                    "h2d_bytes_per_step": M * cfg.hidden * 2, "d2h_bytes_per_step": M * cfg.hidden * 4},
+            "gpu_launches": 3 * cfg.n_layers * args.steps,
+            "roofline": {
+                "kernel": "gateup_swiglu", "bound": "hbm", "achieved": round(gu_gbs, 1), "peak": hbm,
+                "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(gu_gbs / hbm, 4), "traffic": None,
+                "bytes_per_launch": gu_bytes, "avg_launch_us": round(stage["gateup_us"], 3),
+            },
+            "stage_us": {k: round(v, 3) for k, v in stage.items()},
+            "clocks": clocks,
+        }
+        if bytes_tok:
+            gbs = bytes_tok / (us_tok * 1e-6) / 1e9
+            line["step_hbm"] = {
+                "expert_bytes_per_token": bytes_tok, "achieved_gbs": round(gbs, 1),
+                "frac_of_8tbs": round(gbs / NOMINAL_HBM_GBS, 4), f"frac_of_{hbm_kind}": round(gbs / hbm, 4),
+                "bytes_with_router": bytes_tok + cfg.n_layers * (cfg.router_bytes + cfg.hidden * 4),
+            }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg, n_layers_sample=2, budget_s=args.cpu_budget)
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def stage_timings(pkg, layers, x, M: int, dev, reps: int = 2) -> dict:
+    """Average duration of each stage launch over all layers, CUDA events on the
+    launching stream (eager calls through the stage entry points)."""
+    import torch
+
+    mls = [pkg.MoELayer(l, max_tokens=max(M, 1)) for l in layers]
+    x = x.contiguous()
+    acc = {"route_us": [], "gateup_us": [], "down_us": []}
+    for _ in range(reps + 1):
+        for ml in mls:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
+            ids, w, sl = ml.route(x)
+            ev[1].record()
+            h = ml.gate_up(x, ids)
+            ev[2].record()
+            ml.down(h, ids, w, sl)
+            ev[3].record()
+            torch.cuda.synchronize(dev)
+            acc["route_us"].append(ev[0].elapsed_time(ev[1]) * 1000)
+            acc["gateup_us"].append(ev[1].elapsed_time(ev[2]) * 1000)
+            acc["down_us"].append(ev[2].elapsed_time(ev[3]) * 1000)
+    n = len(mls)
+    return {k: statistics.mean(v[n:]) for k, v in acc.items()}  # first pass is warm-up
+
+
+def run_reference_arm(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    pkg = load_pkg()
+    cfg = pkg.MoEConfig(n_layers=args.layers)
+    from oracle import moe_ref
+
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(cfg, n_layers_sample=1, budget_s=0.0, seed=i % 2)
+        if i >= args.warmup:
+            per_step.append(r["value"])
+    v = statistics.median(per_step)
+    line = {
+        "metric": METRIC, "value": round(v, 1), "unit": "us/token", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(v / 1000.0, 3), "higher_is_better": False,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "impl": "reference",
+        "dtype": "iq4xs weights, fp32 compute", "data": "synthetic (host-family seeded weights)",
+        "config": {"workload": f"BASELINE config 2 sampled: one layer per step, scaled to {cfg.n_layers} layers",
+                   "tokens_per_step": 1, "layers": cfg.n_layers},
+        "cpu_baseline": {"value": round(v, 1), "unit": "us/token", "cores": moe_ref.threads(), "kind": "port",
+                         "sample": "one seeded layer per step (cold IQ4_XS dequant of the 11 experts used), "
+                                   f"median over {args.steps} steps, x {cfg.n_layers} layers"},
+        "e2e": {"value": round(v, 1), "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

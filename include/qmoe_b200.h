@@ -1,0 +1,173 @@
+/*
+ * qmoe_b200.h -- C ABI of the B200 (sm_100a) qwen4exp MoE block.
+ *
+ * Plain pointers and sizes only.  Every pointer named "device" must point to
+ * CUDA device memory of the current device; `stream` is a cudaStream_t passed
+ * as void* (NULL = legacy default stream).  Every function returns an int
+ * status (QMOE_OK = 0); qmoe_status_string() names it.  Kernels never trap:
+ * device-side range violations (an expert id outside [0, n_experts)) are
+ * recorded in the workspace status word and read back by qmoe_read_status().
+ *
+ * Weight formats (all little-endian, GGUF byte order):
+ *   - router:   fp32 [n_experts, hidden] row-major       (blk.L.ffn_gate_inp.weight)
+ *   - gate_vec: fp32 [hidden]                             (blk.L.ffn_gate_inp_shexp.weight)
+ *   - gate_up:  IQ4_XS, per local expert 2*inter_local rows of `hidden`
+ *               values: gate rows [0, inter_local) then up rows
+ *               [inter_local, 2*inter_local).  Row = hidden/256 super-blocks of
+ *               136 bytes (blk.L.ffn_gate_exps / ffn_up_exps, rows concatenated).
+ *   - down:     IQ4_XS row slices, per local expert `hidden` rows; a row holds
+ *               `down_nseg` segments of (8-byte super-block header + down_nsub
+ *               sub-blocks of 16 bytes of qs).  Unsliced rows (n_seg = inter/256,
+ *               n_sub = 8) are exactly the GGUF bytes of blk.L.ffn_down_exps.
+ * The shared expert uses the same formats with one expert.
+ */
+#ifndef QMOE_B200_H
+#define QMOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum qmoe_status_code {
+    QMOE_OK = 0,
+    QMOE_ERR_INVALID_ARG = 1,      /* null pointer, negative size, bad enum        */
+    QMOE_ERR_UNSUPPORTED = 2,      /* shape outside what the kernels are built for */
+    QMOE_ERR_ALIGNMENT = 3,        /* a pointer breaks the 16-byte alignment rule  */
+    QMOE_ERR_WORKSPACE = 4,        /* workspace missing or too small               */
+    QMOE_ERR_CUDA = 5,             /* a CUDA runtime call failed                   */
+    QMOE_ERR_DEVICE_RANGE = 6,     /* a kernel saw an expert id out of range       */
+    QMOE_ERR_NOT_FINITE = 7        /* a kernel saw a non-finite router logit       */
+};
+
+/* Activation element types accepted by the entry points. */
+enum qmoe_act_dtype {
+    QMOE_ACT_BF16 = 0,   /* bf16 activations (the reference's device dtype)        */
+    QMOE_ACT_F32 = 1     /* fp32, rounded to bf16 on load (layer chaining)         */
+};
+
+/* One layer's weights.  sh_* may be NULL: no shared expert on this rank. */
+typedef struct qmoe_layer_weights {
+    const float* router;        /* [n_experts, hidden] fp32                        */
+    const float* gate_vec;      /* [hidden] fp32 or NULL (no shared expert)        */
+    const void* gate_up;        /* local routed experts, IQ4_XS                    */
+    const void* down;           /* local routed experts, IQ4_XS row slices         */
+    const void* sh_gate_up;     /* shared expert gate|up or NULL                   */
+    const void* sh_down;        /* shared expert down or NULL                      */
+} qmoe_layer_weights;
+
+/* Shapes and the shard this rank holds.
+ *   variant A (expert axis):        expert_lo/expert_hi = this rank's window.
+ *   variant B (intermediate axis):  inter_local = inter/n, down_ib0/down_nsub
+ *                                   describe the column slice of each down row. */
+typedef struct qmoe_dims {
+    int hidden;          /* D: multiple of 256, <= 4096                          */
+    int inter;           /* I: full expert intermediate (multiple of 256)        */
+    int n_experts;       /* E: multiple of 32, <= 1024                           */
+    int top_k;           /* k: 1..16                                             */
+    int expert_lo;       /* first local expert id                                */
+    int expert_hi;       /* one past the last local expert id (== lo: none)      */
+    int inter_local;     /* rows of gate (and of up) held per routed expert     */
+    int down_nseg;       /* segments per routed down row                         */
+    int down_nsub;       /* 32-value sub-blocks per segment (1..8)               */
+    int down_ib0;        /* first sub-block index inside the super-block          */
+    int sh_inter_local;  /* shared expert rows of gate per rank (0 = none)       */
+    int sh_down_nseg;
+    int sh_down_nsub;
+    int sh_down_ib0;
+} qmoe_dims;
+
+/* ---- library ------------------------------------------------------------ */
+const char* qmoe_status_string(int status);
+int qmoe_version(void);
+/* Largest token count the decode/verify (GEMV) kernels accept. */
+int qmoe_max_tokens(void);
+
+/* Workspace bytes for calls with up to `max_tokens` rows.  The workspace must
+ * be zero-filled once before first use (qmoe_workspace_init). */
+size_t qmoe_workspace_bytes(const qmoe_dims* dims, int max_tokens);
+int qmoe_workspace_init(void* workspace, size_t bytes, void* stream);
+/* Copies the device status word to *status_out (synchronising `stream`) and
+ * clears it.  *status_out is QMOE_OK or a QMOE_ERR_* code. */
+int qmoe_read_status(void* workspace, int* status_out, void* stream);
+
+/* ---- IQ4_XS ------------------------------------------------------------- */
+/* Replaces gguf/quants.py:112-129 (_dequant_iq4_xs) through dequantize()
+ * (gguf/quants.py:214).  blocks: device, n_blocks*136 bytes; out: device
+ * fp32, n_blocks*256 values.  Bit-exact with the reference. */
+int qmoe_dequant_iq4xs_f32(const void* blocks, int64_t n_blocks, float* out, void* stream);
+
+/* Synthetic-weight builder (the reference converts a real checkpoint with
+ * tt/convert.py:151; this project generates seeded weights instead).
+ * Host quantiser: fp32 -> IQ4_XS, n_values a multiple of 256. */
+int qmoe_quantize_iq4xs_host(const float* values, int64_t n_values, void* out_blocks, int n_threads);
+/* Same quantiser on the device (bit-identical to the host one). */
+int qmoe_quantize_iq4xs(const float* values, int64_t n_values, void* out_blocks, void* stream);
+/* Device generator: N(0, std^2) values from a counter-based RNG keyed by
+ * (seed, stream_id), quantised to IQ4_XS (synth_iq4xs) or kept fp32. */
+int qmoe_synth_iq4xs(uint64_t seed, uint64_t stream_id, int64_t n_values, float std_dev,
+                     void* out_blocks, void* stream);
+int qmoe_synth_f32(uint64_t seed, uint64_t stream_id, int64_t n_values, float std_dev,
+                   float* out, void* stream);
+
+/* ---- the MoE block, by stage --------------------------------------------- */
+/* Router + top-k + renormalise.  Replaces reference/model.py:399-403 and the
+ * device pair tt/moe.py:199-237 (ksgemv router, softmax, fused_router_select /
+ * scripts/kernels/router_select.cpp:159-273 with EXACT_TOPK).  Selection is on
+ * fp32 logits, ties to the lower expert id; weights are the softmax over the
+ * k selected, in descending order.  ids/weights: device [M, k];
+ * shared_logit: device [M] (x . gate_vec, before the sigmoid) or NULL. */
+int qmoe_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+               const qmoe_dims* dims, int32_t* ids, float* weights, float* shared_logit,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Gathered gate|up GEMV + SwiGLU over the selected experts and the shared one.
+ * Replaces tt/moe.py:946-953 (gather_gemv MODE 2 + fused_swiglu) and the
+ * shared half of tt/moe.py:999-1028.  h: device fp32 [M, k+1, h_stride]; slot
+ * k holds the shared expert. */
+int qmoe_gateup_swiglu(const void* x, int x_dtype, int n_tokens, const int32_t* ids,
+                       const qmoe_layer_weights* w, const qmoe_dims* dims, float* h,
+                       int h_stride, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Gathered down GEMV fused with the routing-weighted sum and the
+ * sigmoid-gated shared expert.  Replaces tt/moe.py:958-975 (gather_gemv
+ * MODE 0, the combine) and tt/moe.py:1029-1044.  out: device fp32 [M, hidden]
+ * (this rank's partial sum when sharded). */
+int qmoe_down_combine(const float* h, int h_stride, int n_tokens, const int32_t* ids,
+                      const float* weights, const float* shared_logit,
+                      const qmoe_layer_weights* w, const qmoe_dims* dims, float* out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* The whole block: routed experts + shared expert, x [M, hidden] -> out fp32
+ * [M, hidden].  Replaces TTModel._moe_block (tt/model.py:2010-2052: moe_block
+ * tt/moe.py:159 + shared_expert tt/moe.py:983) before its all-reduce, and the
+ * oracle Qwen4ExpModel._moe (reference/model.py:387-417). */
+int qmoe_moe_block(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                   const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* The shared expert alone: sigmoid(x . gate_vec) * down(silu(gate x) * up x).
+ * Replaces tt/moe.py:983-1044 (shared_expert) and reference/model.py:392-397.
+ * Uses gate_vec, sh_gate_up and sh_down of `w`; routed fields are ignored. */
+int qmoe_shared_expert(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                       const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* A stack of n_layers blocks, the output of layer L (rounded to bf16) feeding
+ * layer L+1; the per-layer MoE calls of TTModel.step (tt/model.py:2056,
+ * 48 x _moe_block) with nothing between them.  layers: host array of
+ * n_layers weight sets; x: device bf16 [M, hidden]; out: device fp32
+ * [M, hidden] (the last layer's output); act: device fp32 scratch
+ * [M, hidden] or NULL (then `out` is used).  Stream-ordered, no host sync,
+ * no allocation: capturable into a CUDA graph. */
+int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* layers,
+                      int n_layers, const qmoe_dims* dims, float* out, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QMOE_B200_H */

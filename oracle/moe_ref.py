@@ -1,0 +1,198 @@
+"""TEST INFRASTRUCTURE ONLY -- the CPU oracle of the qwen4exp MoE block.
+
+Only tests/, `__graft_entry__.smoke()` and bench.py's CPU-baseline leg may
+import this module, and only as the checker (or the timed CPU baseline); the
+product path never calls it.
+
+A numpy restatement of the reference's plain-PyTorch CPU MoE,
+`Qwen4ExpModel._moe` (ttrunner_qwen38_flash_next/reference/model.py:387-417),
+on weights served by a `WeightStore`-like source that dequantises one
+expert at a time (reference/weights.py:118-179).  IQ4_XS decoding is the C
+restatement in iq4xs_ref.c (gguf/quants.py:112-129).
+
+Pinning: tests/golden/ holds outputs of the reference itself (imported in the
+development container and run on the same seeded IQ4_XS bytes) and of its
+dequantiser; tests/test_oracle.py checks this module against them.
+
+The one deliberate difference from the reference is the tie rule of top-k:
+the reference's `torch.topk` (model.py:401) does not break ties by lower
+index on CPU, so the oracle canonicalises to a stable (-p, index) order -- the
+rule of the reference's own device kernel (scripts/kernels/router_select.cpp
+:163-164).  `raw_topk_differs` reports when that changes the selected set.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+_SO = HERE / "liboracle_iq4xs.so"
+
+
+def build() -> Path:
+    """Compile the C restatement (make in this directory)."""
+    src = HERE / "iq4xs_ref.c"
+    if not _SO.exists() or _SO.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return _SO
+
+
+_lib = None
+
+
+def _c() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        _lib = ctypes.CDLL(str(build()))
+        _lib.oracle_dequant_iq4xs.restype = None
+        _lib.oracle_dequant_iq4xs.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+    return _lib
+
+
+def dequant_iq4xs(raw: np.ndarray) -> np.ndarray:
+    """IQ4_XS bytes [..., n_sb*136] -> fp32 [..., n_sb*256] (quants.py:112-129)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    if raw.shape[-1] % 136:
+        raise ValueError("last dimension is not a whole number of 136-byte super-blocks")
+    nb = raw.size // 136
+    out = np.empty(raw.shape[:-1] + (raw.shape[-1] // 136 * 256,), dtype=np.float32)
+    _c().oracle_dequant_iq4xs(raw.ctypes.data, nb, out.ctypes.data)
+    return out
+
+
+def dequant_iq4xs_numpy(raw: np.ndarray) -> np.ndarray:
+    """The same decode written with numpy array operations (a second restatement)."""
+    kv = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], dtype=np.int8)
+    b = np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1, 136)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    sh = b[:, 2:4].copy().view(np.uint16).astype(np.uint32)[:, 0]
+    sl = b[:, 4:8].astype(np.uint32)
+    qs = b[:, 8:136]
+    out = np.empty((b.shape[0], 256), dtype=np.float32)
+    for ib in range(8):
+        ls = ((sl[:, ib // 2] >> (4 * (ib % 2))) & 0xF) | (((sh >> (2 * ib)) & 3) << 4)
+        dl = d * (ls.astype(np.float32) - np.float32(32.0))
+        q = qs[:, ib * 16:(ib + 1) * 16]
+        out[:, ib * 32:ib * 32 + 16] = kv[q & 0xF] * dl[:, None]
+        out[:, ib * 32 + 16:ib * 32 + 32] = kv[q >> 4] * dl[:, None]
+    return out.reshape(raw.shape[:-1] + (raw.shape[-1] // 136 * 256,))
+
+
+def _silu(v: np.ndarray) -> np.ndarray:
+    return v / (np.float32(1.0) + np.exp(-v))
+
+
+def _sigmoid(v: np.ndarray) -> np.ndarray:
+    return np.float32(1.0) / (np.float32(1.0) + np.exp(-v))
+
+
+def softmax(logits: np.ndarray) -> np.ndarray:
+    """fp32 softmax over the last axis (model.py:400)."""
+    z = logits - logits.max(axis=-1, keepdims=True)
+    e = np.exp(z, dtype=np.float32)
+    return (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+
+
+def topk_canonical(probs: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """The k largest per row, ties to the lower index, in descending order."""
+    order = np.argsort(-probs, axis=-1, kind="stable")[..., :k]
+    return np.take_along_axis(probs, order, -1), order.astype(np.int64)
+
+
+def route(x: np.ndarray, router: np.ndarray, k: int) -> dict:
+    """model.py:399-403: logits, probabilities, top-k and renormalised weights."""
+    logits = (x @ router.T).astype(np.float32)
+    probs = softmax(logits)
+    w, ids = topk_canonical(probs, k)
+    w = (w / w.sum(axis=-1, keepdims=True)).astype(np.float32)
+    return {"logits": logits, "probs": probs, "ids": ids, "weights": w}
+
+
+def raw_topk_differs(probs: np.ndarray, ids: np.ndarray, k: int) -> np.ndarray:
+    """Rows whose `torch.topk` selection differs as a set from the canonical one."""
+    import torch
+
+    raw = torch.topk(torch.from_numpy(probs), k, dim=-1).indices.numpy()
+    return np.array([set(a) != set(b) for a, b in zip(raw.tolist(), ids.tolist())])
+
+
+class ExpertSource:
+    """Dequantising weight source in the role of WeightStore.get_rows
+    (reference/weights.py:118-179): experts come from `expert(e)` as IQ4_XS
+    bytes (gate|up [2I, rb], down [D, rb_dn]) and are decoded on each use."""
+
+    def __init__(self, expert, sh_gate_up: np.ndarray | None, sh_down: np.ndarray | None,
+                 router: np.ndarray, gate_vec: np.ndarray | None, inter: int, shared_inter: int):
+        self.expert = expert
+        self.sh_gate_up = sh_gate_up
+        self.sh_down = sh_down
+        self.router = router
+        self.gate_vec = gate_vec
+        self.inter = inter
+        self.shared_inter = shared_inter
+
+    @classmethod
+    def from_host_layer(cls, hl) -> "ExpertSource":
+        return cls(hl.expert, hl.sh_gate_up, hl.sh_down, hl.router, hl.gate_vec,
+                   hl.cfg.inter, hl.cfg.shared_inter)
+
+
+def moe_forward(x: np.ndarray, src: ExpertSource, k: int, with_shared: bool = True,
+                expert_window: tuple[int, int] | None = None,
+                inter_window: tuple[int, int] | None = None) -> dict:
+    """Qwen4ExpModel._moe (model.py:387-417) on flat fp32 x [M, D].
+
+    expert_window / inter_window restrict the routed experts to a variant-A
+    window or every expert (and the shared one) to a variant-B slice of the
+    intermediate axis: the partial sum a rank produces before the all-reduce.
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M = x.shape[0]
+    I, Ish = src.inter, src.shared_inter
+    lo, hi = inter_window if inter_window is not None else (0, I)
+    slo, shi = (lo * Ish // I, hi * Ish // I) if inter_window is not None else (0, Ish)
+
+    shared = np.zeros_like(x)
+    if with_shared and src.sh_gate_up is not None:                                   # :392-397
+        gu = dequant_iq4xs(src.sh_gate_up)
+        dn = dequant_iq4xs(src.sh_down)
+        h = _silu(x @ gu[slo:shi].T) * (x @ gu[Ish + slo:Ish + shi].T)
+        s = h @ dn[:, slo:shi].T
+        gate = _sigmoid(x @ src.gate_vec.reshape(-1, 1))
+        shared = (s * gate).astype(np.float32)
+
+    r = route(x, src.router, k)                                                      # :399-403
+    ids, weights = r["ids"], r["weights"]
+    out = np.zeros_like(x)
+    for e in np.unique(ids):                                                          # :407
+        e = int(e)
+        if expert_window is not None and not expert_window[0] <= e < expert_window[1]:
+            continue
+        slot, tok = np.nonzero(ids == e)                                             # :409
+        gu_b, dn_b = src.expert(e)
+        gu = dequant_iq4xs(gu_b)                                                      # :411-413
+        dn = dequant_iq4xs(dn_b)
+        xs = x[slot]
+        h = _silu(xs @ gu[lo:hi].T) * (xs @ gu[I + lo:I + hi].T)                      # :414
+        np.add.at(out, slot, (h @ dn[:, lo:hi].T) * weights[slot, tok, None])        # :415
+    r.update(out=(out + shared).astype(np.float32), routed=out, shared=shared)       # :417
+    return r
+
+
+def max_rel_err(got: np.ndarray, ref: np.ndarray) -> float:
+    """max|got - ref| / max|ref|, the reference harnesses' error metric
+    (scripts/stage3_swiglu_fusion.py:128-133)."""
+    denom = float(np.max(np.abs(ref)))
+    diff = float(np.max(np.abs(np.asarray(got, dtype=np.float64) - np.asarray(ref, dtype=np.float64))))
+    if denom == 0.0:
+        return 0.0 if diff == 0.0 else float("inf")
+    return diff / denom
+
+
+def threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)

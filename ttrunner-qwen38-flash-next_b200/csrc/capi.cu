@@ -1,0 +1,423 @@
+// extern "C" entry points: argument checks, workspace layout, launches.
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace qmoe {
+
+size_t gateup_smem_bytes(const ExpertArgs& a);
+size_t down_smem_bytes(const ExpertArgs& a);
+
+namespace {
+
+constexpr size_t kSmemLimit = 200 * 1024;  // dynamic shared memory ceiling per CTA
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+int check_dims(const qmoe_dims* d) {
+    if (!d) return QMOE_ERR_INVALID_ARG;
+    if (d->hidden < 256 || d->hidden > kMaxHidden || d->hidden % 256) return QMOE_ERR_UNSUPPORTED;
+    if (d->inter < 32 || d->inter % 32) return QMOE_ERR_UNSUPPORTED;
+    if (d->n_experts < 32 || d->n_experts > kMaxExperts || d->n_experts % 32) return QMOE_ERR_UNSUPPORTED;
+    if (d->top_k < 1 || d->top_k > kMaxTopK || d->top_k > d->n_experts) return QMOE_ERR_UNSUPPORTED;
+    if (d->expert_lo < 0 || d->expert_hi > d->n_experts || d->expert_lo > d->expert_hi)
+        return QMOE_ERR_INVALID_ARG;
+    if (d->inter_local < 32 || d->inter_local % 32 || d->inter_local > d->inter) return QMOE_ERR_UNSUPPORTED;
+    if (d->down_nseg < 1 || d->down_nsub < 1 || d->down_nsub > 8 || d->down_ib0 < 0 ||
+        d->down_ib0 + d->down_nsub > 8 || d->down_nseg * d->down_nsub * 32 != d->inter_local)
+        return QMOE_ERR_UNSUPPORTED;
+    if (d->sh_inter_local < 0 || d->sh_inter_local % 32 || d->sh_inter_local > 8192) return QMOE_ERR_UNSUPPORTED;
+    if (d->sh_inter_local > 0 &&
+        (d->sh_down_nseg < 1 || d->sh_down_nsub < 1 || d->sh_down_nsub > 8 || d->sh_down_ib0 < 0 ||
+         d->sh_down_ib0 + d->sh_down_nsub > 8 ||
+         d->sh_down_nseg * d->sh_down_nsub * 32 != d->sh_inter_local))
+        return QMOE_ERR_UNSUPPORTED;
+    return QMOE_OK;
+}
+
+int check_tokens(int M) { return (M >= 1 && M <= kMaxTokens) ? QMOE_OK : QMOE_ERR_UNSUPPORTED; }
+
+int check_act(const void* x, int x_dtype) {
+    if (!x) return QMOE_ERR_INVALID_ARG;
+    if (x_dtype != QMOE_ACT_BF16 && x_dtype != QMOE_ACT_F32) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(x, x_dtype == QMOE_ACT_F32 ? 4 : 2)) return QMOE_ERR_ALIGNMENT;
+    return QMOE_OK;
+}
+
+int check_weights_route(const qmoe_layer_weights* w) {
+    if (!w || !w->router) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(w->router, 16)) return QMOE_ERR_ALIGNMENT;
+    if (w->gate_vec && !aligned(w->gate_vec, 16)) return QMOE_ERR_ALIGNMENT;
+    return QMOE_OK;
+}
+
+int check_weights_experts(const qmoe_layer_weights* w, const qmoe_dims* d) {
+    if (!w) return QMOE_ERR_INVALID_ARG;
+    if (d->expert_hi > d->expert_lo) {  // an empty window holds no routed experts
+        if (!w->gate_up || !w->down) return QMOE_ERR_INVALID_ARG;
+        if (!aligned(w->gate_up, 8) || !aligned(w->down, 8)) return QMOE_ERR_ALIGNMENT;
+    }
+    if (d->sh_inter_local > 0) {
+        if (!w->sh_gate_up || !w->sh_down) return QMOE_ERR_INVALID_ARG;
+        if (!aligned(w->sh_gate_up, 8) || !aligned(w->sh_down, 8)) return QMOE_ERR_ALIGNMENT;
+    }
+    return QMOE_OK;
+}
+
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return QMOE_OK;
+    fprintf(stderr, "qmoe: CUDA error %s\n", cudaGetErrorString(e));
+    return QMOE_ERR_CUDA;
+}
+
+ExpertArgs expert_args(const void* x, int x_dtype, int M, const int32_t* ids, const float* weights,
+                       const float* shared_logit, const qmoe_layer_weights* w, const qmoe_dims* d,
+                       float* h, int h_stride, float* out, int* status) {
+    ExpertArgs a{};
+    a.x = x;
+    a.x_f32 = x_dtype == QMOE_ACT_F32;
+    a.M = M;
+    a.D = d->hidden;
+    a.k = d->top_k;
+    a.e_lo = d->expert_lo;
+    a.e_hi = d->expert_hi;
+    a.E = d->n_experts;
+    a.ids = ids;
+    a.weights = weights;
+    a.shared_logit = shared_logit;
+    a.gate_up = (const uint8_t*)w->gate_up;
+    a.I_loc = d->inter_local;
+    a.gu_expert_bytes = (size_t)2 * d->inter_local * (d->hidden / 256) * QMOE_SB_BYTES;
+    a.sh_gate_up = d->sh_inter_local > 0 ? (const uint8_t*)w->sh_gate_up : nullptr;
+    a.sh_I_loc = d->sh_inter_local;
+    a.h = h;
+    a.h_stride = h_stride;
+    a.down = (const uint8_t*)w->down;
+    a.dn_nseg = d->down_nseg;
+    a.dn_nsub = d->down_nsub;
+    a.dn_ib0 = d->down_ib0;
+    a.dn_expert_bytes = (size_t)d->hidden * d->down_nseg * (8 + 16 * d->down_nsub);
+    a.sh_down = d->sh_inter_local > 0 ? (const uint8_t*)w->sh_down : nullptr;
+    a.sh_nseg = d->sh_inter_local > 0 ? d->sh_down_nseg : 1;
+    a.sh_nsub = d->sh_inter_local > 0 ? d->sh_down_nsub : 1;
+    a.sh_ib0 = d->sh_inter_local > 0 ? d->sh_down_ib0 : 0;
+    a.out = out;
+    a.status = status;
+    return a;
+}
+
+int check_smem(const ExpertArgs& a) {
+    if (gateup_smem_bytes(a) > kSmemLimit || down_smem_bytes(a) > kSmemLimit) return QMOE_ERR_UNSUPPORTED;
+    return QMOE_OK;
+}
+
+int route_smem_ok(int M, int D) {
+    return (size_t)M * D * sizeof(float) <= kSmemLimit - 16 * 1024 ? QMOE_OK : QMOE_ERR_UNSUPPORTED;
+}
+
+struct Ws {
+    WsLayout L;
+    unsigned char* base;
+    int* status() const { return (int*)(base + L.status); }
+    unsigned int* counter() const { return (unsigned int*)(base + L.counter); }
+    float* logits() const { return (float*)(base + L.logits); }
+    int32_t* ids() const { return (int32_t*)(base + L.ids); }
+    float* weights() const { return (float*)(base + L.weights); }
+    float* shared() const { return (float*)(base + L.shared); }
+    float* h() const { return (float*)(base + L.h); }
+};
+
+int get_ws(void* workspace, size_t bytes, const qmoe_dims* d, int M, Ws* ws) {
+    if (!workspace) return QMOE_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return QMOE_ERR_ALIGNMENT;
+    ws->L = ws_layout(*d, M);
+    if (bytes < ws->L.total) return QMOE_ERR_WORKSPACE;
+    ws->base = (unsigned char*)workspace;
+    return QMOE_OK;
+}
+
+#define QMOE_TRY(expr)                 \
+    do {                               \
+        const int _rc = (expr);        \
+        if (_rc != QMOE_OK) return _rc; \
+    } while (0)
+
+int run_route(const void* x, int x_dtype, int M, const qmoe_layer_weights* w, const qmoe_dims* d,
+              int32_t* ids, float* weights, float* shared_logit, const Ws& ws, cudaStream_t s) {
+    RouteArgs r{};
+    r.x = x;
+    r.x_f32 = x_dtype == QMOE_ACT_F32;
+    r.M = M;
+    r.D = d->hidden;
+    r.E = d->n_experts;
+    r.k = d->top_k;
+    r.router = w->router;
+    r.gate_vec = w->gate_vec;
+    r.logits = ws.logits();
+    r.counter = ws.counter();
+    r.ids = ids;
+    r.weights = weights;
+    r.shared_logit = shared_logit;
+    r.status = ws.status();
+    return cuda_status(launch_route(r, s));
+}
+
+int run_block(const void* x, int x_dtype, int M, const qmoe_layer_weights* w, const qmoe_dims* d,
+              float* out, const Ws& ws, cudaStream_t s) {
+    QMOE_TRY(run_route(x, x_dtype, M, w, d, ws.ids(), ws.weights(), ws.shared(), ws, s));
+    ExpertArgs a = expert_args(x, x_dtype, M, ws.ids(), ws.weights(), ws.shared(), w, d, ws.h(),
+                               ws.L.h_stride, out, ws.status());
+    QMOE_TRY(cuda_status(launch_gateup(a, s)));
+    return cuda_status(launch_down(a, s));
+}
+
+}  // namespace
+
+WsLayout ws_layout(const qmoe_dims& d, int max_tokens) {
+    WsLayout L{};
+    const int M = max_tokens;
+    const int hmax = d.inter_local > d.sh_inter_local ? d.inter_local : d.sh_inter_local;
+    L.h_stride = (int)align_up((size_t)hmax, 32);
+    size_t off = 0;
+    L.status = off;
+    L.counter = off + 64;
+    off = 256;
+    L.logits = off;
+    off = align_up(off + (size_t)M * (d.n_experts + 1) * 4, 256);
+    L.ids = off;
+    off = align_up(off + (size_t)M * d.top_k * 4, 256);
+    L.weights = off;
+    off = align_up(off + (size_t)M * d.top_k * 4, 256);
+    L.shared = off;
+    off = align_up(off + (size_t)M * 4, 256);
+    L.h = off;
+    off = align_up(off + (size_t)M * (d.top_k + 1) * L.h_stride * 4, 256);
+    L.total = off;
+    return L;
+}
+
+int device_sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+    return n;
+}
+
+}  // namespace qmoe
+
+using namespace qmoe;
+
+extern "C" {
+
+const char* qmoe_status_string(int status) {
+    switch (status) {
+        case QMOE_OK: return "ok";
+        case QMOE_ERR_INVALID_ARG: return "invalid argument";
+        case QMOE_ERR_UNSUPPORTED: return "unsupported shape";
+        case QMOE_ERR_ALIGNMENT: return "misaligned pointer";
+        case QMOE_ERR_WORKSPACE: return "workspace missing or too small";
+        case QMOE_ERR_CUDA: return "CUDA runtime error";
+        case QMOE_ERR_DEVICE_RANGE: return "expert id out of range";
+        case QMOE_ERR_NOT_FINITE: return "non-finite router logit";
+        default: return "unknown status";
+    }
+}
+
+int qmoe_version(void) { return 1; }
+int qmoe_max_tokens(void) { return kMaxTokens; }
+
+size_t qmoe_workspace_bytes(const qmoe_dims* dims, int max_tokens) {
+    if (check_dims(dims) != QMOE_OK || check_tokens(max_tokens) != QMOE_OK) return 0;
+    return ws_layout(*dims, max_tokens).total;
+}
+
+int qmoe_workspace_init(void* workspace, size_t bytes, void* stream) {
+    if (!workspace) return QMOE_ERR_WORKSPACE;
+    return cuda_status(cudaMemsetAsync(workspace, 0, bytes, (cudaStream_t)stream));
+}
+
+int qmoe_read_status(void* workspace, int* status_out, void* stream) {
+    if (!workspace || !status_out) return QMOE_ERR_INVALID_ARG;
+    int v = 0;
+    cudaStream_t s = (cudaStream_t)stream;
+    QMOE_TRY(cuda_status(cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s)));
+    QMOE_TRY(cuda_status(cudaStreamSynchronize(s)));
+    QMOE_TRY(cuda_status(cudaMemsetAsync(workspace, 0, sizeof(int), s)));
+    *status_out = v;
+    return QMOE_OK;
+}
+
+int qmoe_dequant_iq4xs_f32(const void* blocks, int64_t n_blocks, float* out, void* stream) {
+    if (n_blocks < 0) return QMOE_ERR_INVALID_ARG;
+    if (n_blocks == 0) return QMOE_OK;
+    if (!blocks || !out) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(blocks, 8) || !aligned(out, 16)) return QMOE_ERR_ALIGNMENT;
+    return cuda_status(launch_dequant((const uint8_t*)blocks, n_blocks, out, (cudaStream_t)stream));
+}
+
+int qmoe_quantize_iq4xs(const float* values, int64_t n_values, void* out_blocks, void* stream) {
+    if (n_values < 0 || n_values % 256) return QMOE_ERR_INVALID_ARG;
+    if (n_values == 0) return QMOE_OK;
+    if (!values || !out_blocks) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(values, 16) || !aligned(out_blocks, 8)) return QMOE_ERR_ALIGNMENT;
+    return cuda_status(launch_quantize(values, n_values / 256, (uint8_t*)out_blocks, (cudaStream_t)stream));
+}
+
+int qmoe_synth_iq4xs(uint64_t seed, uint64_t stream_id, int64_t n_values, float std_dev,
+                     void* out_blocks, void* stream) {
+    if (n_values < 0 || n_values % 256) return QMOE_ERR_INVALID_ARG;
+    if (n_values == 0) return QMOE_OK;
+    if (!out_blocks) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(out_blocks, 8)) return QMOE_ERR_ALIGNMENT;
+    return cuda_status(launch_synth_iq4xs(seed, stream_id, n_values / 256, std_dev,
+                                          (uint8_t*)out_blocks, (cudaStream_t)stream));
+}
+
+int qmoe_synth_f32(uint64_t seed, uint64_t stream_id, int64_t n_values, float std_dev, float* out,
+                   void* stream) {
+    if (n_values < 0) return QMOE_ERR_INVALID_ARG;
+    if (n_values == 0) return QMOE_OK;
+    if (!out) return QMOE_ERR_INVALID_ARG;
+    return cuda_status(launch_synth_f32(seed, stream_id, n_values, std_dev, out, (cudaStream_t)stream));
+}
+
+int qmoe_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+               const qmoe_dims* dims, int32_t* ids, float* weights, float* shared_logit,
+               void* workspace, size_t workspace_bytes, void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_act(x, x_dtype));
+    QMOE_TRY(check_weights_route(w));
+    QMOE_TRY(route_smem_ok(n_tokens, dims->hidden));
+    if (!ids || !weights) return QMOE_ERR_INVALID_ARG;
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    return run_route(x, x_dtype, n_tokens, w, dims, ids, weights, shared_logit, ws, (cudaStream_t)stream);
+}
+
+int qmoe_gateup_swiglu(const void* x, int x_dtype, int n_tokens, const int32_t* ids,
+                       const qmoe_layer_weights* w, const qmoe_dims* dims, float* h, int h_stride,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_act(x, x_dtype));
+    QMOE_TRY(check_weights_experts(w, dims));
+    if (!ids || !h) return QMOE_ERR_INVALID_ARG;
+    if (h_stride < dims->inter_local || h_stride < dims->sh_inter_local) return QMOE_ERR_INVALID_ARG;
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    ExpertArgs a = expert_args(x, x_dtype, n_tokens, ids, nullptr, nullptr, w, dims, h, h_stride,
+                               nullptr, ws.status());
+    QMOE_TRY(check_smem(a));
+    return cuda_status(launch_gateup(a, (cudaStream_t)stream));
+}
+
+int qmoe_down_combine(const float* h, int h_stride, int n_tokens, const int32_t* ids,
+                      const float* weights, const float* shared_logit, const qmoe_layer_weights* w,
+                      const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_weights_experts(w, dims));
+    if (!h || !ids || !weights || !out) return QMOE_ERR_INVALID_ARG;
+    if (h_stride < dims->inter_local || h_stride < dims->sh_inter_local) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(h, 16) || h_stride % 4) return QMOE_ERR_ALIGNMENT;
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    ExpertArgs a = expert_args(nullptr, QMOE_ACT_F32, n_tokens, ids, weights, shared_logit, w, dims,
+                               (float*)h, h_stride, out, ws.status());
+    QMOE_TRY(check_smem(a));
+    return cuda_status(launch_down(a, (cudaStream_t)stream));
+}
+
+int qmoe_moe_block(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                   const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_act(x, x_dtype));
+    QMOE_TRY(check_weights_route(w));
+    QMOE_TRY(check_weights_experts(w, dims));
+    QMOE_TRY(route_smem_ok(n_tokens, dims->hidden));
+    if (!out) return QMOE_ERR_INVALID_ARG;
+    // out may alias an fp32 x: the router and gate|up launches finish reading
+    // x before the down launch writes out (stream order).
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    ExpertArgs probe = expert_args(x, x_dtype, n_tokens, nullptr, nullptr, nullptr, w, dims, ws.h(),
+                                   ws.L.h_stride, out, nullptr);
+    QMOE_TRY(check_smem(probe));
+    return run_block(x, x_dtype, n_tokens, w, dims, out, ws, (cudaStream_t)stream);
+}
+
+int qmoe_shared_expert(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                       const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_act(x, x_dtype));
+    if (!w || !w->gate_vec || !w->sh_gate_up || !w->sh_down || !out) return QMOE_ERR_INVALID_ARG;
+    if (dims->sh_inter_local <= 0) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(w->gate_vec, 16) || !aligned(w->sh_gate_up, 8) || !aligned(w->sh_down, 8))
+        return QMOE_ERR_ALIGNMENT;
+    QMOE_TRY(route_smem_ok(n_tokens, dims->hidden));
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    qmoe_dims d = *dims;  // no routed experts: an empty window
+    d.expert_lo = d.expert_hi = 0;
+    qmoe_layer_weights sw = *w;
+    sw.gate_up = sw.down = nullptr;
+    cudaStream_t s = (cudaStream_t)stream;
+    RouteArgs r{};
+    r.x = x;
+    r.x_f32 = x_dtype == QMOE_ACT_F32;
+    r.M = n_tokens;
+    r.D = d.hidden;
+    r.E = 0;  // the gate-vector row alone
+    r.k = d.top_k;
+    r.gate_vec = w->gate_vec;
+    r.logits = ws.logits();
+    r.counter = ws.counter();
+    r.shared_logit = ws.shared();
+    r.status = ws.status();
+    QMOE_TRY(cuda_status(launch_route(r, s)));
+    // Any in-range ids will do: none falls in the empty window.
+    QMOE_TRY(cuda_status(cudaMemsetAsync(ws.ids(), 0, (size_t)n_tokens * d.top_k * 4, s)));
+    ExpertArgs a = expert_args(x, x_dtype, n_tokens, ws.ids(), ws.weights(), ws.shared(), &sw, &d,
+                               ws.h(), ws.L.h_stride, out, ws.status());
+    QMOE_TRY(check_smem(a));
+    QMOE_TRY(cuda_status(launch_gateup(a, s)));
+    return cuda_status(launch_down(a, s));
+}
+
+int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* layers, int n_layers,
+                      const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_act(x, QMOE_ACT_BF16));
+    if (!layers || n_layers < 1 || !out) return QMOE_ERR_INVALID_ARG;
+    QMOE_TRY(route_smem_ok(n_tokens, dims->hidden));
+    for (int l = 0; l < n_layers; ++l) {
+        QMOE_TRY(check_weights_route(&layers[l]));
+        QMOE_TRY(check_weights_experts(&layers[l], dims));
+    }
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    ExpertArgs probe = expert_args(x, QMOE_ACT_BF16, n_tokens, nullptr, nullptr, nullptr, &layers[0],
+                                   dims, ws.h(), ws.L.h_stride, out, nullptr);
+    QMOE_TRY(check_smem(probe));
+    cudaStream_t s = (cudaStream_t)stream;
+    // Layer L+1 reads `out` (layer L's result) in its router and gate|up
+    // launches; its down launch overwrites `out` only after both, in stream
+    // order, so one buffer carries the activation through the stack.
+    for (int l = 0; l < n_layers; ++l) {
+        const void* in = l == 0 ? x : (const void*)out;
+        const int dt = l == 0 ? QMOE_ACT_BF16 : QMOE_ACT_F32;
+        QMOE_TRY(run_block(in, dt, n_tokens, &layers[l], dims, out, ws, s));
+    }
+    return QMOE_OK;
+}
+
+}  // extern "C"

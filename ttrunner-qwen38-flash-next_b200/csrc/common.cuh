@@ -1,0 +1,117 @@
+// Internal declarations shared by the kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/qmoe_b200.h"
+#include "iq4xs.cuh"
+
+namespace qmoe {
+
+constexpr int kMaxTokens = 16;     // decode / verify GEMV path
+constexpr int kMaxTopK = 16;
+constexpr int kMaxExperts = 1024;
+constexpr int kMaxHidden = 4096;
+constexpr int kMaxUnique = kMaxTokens * kMaxTopK + 1;
+
+// Workspace layout (bytes from the workspace base), sized for max_tokens.
+struct WsLayout {
+    size_t status;      // int32 status word + padding
+    size_t counter;     // uint32 arrival counter of the router's last-CTA select
+    size_t logits;      // fp32 [max_tokens][n_experts + 1]
+    size_t ids;         // int32 [max_tokens][top_k]
+    size_t weights;     // fp32 [max_tokens][top_k]
+    size_t shared;      // fp32 [max_tokens]
+    size_t h;           // fp32 [max_tokens][top_k + 1][h_stride]
+    size_t total;
+    int h_stride;
+};
+
+WsLayout ws_layout(const qmoe_dims& d, int max_tokens);
+
+// Launch arguments of the routing kernel.
+struct RouteArgs {
+    const void* x;
+    int x_f32;
+    int M, D, E, k;
+    const float* router;
+    const float* gate_vec;  // may be null
+    float* logits;          // [M][E + 1] workspace
+    unsigned int* counter;
+    int32_t* ids;           // [M][k]
+    float* weights;         // [M][k]
+    float* shared_logit;    // [M] or null
+    int* status;
+};
+
+// Arguments shared by the two expert kernels.
+struct ExpertArgs {
+    const void* x;          // gate|up input
+    int x_f32;
+    int M, D, k;
+    int e_lo, e_hi, E;
+    const int32_t* ids;     // [M][k]
+    const float* weights;   // [M][k]
+    const float* shared_logit;  // [M] or null
+    // gate|up
+    const uint8_t* gate_up;
+    size_t gu_expert_bytes;
+    int I_loc;              // gate rows (= up rows) per routed expert
+    const uint8_t* sh_gate_up;
+    int sh_I_loc;           // 0: no shared expert
+    float* h;               // [M][k+1][h_stride]
+    int h_stride;
+    // down
+    const uint8_t* down;
+    size_t dn_expert_bytes;
+    int dn_nseg, dn_nsub, dn_ib0;
+    const uint8_t* sh_down;
+    int sh_nseg, sh_nsub, sh_ib0;
+    float* out;             // [M][D]
+    int* status;
+};
+
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t s);
+cudaError_t launch_gateup(const ExpertArgs& a, cudaStream_t s);
+cudaError_t launch_down(const ExpertArgs& a, cudaStream_t s);
+cudaError_t launch_dequant(const uint8_t* blocks, int64_t n_blocks, float* out, cudaStream_t s);
+cudaError_t launch_quantize(const float* x, int64_t n_blocks, uint8_t* out, cudaStream_t s);
+cudaError_t launch_synth_iq4xs(uint64_t seed, uint64_t sid, int64_t n_blocks, float std_dev,
+                               uint8_t* out, cudaStream_t s);
+cudaError_t launch_synth_f32(uint64_t seed, uint64_t sid, int64_t n, float std_dev, float* out,
+                             cudaStream_t s);
+
+int device_sm_count();
+
+}  // namespace qmoe
+
+#if defined(__CUDACC__)
+namespace qmoe {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Activation element i of row m as float: bf16 as stored, or fp32 rounded to
+// bf16 (the activation dtype between layers).
+__device__ __forceinline__ float load_act(const void* x, int x_f32, size_t i) {
+    if (x_f32) {
+        const float v = reinterpret_cast<const float*>(x)[i];
+        return __bfloat162float(__float2bfloat16_rn(v));
+    }
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
+}
+
+__device__ __forceinline__ void record_status(int* status, int code) {
+    if (status) atomicCAS(status, 0, code);
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+__device__ __forceinline__ float sigmoid(float z) { return 1.0f / (1.0f + expf(-z)); }
+
+}  // namespace qmoe
+#endif

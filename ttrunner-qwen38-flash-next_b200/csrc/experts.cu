@@ -1,0 +1,436 @@
+// Gathered expert GEMVs on IQ4_XS weights.
+//
+//  gate|up:  h[m][slot][r] = silu(G_e[r] . x_m) * (U_e[r] . x_m) for every
+//            selected expert e of token m (reference/model.py:411-414; the
+//            device pair gather_gemv MODE 2 + fused_swiglu, tt/moe.py:946-953)
+//            and the shared expert in slot k (reference/model.py:392-394).
+//  down:     out[m][j] = sum_s w[m][s] * D_e[j] . h[m][s]
+//                        + sigmoid(x_m . g) * D_sh[j] . h[m][k]
+//            (reference/model.py:395-397, 413-417; gather_gemv MODE 0,
+//            tt/moe.py:958-975, which stacks experts on K to do the combine).
+//
+// Only the selected experts' super-blocks are read; nothing is copied or
+// dequantised to memory.  Each warp owns one weight row (gate|up: a row pair
+// r, I+r; down: an output row j across every selected expert), lanes split
+// the row's 32-value sub-blocks (the k-split), and a shuffle reduction folds
+// the lanes.  Sub-block sums are exact int32 dot products of the 4-bit codes'
+// int8 codebook values with the activation in block floating point (int16
+// mantissas, one power-of-two step per 32 values); the fp32 accumulation
+// then applies d * (ls - 32) and the activation step.
+//
+// Tokens that share an expert share its weight reads: the kernels first
+// build, per CTA, the list of distinct local experts and which tokens (and
+// in which top-k slot) use each one.
+#include "common.cuh"
+
+namespace qmoe {
+namespace {
+
+constexpr int kWarps = 8;
+
+struct Plan {
+    int n;                                   // distinct routed local experts
+    int expert[kMaxUnique];                  // local expert index
+    uint32_t mask[kMaxUnique];               // tokens using it
+    int8_t slot[kMaxUnique][kMaxTokens];     // top-k slot per token
+};
+
+__device__ __forceinline__ uint2 ldg2(const uint8_t* p) {
+    return __ldg(reinterpret_cast<const uint2*>(p));
+}
+
+// Distinct local experts over the M x k routing table, in first-use order.
+__device__ void build_plan(const ExpertArgs& a, Plan& p, int* owner /* smem [E] */) {
+    const int tid = threadIdx.x;
+    const int Mk = a.M * a.k;
+    if (a.M == 1) {
+        if (tid < 32) {
+            const int lane = tid;
+            int id = lane < a.k ? a.ids[lane] : -1;
+            if (lane < a.k && (id < 0 || id >= a.E)) {
+                record_status(a.status, QMOE_ERR_DEVICE_RANGE);
+                id = -1;
+            }
+            const bool local = id >= a.e_lo && id < a.e_hi;
+            const unsigned b = __ballot_sync(0xffffffffu, local);
+            if (local) {
+                const int pos = __popc(b & ((1u << lane) - 1u));
+                p.expert[pos] = id - a.e_lo;
+                p.mask[pos] = 1u;
+                p.slot[pos][0] = (int8_t)lane;
+            }
+            if (lane == 0) p.n = __popc(b);
+        }
+        __syncthreads();
+        return;
+    }
+    const int n_loc = a.e_hi - a.e_lo;
+    for (int i = tid; i < n_loc; i += blockDim.x) owner[i] = 0x7fffffff;
+    __syncthreads();
+    for (int t = tid; t < Mk; t += blockDim.x) {
+        const int id = a.ids[t];
+        if (id < 0 || id >= a.E) {
+            record_status(a.status, QMOE_ERR_DEVICE_RANGE);
+            continue;
+        }
+        if (id >= a.e_lo && id < a.e_hi) atomicMin(&owner[id - a.e_lo], t);
+    }
+    __syncthreads();
+    // Serial compaction in t order by one warp: Mk <= 256.
+    if (tid < 32) {
+        int base = 0;
+        for (int t0 = 0; t0 < Mk; t0 += 32) {
+            const int t = t0 + tid;
+            bool first = false;
+            int id = -1;
+            if (t < Mk) {
+                id = a.ids[t];
+                first = id >= a.e_lo && id < a.e_hi && owner[id - a.e_lo] == t;
+            }
+            const unsigned b = __ballot_sync(0xffffffffu, first);
+            if (first) {
+                const int pos = base + __popc(b & ((1u << tid) - 1u));
+                p.expert[pos] = id - a.e_lo;
+                p.mask[pos] = 0u;
+                owner[id - a.e_lo] = -1 - pos;  // owner now holds -(pos + 1)
+            }
+            base += __popc(b);
+        }
+        if (tid == 0) p.n = base;
+    }
+    __syncthreads();
+    for (int t = tid; t < Mk; t += blockDim.x) {
+        const int id = a.ids[t];
+        if (id >= a.e_lo && id < a.e_hi) {
+            const int pos = -1 - owner[id - a.e_lo];
+            const int m = t / a.k, s = t % a.k;
+            atomicOr(&p.mask[pos], 1u << m);
+            p.slot[pos][m] = (int8_t)s;
+        }
+    }
+    __syncthreads();
+}
+
+// One 32-value activation block -> int16 pair words + power-of-two step.
+__device__ __forceinline__ void to_block_fp(const float* v, int* pairs, float* step) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    if (!(amax > 0.0f) || !(amax <= 3.0e38f)) {
+#pragma unroll
+        for (int p = 0; p < 16; ++p) pairs[p] = 0;
+        *step = (amax > 0.0f) ? __int_as_float(0x7fc00000) : 0.0f;  // NaN/inf propagate
+        return;
+    }
+    const int e = qmoe_block_exponent(amax);
+#pragma unroll
+    for (int p = 0; p < 16; ++p) {
+        const int lo = __float2int_rn(ldexpf(v[p], 14 - e));
+        const int hi = __float2int_rn(ldexpf(v[16 + p], 14 - e));
+        pairs[p] = (lo & 0xFFFF) | (hi << 16);
+    }
+    *step = ldexpf(1.0f, e - 14);
+}
+
+// ---------------------------------------------------------------------------
+// gate|up + SwiGLU.  SBL = 32-value sub-blocks per lane along D (D / 1024).
+template <int MAXM, int SBL>
+__global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ Plan plan;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int D = a.D, M = a.M;
+    const int nsb = D >> 5;
+    int* xq = reinterpret_cast<int*>(smem);                        // [M][nsb][16]
+    float* xs = reinterpret_cast<float*>(xq + (size_t)M * nsb * 16);  // [M][nsb]
+    int* owner = reinterpret_cast<int*>(xs + (size_t)M * nsb);     // [E_loc]
+
+    build_plan(a, plan, owner);
+    for (int b = tid; b < M * nsb; b += blockDim.x) {
+        const int m = b / nsb, sb = b % nsb;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = load_act(a.x, a.x_f32, (size_t)m * D + sb * 32 + i);
+        to_block_fp(v, xq + (size_t)b * 16, xs + b);
+    }
+    __syncthreads();
+
+    // M == 1: the lane's activation blocks stay in registers for every row.
+    int xr[SBL][16];
+    float xsr[SBL];
+    if (MAXM == 1) {
+#pragma unroll
+        for (int i = 0; i < SBL; ++i) {
+            const int b = lane + 32 * i;
+#pragma unroll
+            for (int p = 0; p < 16; ++p) xr[i][p] = b < nsb ? xq[b * 16 + p] : 0;
+            xsr[i] = b < nsb ? xs[b] : 0.0f;
+        }
+    }
+
+    const int row_bytes = (D >> 8) * QMOE_SB_BYTES;
+    const int n_routed = plan.n;
+    const int has_sh = (a.sh_gate_up != nullptr && a.sh_I_loc > 0) ? 1 : 0;
+    const int T = n_routed * a.I_loc + has_sh * a.sh_I_loc;
+    const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
+
+    for (int t = gw; t < T; t += nw) {
+        const uint8_t* base;
+        int r, u, rows;
+        if (t < n_routed * a.I_loc) {
+            u = t / a.I_loc;
+            r = t - u * a.I_loc;
+            base = a.gate_up + (size_t)plan.expert[u] * a.gu_expert_bytes;
+            rows = a.I_loc;
+        } else {
+            u = n_routed;
+            r = t - n_routed * a.I_loc;
+            base = a.sh_gate_up;
+            rows = a.sh_I_loc;
+        }
+        const uint8_t* grow = base + (size_t)r * row_bytes;
+        const uint8_t* urow = base + (size_t)(rows + r) * row_bytes;
+
+        // Issue every load of this row pair before any decode.
+        uint2 hg[SBL], hu[SBL], qg[SBL][2], qu[SBL][2];
+#pragma unroll
+        for (int i = 0; i < SBL; ++i) {
+            const int b = lane + 32 * i;
+            if (b < nsb) {
+                const int off = (b >> 3) * QMOE_SB_BYTES, q = off + 8 + 16 * (b & 7);
+                hg[i] = ldg2(grow + off);
+                hu[i] = ldg2(urow + off);
+                qg[i][0] = ldg2(grow + q);
+                qg[i][1] = ldg2(grow + q + 8);
+                qu[i][0] = ldg2(urow + q);
+                qu[i][1] = ldg2(urow + q + 8);
+            }
+        }
+
+        const uint32_t tmask = (u < n_routed) ? plan.mask[u] : ((M >= 32) ? 0xffffffffu : ((1u << M) - 1u));
+        float accg[MAXM], accu[MAXM];
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) accg[m] = accu[m] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < SBL; ++i) {
+            const int b = lane + 32 * i;
+            if (b >= nsb) continue;
+            const int ib = b & 7;
+            const float dg = qmoe_half_bits_to_float((uint16_t)(hg[i].x & 0xFFFFu)) *
+                             (float)(qmoe_iq4xs_ls(hg[i].x, hg[i].y, ib) - 32);
+            const float du = qmoe_half_bits_to_float((uint16_t)(hu[i].x & 0xFFFFu)) *
+                             (float)(qmoe_iq4xs_ls(hu[i].x, hu[i].y, ib) - 32);
+            if (MAXM == 1) {
+                const int sg = qmoe_subblock_dot(qg[i][0].x, qg[i][0].y, qg[i][1].x, qg[i][1].y, xr[i], 0);
+                const int su = qmoe_subblock_dot(qu[i][0].x, qu[i][0].y, qu[i][1].x, qu[i][1].y, xr[i], 0);
+                accg[0] = fmaf(dg * xsr[i], (float)sg, accg[0]);
+                accu[0] = fmaf(du * xsr[i], (float)su, accu[0]);
+            } else {
+#pragma unroll
+                for (int m = 0; m < MAXM; ++m) {
+                    if (m < M && ((tmask >> m) & 1u)) {
+                        int xp[16];
+                        const int4* src = reinterpret_cast<const int4*>(xq + ((size_t)m * nsb + b) * 16);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            const int4 w4 = src[v];
+                            xp[4 * v] = w4.x;
+                            xp[4 * v + 1] = w4.y;
+                            xp[4 * v + 2] = w4.z;
+                            xp[4 * v + 3] = w4.w;
+                        }
+                        const float st = xs[m * nsb + b];
+                        const int sg = qmoe_subblock_dot(qg[i][0].x, qg[i][0].y, qg[i][1].x, qg[i][1].y, xp, 0);
+                        const int su = qmoe_subblock_dot(qu[i][0].x, qu[i][0].y, qu[i][1].x, qu[i][1].y, xp, 0);
+                        accg[m] = fmaf(dg * st, (float)sg, accg[m]);
+                        accu[m] = fmaf(du * st, (float)su, accu[m]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+            if (m < M && ((tmask >> m) & 1u)) {
+                const float g = warp_sum(accg[m]);
+                const float uu = warp_sum(accu[m]);
+                if (lane == 0) {
+                    const int slot = (u < n_routed) ? plan.slot[u][m] : a.k;
+                    a.h[((size_t)m * (a.k + 1) + slot) * a.h_stride + r] = silu(g) * uu;
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// down + weighted combine + gated shared expert.
+template <int MAXM>
+__global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ Plan plan;
+    __shared__ float s_w[kMaxTokens][kMaxTopK + 1];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int M = a.M, K1 = a.k + 1;
+    const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
+    const int nsbh = I_max >> 5;                                     // h blocks per slot
+    int* hq = reinterpret_cast<int*>(smem);                          // [M][k+1][nsbh][16]
+    float* hs = reinterpret_cast<float*>(hq + (size_t)M * K1 * nsbh * 16);  // [M][k+1][nsbh]
+    int* owner = reinterpret_cast<int*>(hs + (size_t)M * K1 * nsbh);
+
+    build_plan(a, plan, owner);
+    const int has_sh = (a.sh_down != nullptr && a.sh_I_loc > 0) ? 1 : 0;
+    for (int i = tid; i < M * K1; i += blockDim.x) {
+        const int m = i / K1, s = i % K1;
+        float w;
+        if (s < a.k) w = a.weights[m * a.k + s];
+        else w = (has_sh && a.shared_logit) ? sigmoid(a.shared_logit[m]) : (has_sh ? 1.0f : 0.0f);
+        s_w[m][s] = w;
+    }
+    // Convert the used h slots to block floating point.
+    for (int i = tid; i < M * K1 * nsbh; i += blockDim.x) {
+        const int b = i % nsbh, ms = i / nsbh, s = ms % K1, m = ms / K1;
+        bool used;
+        int n_valid;
+        if (s < a.k) {
+            const int id = a.ids[m * a.k + s];
+            used = id >= a.e_lo && id < a.e_hi;
+            n_valid = a.I_loc >> 5;
+        } else {
+            used = has_sh != 0;
+            n_valid = a.sh_I_loc >> 5;
+        }
+        if (!used || b >= n_valid) continue;
+        float v[32];
+        const float* src = a.h + ((size_t)m * K1 + s) * a.h_stride + b * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = src[j];
+        to_block_fp(v, hq + (size_t)i * 16, hs + i);
+    }
+    __syncthreads();
+
+    const int nsb_r = a.dn_nseg * a.dn_nsub;
+    const int nsb_s = a.sh_nseg * a.sh_nsub;
+    const int rb_r = a.dn_nseg * (8 + 16 * a.dn_nsub);
+    const int rb_s = a.sh_nseg * (8 + 16 * a.sh_nsub);
+    const int n_routed = plan.n;
+    const int P = n_routed * nsb_r + has_sh * nsb_s;
+    const uint32_t all = (M >= 32) ? 0xffffffffu : ((1u << M) - 1u);
+    const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
+
+    for (int j = gw; j < a.D; j += nw) {
+        float acc[MAXM];
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
+        for (int p = lane; p < P; p += 32) {
+            int u, t, nsub, ib0;
+            const uint8_t* row;
+            if (p < n_routed * nsb_r) {
+                u = p / nsb_r;
+                t = p - u * nsb_r;
+                row = a.down + (size_t)plan.expert[u] * a.dn_expert_bytes + (size_t)j * rb_r;
+                nsub = a.dn_nsub;
+                ib0 = a.dn_ib0;
+            } else {
+                u = n_routed;
+                t = p - n_routed * nsb_r;
+                row = a.sh_down + (size_t)j * rb_s;
+                nsub = a.sh_nsub;
+                ib0 = a.sh_ib0;
+            }
+            const int seg = t / nsub, ibl = t - seg * nsub;
+            const uint8_t* sp = row + seg * (8 + 16 * nsub);
+            const uint2 hdr = ldg2(sp);
+            const uint2 q0 = ldg2(sp + 8 + 16 * ibl);
+            const uint2 q1 = ldg2(sp + 16 + 16 * ibl);
+            const float dl = qmoe_half_bits_to_float((uint16_t)(hdr.x & 0xFFFFu)) *
+                             (float)(qmoe_iq4xs_ls(hdr.x, hdr.y, ib0 + ibl) - 32);
+            const uint32_t tmask = (u < n_routed) ? plan.mask[u] : all;
+#pragma unroll
+            for (int m = 0; m < MAXM; ++m) {
+                if (m < M && ((tmask >> m) & 1u)) {
+                    const int s = (u < n_routed) ? plan.slot[u][m] : a.k;
+                    const size_t hb = ((size_t)m * K1 + s) * nsbh + t;
+                    int xp[16];
+                    const int4* src = reinterpret_cast<const int4*>(hq + hb * 16);
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        const int4 w4 = src[v];
+                        xp[4 * v] = w4.x;
+                        xp[4 * v + 1] = w4.y;
+                        xp[4 * v + 2] = w4.z;
+                        xp[4 * v + 3] = w4.w;
+                    }
+                    const int S = qmoe_subblock_dot(q0.x, q0.y, q1.x, q1.y, xp, 0);
+                    acc[m] = fmaf(s_w[m][s] * dl * hs[hb], (float)S, acc[m]);
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+            if (m < M) {
+                const float v = warp_sum(acc[m]);
+                if (lane == 0) a.out[(size_t)m * a.D + j] = v;
+            }
+        }
+    }
+}
+
+template <typename K>
+cudaError_t launch_with_smem(K kernel, unsigned grid, size_t smem, const ExpertArgs& a,
+                             cudaStream_t s) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    kernel<<<grid, kWarps * 32, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+template <int MAXM>
+cudaError_t launch_gateup_m(const ExpertArgs& a, cudaStream_t s) {
+    const int nsb = a.D >> 5;
+    const size_t smem = (size_t)a.M * nsb * (16 * 4 + 4) + (size_t)(a.e_hi - a.e_lo) * 4;
+    const int n_units = a.M * a.k + 1;
+    const long tasks = (long)n_units * (a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc);
+    const unsigned grid = (unsigned)((tasks + kWarps - 1) / kWarps);
+    const int sbl = (nsb + 31) / 32;
+    switch (sbl) {
+        case 1: return launch_with_smem(gateup_kernel<MAXM, 1>, grid, smem, a, s);
+        case 2: return launch_with_smem(gateup_kernel<MAXM, 2>, grid, smem, a, s);
+        case 3: return launch_with_smem(gateup_kernel<MAXM, 3>, grid, smem, a, s);
+        default: return launch_with_smem(gateup_kernel<MAXM, 4>, grid, smem, a, s);
+    }
+}
+
+template <int MAXM>
+cudaError_t launch_down_m(const ExpertArgs& a, cudaStream_t s) {
+    const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
+    const size_t smem = (size_t)a.M * (a.k + 1) * (I_max >> 5) * (16 * 4 + 4) +
+                        (size_t)(a.e_hi - a.e_lo) * 4;
+    const unsigned grid = (unsigned)((a.D + kWarps - 1) / kWarps);
+    return launch_with_smem(down_kernel<MAXM>, grid, smem, a, s);
+}
+
+}  // namespace
+
+size_t gateup_smem_bytes(const ExpertArgs& a) {
+    return (size_t)a.M * (a.D >> 5) * (16 * 4 + 4) + (size_t)(a.e_hi - a.e_lo) * 4;
+}
+size_t down_smem_bytes(const ExpertArgs& a) {
+    const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
+    return (size_t)a.M * (a.k + 1) * (I_max >> 5) * (16 * 4 + 4) + (size_t)(a.e_hi - a.e_lo) * 4;
+}
+
+cudaError_t launch_gateup(const ExpertArgs& a, cudaStream_t s) {
+    if (a.M <= 1) return launch_gateup_m<1>(a, s);
+    if (a.M <= 4) return launch_gateup_m<4>(a, s);
+    if (a.M <= 8) return launch_gateup_m<8>(a, s);
+    return launch_gateup_m<16>(a, s);
+}
+
+cudaError_t launch_down(const ExpertArgs& a, cudaStream_t s) {
+    if (a.M <= 1) return launch_down_m<1>(a, s);
+    if (a.M <= 4) return launch_down_m<4>(a, s);
+    if (a.M <= 8) return launch_down_m<8>(a, s);
+    return launch_down_m<16>(a, s);
+}
+
+}  // namespace qmoe

@@ -1,0 +1,293 @@
+"""The MoE block on the device, behind the reference's operator interface.
+
+`MoELayer` is the drop-in for `TTModel._moe_block(mixed, layer)`
+(tt/model.py:2010-2052): routed experts plus the sigmoid-gated shared
+expert, x [M, hidden] -> [M, hidden] fp32 (a partial sum when sharded; the
+caller all-reduces).  Its stages are exposed as the reference's operators:
+
+  route(x, router_w, top_k)                 tt/moe.py:308   -> (weights, keep) [M, E]
+  apply_experts(x, weights, keep, ...)      tt/moe.py:330   -> routed output
+  moe_block(x, router_w, gate_w, up_w, ...) tt/moe.py:159   -> routed output
+  shared_expert(x, gate_w, up_w, down_w, g) tt/moe.py:983   -> shared output
+
+Differences from the reference, by design: routing is exact top-k with ties
+to the lower expert id (the reference's device kernel in EXACT_TOPK mode,
+scripts/kernels/router_select.cpp:198-222; its ttnn threshold chain admits
+ties), and errors raise `QMoEError` instead of warning and falling back
+(tt/moe.py:264-271) -- there is no fallback path.
+
+IQ4_XS operands are uint8 tensors of GGUF bytes: gate_w [E, I, D/256*136]
+(or the fused gate|up [E, 2I, D/256*136] with up_w None, as
+`TTWeights.fused_gate_up`, tt/weights.py:66-99), down_w [E, D, I/256*136].
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import Dims, LayerWeights, QMoEError, check, lib
+from .config import MoEConfig, Shard
+from .weights import DeviceLayer
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dims_key(d: Dims) -> tuple:
+    return tuple(getattr(d, f) for f, _ in Dims._fields_)
+
+
+class Workspace:
+    """Device scratch for one shape family: router logits, routing table, h."""
+
+    def __init__(self, dims: Dims, max_tokens: int, device: torch.device):
+        self.dims = dims
+        self.max_tokens = max_tokens
+        nbytes = lib.qmoe_workspace_bytes(ctypes.byref(dims), max_tokens)
+        if nbytes == 0:
+            raise QMoEError(_lib.QMOE_ERR_UNSUPPORTED, "qmoe_workspace_bytes")
+        self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        check(lib.qmoe_workspace_init(self.buf.data_ptr(), nbytes, _stream()), "qmoe_workspace_init")
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    @property
+    def nbytes(self) -> int:
+        return self.buf.numel()
+
+    def read_status(self) -> int:
+        st = ctypes.c_int(0)
+        check(lib.qmoe_read_status(self.ptr, ctypes.byref(st), _stream()), "qmoe_read_status")
+        return st.value
+
+    def raise_if_error(self, where: str = "device") -> None:
+        st = self.read_status()
+        if st != _lib.QMOE_OK:
+            raise QMoEError(st, where)
+
+
+_WS: dict[tuple, Workspace] = {}
+
+
+def workspace_for(dims: Dims, max_tokens: int, device: torch.device) -> Workspace:
+    key = (_dims_key(dims), max_tokens, str(device))
+    ws = _WS.get(key)
+    if ws is None:
+        ws = _WS[key] = Workspace(dims, max_tokens, device)
+    return ws
+
+
+def _act(x: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """[.., M, D] bf16/fp32 -> contiguous [M, D] and its act dtype code."""
+    if not x.is_cuda:
+        raise ValueError("x must be a CUDA tensor")
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    if x2.dtype == torch.bfloat16:
+        return x2, _lib.QMOE_ACT_BF16
+    if x2.dtype == torch.float32:
+        return x2, _lib.QMOE_ACT_F32
+    raise TypeError(f"activations must be bf16 or fp32, got {x.dtype}")
+
+
+class MoELayer:
+    """One MoE block resident in HBM (one shard of it)."""
+
+    def __init__(self, layer: DeviceLayer, max_tokens: int | None = None):
+        self.layer = layer
+        self.cfg: MoEConfig = layer.cfg
+        self.shard: Shard = layer.shard
+        self.dims = layer.shard.dims(layer.cfg)
+        self.max_tokens = max_tokens or lib.qmoe_max_tokens()
+        self.weights = layer.c_struct()
+        self.ws = workspace_for(self.dims, self.max_tokens, layer.router.device)
+
+    def _m(self, x: torch.Tensor) -> int:
+        m = x.shape[0]
+        if not 1 <= m <= self.max_tokens:
+            raise ValueError(f"{m} tokens outside [1, {self.max_tokens}]")
+        return m
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        x2, dt = _act(x)
+        m = self._m(x2)
+        if out is None:
+            out = torch.empty(m, self.cfg.hidden, dtype=torch.float32, device=x2.device)
+        check(lib.qmoe_moe_block(x2.data_ptr(), dt, m, ctypes.byref(self.weights), ctypes.byref(self.dims),
+                                 out.data_ptr(), self.ws.ptr, self.ws.nbytes, _stream()), "qmoe_moe_block")
+        return out
+
+    def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(ids [M, k] int32, weights [M, k] fp32, shared_logit [M] fp32)."""
+        x2, dt = _act(x)
+        m = self._m(x2)
+        k = self.cfg.top_k
+        ids = torch.empty(m, k, dtype=torch.int32, device=x2.device)
+        w = torch.empty(m, k, dtype=torch.float32, device=x2.device)
+        sl = torch.empty(m, dtype=torch.float32, device=x2.device)
+        check(lib.qmoe_route(x2.data_ptr(), dt, m, ctypes.byref(self.weights), ctypes.byref(self.dims),
+                             ids.data_ptr(), w.data_ptr(), sl.data_ptr(), self.ws.ptr, self.ws.nbytes,
+                             _stream()), "qmoe_route")
+        return ids, w, sl
+
+    def gate_up(self, x: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+        """h [M, k+1, I_loc] fp32; slot k is the shared expert."""
+        x2, dt = _act(x)
+        m = self._m(x2)
+        hs = max(self.dims.inter_local, self.dims.sh_inter_local)
+        h = torch.zeros(m, self.cfg.top_k + 1, hs, dtype=torch.float32, device=x2.device)
+        ids = ids.to(torch.int32).contiguous()
+        check(lib.qmoe_gateup_swiglu(x2.data_ptr(), dt, m, ids.data_ptr(), ctypes.byref(self.weights),
+                                     ctypes.byref(self.dims), h.data_ptr(), hs, self.ws.ptr,
+                                     self.ws.nbytes, _stream()), "qmoe_gateup_swiglu")
+        return h
+
+    def down(self, h: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+             shared_logit: torch.Tensor | None) -> torch.Tensor:
+        m = h.shape[0]
+        out = torch.empty(m, self.cfg.hidden, dtype=torch.float32, device=h.device)
+        ids = ids.to(torch.int32).contiguous()
+        weights = weights.to(torch.float32).contiguous()
+        check(lib.qmoe_down_combine(h.data_ptr(), h.shape[-1], m, ids.data_ptr(), weights.data_ptr(),
+                                    None if shared_logit is None else shared_logit.data_ptr(),
+                                    ctypes.byref(self.weights), ctypes.byref(self.dims), out.data_ptr(),
+                                    self.ws.ptr, self.ws.nbytes, _stream()), "qmoe_down_combine")
+        return out
+
+
+# ---------------------------------------------------------------------------
+# the reference's operator interface on raw tensors
+
+_FUSED: dict[tuple, torch.Tensor] = {}
+
+
+def _fused_gate_up(gate_w: torch.Tensor, up_w: torch.Tensor | None) -> torch.Tensor:
+    if up_w is None:
+        return gate_w.contiguous()
+    key = (gate_w.data_ptr(), up_w.data_ptr(), tuple(gate_w.shape))
+    t = _FUSED.get(key)
+    if t is None:
+        t = _FUSED[key] = torch.cat([gate_w, up_w], dim=-2).contiguous()
+    return t
+
+
+def _raw_dims(hidden: int, inter: int, n_experts: int, top_k: int, shared_inter: int = 0) -> Dims:
+    nseg, nsub, ib0 = Shard.row_slice(0, inter)
+    d = Dims(hidden=hidden, inter=inter, n_experts=n_experts, top_k=top_k, expert_lo=0,
+             expert_hi=n_experts, inter_local=inter, down_nseg=nseg, down_nsub=nsub, down_ib0=ib0)
+    if shared_inter:
+        s = Shard.row_slice(0, shared_inter)
+        d.sh_inter_local = shared_inter
+        d.sh_down_nseg, d.sh_down_nsub, d.sh_down_ib0 = s
+    return d
+
+
+def _check_u8(t: torch.Tensor, name: str) -> None:
+    if t.dtype != torch.uint8 or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA uint8 tensor of IQ4_XS bytes")
+
+
+def moe_block(x: torch.Tensor, router_w: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor | None,
+              down_w: torch.Tensor, top_k: int, num_experts: int, hidden_size: int,
+              intermediate_size: int) -> torch.Tensor:
+    """Routed experts only, x [.., M, K] -> [M, K] fp32 (tt/moe.py:159-295)."""
+    _check_u8(gate_w, "gate_w")
+    _check_u8(down_w, "down_w")
+    x2, dt = _act(x)
+    m = x2.shape[0]
+    gu = _fused_gate_up(gate_w, up_w)
+    dims = _raw_dims(hidden_size, intermediate_size, num_experts, top_k)
+    # Keep every operand referenced until the launches are enqueued.
+    r_w, d_w = router_w.float().contiguous(), down_w.contiguous()
+    w = LayerWeights(router=r_w.data_ptr(), gate_vec=None, gate_up=gu.data_ptr(),
+                     down=d_w.data_ptr(), sh_gate_up=None, sh_down=None)
+    ws = workspace_for(dims, max(m, 1), x2.device)
+    out = torch.empty(m, hidden_size, dtype=torch.float32, device=x2.device)
+    check(lib.qmoe_moe_block(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), out.data_ptr(),
+                             ws.ptr, ws.nbytes, _stream()), "moe_block")
+    return out
+
+
+def shared_expert(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, down_w: torch.Tensor,
+                  gate_vec: torch.Tensor) -> torch.Tensor:
+    """sigmoid(x . gate_vec) * down(silu(gate x) * up x) (tt/moe.py:983-1044)."""
+    _check_u8(gate_w, "gate_w")
+    _check_u8(up_w, "up_w")
+    _check_u8(down_w, "down_w")
+    x2, dt = _act(x)
+    m = x2.shape[0]
+    inter = gate_w.shape[-2]
+    hidden = down_w.shape[-2]
+    gu = _fused_gate_up(gate_w, up_w)
+    dims = _raw_dims(hidden, inter, 32, 1, shared_inter=inter)
+    g_v, d_w = gate_vec.float().contiguous(), down_w.contiguous()
+    w = LayerWeights(router=None, gate_vec=g_v.data_ptr(), gate_up=None,
+                     down=None, sh_gate_up=gu.data_ptr(), sh_down=d_w.data_ptr())
+    ws = workspace_for(dims, max(m, 1), x2.device)
+    out = torch.empty(m, hidden, dtype=torch.float32, device=x2.device)
+    check(lib.qmoe_shared_expert(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), out.data_ptr(),
+                                 ws.ptr, ws.nbytes, _stream()), "shared_expert")
+    return out
+
+
+def route_topk(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(ids [M, k] int32, weights [M, k] fp32), descending, ties to the lower id."""
+    x2, dt = _act(x)
+    m = x2.shape[0]
+    E, D = router_w.shape
+    dims = _raw_dims(D, 256, E, top_k)
+    r_w = router_w.float().contiguous()
+    w = LayerWeights(router=r_w.data_ptr())
+    ws = workspace_for(dims, max(m, 1), x2.device)
+    ids = torch.empty(m, top_k, dtype=torch.int32, device=x2.device)
+    wt = torch.empty(m, top_k, dtype=torch.float32, device=x2.device)
+    check(lib.qmoe_route(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), ids.data_ptr(),
+                         wt.data_ptr(), None, ws.ptr, ws.nbytes, _stream()), "route")
+    return ids, wt
+
+
+def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dense routing as tt/moe.py:308-327 returns it: (weights, keep), both [M, E]."""
+    ids, wt = route_topk(x, router_w, top_k)
+    E = router_w.shape[0]
+    dense = torch.zeros(ids.shape[0], E, dtype=torch.float32, device=ids.device)
+    dense.scatter_(1, ids.long(), wt)
+    keep = torch.zeros_like(dense).scatter_(1, ids.long(), 1.0)
+    return dense, keep
+
+
+def apply_experts(x: torch.Tensor, weights: torch.Tensor, keep: torch.Tensor, gate_w: torch.Tensor,
+                  up_w: torch.Tensor | None, down_w: torch.Tensor, num_experts: int, hidden_size: int,
+                  intermediate_size: int) -> torch.Tensor:
+    """Routed output for dense routing (tt/moe.py:330-368): the experts kept per row."""
+    _check_u8(gate_w, "gate_w")
+    _check_u8(down_w, "down_w")
+    x2, dt = _act(x)
+    m = x2.shape[0]
+    k = int(keep.sum(dim=-1).max().item())
+    if k < 1:
+        return torch.zeros(m, hidden_size, dtype=torch.float32, device=x2.device)
+    kv, ids = torch.topk(keep.float() * 2.0 + weights.float(), k, dim=-1)
+    wt = torch.gather(weights.float(), 1, ids)
+    wt = torch.where(torch.gather(keep.float(), 1, ids) > 0, wt, torch.zeros_like(wt))
+    gu = _fused_gate_up(gate_w, up_w)
+    dims = _raw_dims(hidden_size, intermediate_size, num_experts, k)
+    d_w = down_w.contiguous()
+    lw = LayerWeights(gate_up=gu.data_ptr(), down=d_w.data_ptr())
+    ws = workspace_for(dims, max(m, 1), x2.device)
+    hs = intermediate_size
+    h = torch.empty(m, k + 1, hs, dtype=torch.float32, device=x2.device)
+    ids32 = ids.to(torch.int32).contiguous()
+    check(lib.qmoe_gateup_swiglu(x2.data_ptr(), dt, m, ids32.data_ptr(), ctypes.byref(lw), ctypes.byref(dims),
+                                 h.data_ptr(), hs, ws.ptr, ws.nbytes, _stream()), "apply_experts gate|up")
+    out = torch.empty(m, hidden_size, dtype=torch.float32, device=x2.device)
+    wt = wt.contiguous()
+    check(lib.qmoe_down_combine(h.data_ptr(), hs, m, ids32.data_ptr(), wt.data_ptr(), None, ctypes.byref(lw),
+                                ctypes.byref(dims), out.data_ptr(), ws.ptr, ws.nbytes, _stream()),
+          "apply_experts down")
+    return out
