@@ -20,6 +20,23 @@ MOE_CASES = ["small_m1", "small_m4", "tie_m2", "c1_m1", "c1_m4", "c1_m8"]
 _DEV_LAYERS: dict = {}
 
 
+def well_conditioned(probs, k: int, rel_gap: float = 1e-5) -> bool:
+    """True when, for every token, the k-th and (k+1)-th probabilities differ
+    by more than rel_gap relative: selection does not hinge on last-ulp
+    rounding of exp or of the logit summation order, which no two
+    implementations share (a literal chain without normalisation shrinks the
+    activations until the router ties; see the oracle's tie rule)."""
+    p = -np.sort(-probs, axis=-1)
+    return bool(np.all((p[:, k - 1] - p[:, k]) > rel_gap * p[:, k - 1]))
+
+
+def rms_bf16(out: torch.Tensor) -> torch.Tensor:
+    """Unweighted RMS normalisation of a layer output to the next layer's bf16
+    input (the model's hyper-connection mixer normalises there,
+    reference/model.py:53-81); keeps routing realistic through 48 layers."""
+    return (out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+
+
 def device_layer(pkg, g):
     hl = host_layer_for(pkg, g, all_experts=True)
     key = (id(hl), int(g["seed"]))
@@ -184,14 +201,21 @@ def test_stack_matches_layer_chain_and_oracle(pkg, oracle):
     out_eager = eager.decode(x).clone()
     # layer by layer through MoELayer: identical kernels, identical bits
     act = x
+    checked = 0
     for l, dl in enumerate(dls):
         inp = act.to(torch.bfloat16) if act.dtype == torch.float32 else act
-        y = pkg.MoELayer(dl)(inp)
+        ml = pkg.MoELayer(dl)
+        y = ml(inp)
+        ids, _, _ = ml.route(inp)
         # teacher-forced: the oracle gets this layer's bf16 input
         ref = oracle.moe_forward(inp.float().cpu().numpy(), oracle.ExpertSource.from_host_layer(hls[l]), cfg.top_k)
-        assert oracle.max_rel_err(y.cpu().numpy(), ref["out"]) <= TOL, f"layer {l}"
+        if well_conditioned(ref["probs"], cfg.top_k):
+            assert np.array_equal(ids.cpu().numpy(), ref["ids"]), f"layer {l}"
+            assert oracle.max_rel_err(y.cpu().numpy(), ref["out"]) <= TOL, f"layer {l}"
+            checked += 1
         act = y
     torch.cuda.synchronize()
+    assert checked >= 2
     assert torch.equal(out_graph, out_eager)
     assert torch.equal(out_graph, act)
 
@@ -236,13 +260,32 @@ def test_device_family_full_stack_c2(pkg, oracle):
     stack.ws.raise_if_error("c2 stack")
     assert torch.isfinite(out).all()
     act = x
-    for l in range(3):
+    for l in range(2):  # the literal chain stays well conditioned this deep
         y = pkg.MoELayer(dls[l])(act)
         hv = pkg.weights.device_layer_host_view(dls[l])
         ref = oracle.moe_forward(act.float().cpu().numpy(), oracle.ExpertSource.from_host_layer(hv), cfg.top_k)
         ids, _, _ = pkg.MoELayer(dls[l]).route(act)
+        assert well_conditioned(ref["probs"], cfg.top_k)
         assert np.array_equal(ids.cpu().numpy(), ref["ids"])
         assert oracle.max_rel_err(y.cpu().numpy(), ref["out"]) <= TOL
         act = y.to(torch.bfloat16)
+    # RMS-normalised chain through all 48 layers, every layer vs the oracle.
+    act = x
+    checked, worst = 0, 0.0
+    for l in range(cfg.n_layers):
+        ml = pkg.MoELayer(dls[l])
+        y = ml(act)
+        ids, _, _ = ml.route(act)
+        hv = pkg.weights.device_layer_host_view(dls[l])
+        ref = oracle.moe_forward(act.float().cpu().numpy(), oracle.ExpertSource.from_host_layer(hv), cfg.top_k)
+        if well_conditioned(ref["probs"], cfg.top_k):
+            assert np.array_equal(ids.cpu().numpy(), ref["ids"]), f"layer {l}"
+            err = oracle.max_rel_err(y.cpu().numpy(), ref["out"])
+            assert err <= TOL, f"layer {l}: {err}"
+            worst = max(worst, err)
+            checked += 1
+        act = rms_bf16(y)
+    print(f"normalised 48-layer chain: {checked} layers checked, worst max rel err {worst:.2e}")
+    assert checked >= cfg.n_layers - 2
     del stack, dls
     torch.cuda.empty_cache()

@@ -110,6 +110,34 @@ __device__ __forceinline__ void record_status(int* status, int code) {
     if (status) atomicCAS(status, 0, code);
 }
 
+// Block floating point of one 32-value activation block, one value per lane
+// (lane j holds value j).  The step is 2^(e-14) with |x| < 2^e for the
+// block's largest |x|, so every mantissa fits int16 with a bit to spare;
+// values within 2^-6 of the block maximum convert exactly from bf16.
+// Returns, in lanes 0..15, the pair word q_j | q_(16+j) << 16 -- the order in
+// which an IQ4_XS qs byte holds its two codes; *step gets the step in every
+// lane.  Zero or subnormal blocks give zeros; a non-finite value gives a NaN
+// step so the result is NaN, as in fp32 arithmetic.
+__device__ __forceinline__ int warp_block_fp(float v, float* step) {
+    const unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
+    const int E = (int)(mb >> 23);  // biased exponent of the block maximum
+    int q = 0;
+    float st = 0.0f;
+    if (E >= 255) {
+        st = __uint_as_float(0x7fc00000u);
+    } else if (E >= 1) {
+        const int k = 140 - E;  // q = rint(v * 2^k), k in [-114, 139]
+        const int k1 = k >> 1, k2 = k - k1;
+        const float s1 = __uint_as_float((unsigned)(127 + k1) << 23);
+        const float s2 = __uint_as_float((unsigned)(127 + k2) << 23);
+        q = __float2int_rn((v * s1) * s2);
+        st = E >= 14 ? __uint_as_float((unsigned)(E - 13) << 23) : __uint_as_float(1u << (E + 9));
+    }
+    const int hi = __shfl_down_sync(0xffffffffu, q, 16);
+    *step = st;
+    return (q & 0xFFFF) | (hi << 16);
+}
+
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 __device__ __forceinline__ float sigmoid(float z) { return 1.0f / (1.0f + expf(-z)); }
 

@@ -111,25 +111,30 @@ __device__ void build_plan(const ExpertArgs& a, Plan& p, int* owner /* smem [E] 
     __syncthreads();
 }
 
-// One 32-value activation block -> int16 pair words + power-of-two step.
-__device__ __forceinline__ void to_block_fp(const float* v, int* pairs, float* step) {
-    float amax = 0.0f;
+// Convert n 32-value blocks to block floating point, one warp per block, with
+// NB blocks' loads issued per warp before any conversion (one memory round
+// trip per NB * kWarps blocks instead of one per block).
+// load(b, lane) -> float: value `lane` of block b; store(b, lane, pair, step).
+template <int NB, typename LoadF, typename StoreF>
+__device__ __forceinline__ void convert_blocks(int n, LoadF load, StoreF store) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int b0 = warp; b0 < n; b0 += NB * kWarps) {
+        float v[NB];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    if (!(amax > 0.0f) || !(amax <= 3.0e38f)) {
+        for (int i = 0; i < NB; ++i) {
+            const int b = b0 + i * kWarps;
+            v[i] = b < n ? load(b, lane) : 0.0f;
+        }
 #pragma unroll
-        for (int p = 0; p < 16; ++p) pairs[p] = 0;
-        *step = (amax > 0.0f) ? __int_as_float(0x7fc00000) : 0.0f;  // NaN/inf propagate
-        return;
+        for (int i = 0; i < NB; ++i) {
+            const int b = b0 + i * kWarps;
+            if (b < n) {
+                float st;
+                const int pw = warp_block_fp(v[i], &st);
+                store(b, lane, pw, st);
+            }
+        }
     }
-    const int e = qmoe_block_exponent(amax);
-#pragma unroll
-    for (int p = 0; p < 16; ++p) {
-        const int lo = __float2int_rn(ldexpf(v[p], 14 - e));
-        const int hi = __float2int_rn(ldexpf(v[16 + p], 14 - e));
-        pairs[p] = (lo & 0xFFFF) | (hi << 16);
-    }
-    *step = ldexpf(1.0f, e - 14);
 }
 
 // ---------------------------------------------------------------------------
@@ -146,13 +151,12 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
     int* owner = reinterpret_cast<int*>(xs + (size_t)M * nsb);     // [E_loc]
 
     build_plan(a, plan, owner);
-    for (int b = tid; b < M * nsb; b += blockDim.x) {
-        const int m = b / nsb, sb = b % nsb;
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = load_act(a.x, a.x_f32, (size_t)m * D + sb * 32 + i);
-        to_block_fp(v, xq + (size_t)b * 16, xs + b);
-    }
+    convert_blocks<8>(
+        M * nsb, [&](int b, int ln) { return load_act(a.x, a.x_f32, (size_t)b * 32 + ln); },
+        [&](int b, int ln, int pw, float st) {
+            if (ln < 16) xq[(size_t)b * 16 + ln] = pw;
+            if (ln == 0) xs[b] = st;
+        });
     __syncthreads();
 
     // M == 1: the lane's activation blocks stay in registers for every row.
@@ -269,6 +273,7 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ Plan plan;
     __shared__ float s_w[kMaxTokens][kMaxTopK + 1];
+    __shared__ int s_nvalid[kMaxTokens][kMaxTopK + 1];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int M = a.M, K1 = a.k + 1;
     const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
@@ -286,26 +291,30 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
         else w = (has_sh && a.shared_logit) ? sigmoid(a.shared_logit[m]) : (has_sh ? 1.0f : 0.0f);
         s_w[m][s] = w;
     }
-    // Convert the used h slots to block floating point.
-    for (int i = tid; i < M * K1 * nsbh; i += blockDim.x) {
-        const int b = i % nsbh, ms = i / nsbh, s = ms % K1, m = ms / K1;
-        bool used;
-        int n_valid;
+    // Which (token, slot) h rows are in use, then convert them to block
+    // floating point.
+    for (int i = tid; i < M * K1; i += blockDim.x) {
+        const int m = i / K1, s = i % K1;
+        int nv = 0;
         if (s < a.k) {
             const int id = a.ids[m * a.k + s];
-            used = id >= a.e_lo && id < a.e_hi;
-            n_valid = a.I_loc >> 5;
+            nv = (id >= a.e_lo && id < a.e_hi) ? (a.I_loc >> 5) : 0;
         } else {
-            used = has_sh != 0;
-            n_valid = a.sh_I_loc >> 5;
+            nv = has_sh ? (a.sh_I_loc >> 5) : 0;
         }
-        if (!used || b >= n_valid) continue;
-        float v[32];
-        const float* src = a.h + ((size_t)m * K1 + s) * a.h_stride + b * 32;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = src[j];
-        to_block_fp(v, hq + (size_t)i * 16, hs + i);
+        s_nvalid[m][s] = nv;
     }
+    __syncthreads();
+    convert_blocks<8>(
+        M * K1 * nsbh,
+        [&](int i, int ln) {
+            const int b = i % nsbh, ms = i / nsbh;
+            return b < s_nvalid[ms / K1][ms % K1] ? a.h[(size_t)ms * a.h_stride + b * 32 + ln] : 0.0f;
+        },
+        [&](int i, int ln, int pw, float st) {
+            if (ln < 16) hq[(size_t)i * 16 + ln] = pw;
+            if (ln == 0) hs[i] = st;
+        });
     __syncthreads();
 
     const int nsb_r = a.dn_nseg * a.dn_nsub;
@@ -321,47 +330,71 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
         float acc[MAXM];
 #pragma unroll
         for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
-        for (int p = lane; p < P; p += 32) {
-            int u, t, nsub, ib0;
-            const uint8_t* row;
-            if (p < n_routed * nsb_r) {
-                u = p / nsb_r;
-                t = p - u * nsb_r;
-                row = a.down + (size_t)plan.expert[u] * a.dn_expert_bytes + (size_t)j * rb_r;
-                nsub = a.dn_nsub;
-                ib0 = a.dn_ib0;
-            } else {
-                u = n_routed;
-                t = p - n_routed * nsb_r;
-                row = a.sh_down + (size_t)j * rb_s;
-                nsub = a.sh_nsub;
-                ib0 = a.sh_ib0;
-            }
-            const int seg = t / nsub, ibl = t - seg * nsub;
-            const uint8_t* sp = row + seg * (8 + 16 * nsub);
-            const uint2 hdr = ldg2(sp);
-            const uint2 q0 = ldg2(sp + 8 + 16 * ibl);
-            const uint2 q1 = ldg2(sp + 16 + 16 * ibl);
-            const float dl = qmoe_half_bits_to_float((uint16_t)(hdr.x & 0xFFFFu)) *
-                             (float)(qmoe_iq4xs_ls(hdr.x, hdr.y, ib0 + ibl) - 32);
-            const uint32_t tmask = (u < n_routed) ? plan.mask[u] : all;
+        // Batches of kPB (expert, sub-block) pairs per lane: every load of a
+        // batch is issued before any decode.
+        constexpr int kPB = 6;
+        for (int p0 = lane; p0 < P; p0 += 32 * kPB) {
+            uint2 hdr[kPB], q0[kPB], q1[kPB];
+            int ib[kPB];
 #pragma unroll
-            for (int m = 0; m < MAXM; ++m) {
-                if (m < M && ((tmask >> m) & 1u)) {
-                    const int s = (u < n_routed) ? plan.slot[u][m] : a.k;
-                    const size_t hb = ((size_t)m * K1 + s) * nsbh + t;
-                    int xp[16];
-                    const int4* src = reinterpret_cast<const int4*>(hq + hb * 16);
-#pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        const int4 w4 = src[v];
-                        xp[4 * v] = w4.x;
-                        xp[4 * v + 1] = w4.y;
-                        xp[4 * v + 2] = w4.z;
-                        xp[4 * v + 3] = w4.w;
+            for (int i = 0; i < kPB; ++i) {
+                const int p = p0 + 32 * i;
+                if (p < P) {
+                    int u, t, nsub, ib0;
+                    const uint8_t* row;
+                    if (p < n_routed * nsb_r) {
+                        u = p / nsb_r;
+                        t = p - u * nsb_r;
+                        row = a.down + (size_t)plan.expert[u] * a.dn_expert_bytes + (size_t)j * rb_r;
+                        nsub = a.dn_nsub;
+                        ib0 = a.dn_ib0;
+                    } else {
+                        t = p - n_routed * nsb_r;
+                        row = a.sh_down + (size_t)j * rb_s;
+                        nsub = a.sh_nsub;
+                        ib0 = a.sh_ib0;
                     }
-                    const int S = qmoe_subblock_dot(q0.x, q0.y, q1.x, q1.y, xp, 0);
-                    acc[m] = fmaf(s_w[m][s] * dl * hs[hb], (float)S, acc[m]);
+                    const int seg = t / nsub, ibl = t - seg * nsub;
+                    const uint8_t* sp = row + seg * (8 + 16 * nsub);
+                    hdr[i] = ldg2(sp);
+                    q0[i] = ldg2(sp + 8 + 16 * ibl);
+                    q1[i] = ldg2(sp + 16 + 16 * ibl);
+                    ib[i] = ib0 + ibl;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kPB; ++i) {
+                const int p = p0 + 32 * i;
+                if (p >= P) break;
+                int u, t;
+                if (p < n_routed * nsb_r) {
+                    u = p / nsb_r;
+                    t = p - u * nsb_r;
+                } else {
+                    u = n_routed;
+                    t = p - n_routed * nsb_r;
+                }
+                const float dl = qmoe_half_bits_to_float((uint16_t)(hdr[i].x & 0xFFFFu)) *
+                                 (float)(qmoe_iq4xs_ls(hdr[i].x, hdr[i].y, ib[i]) - 32);
+                const uint32_t tmask = (u < n_routed) ? plan.mask[u] : all;
+#pragma unroll
+                for (int m = 0; m < MAXM; ++m) {
+                    if (m < M && ((tmask >> m) & 1u)) {
+                        const int s = (u < n_routed) ? plan.slot[u][m] : a.k;
+                        const size_t hb = ((size_t)m * K1 + s) * nsbh + t;
+                        int xp[16];
+                        const int4* src = reinterpret_cast<const int4*>(hq + hb * 16);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            const int4 w4 = src[v];
+                            xp[4 * v] = w4.x;
+                            xp[4 * v + 1] = w4.y;
+                            xp[4 * v + 2] = w4.z;
+                            xp[4 * v + 3] = w4.w;
+                        }
+                        const int S = qmoe_subblock_dot(q0[i].x, q0[i].y, q1[i].x, q1[i].y, xp, 0);
+                        acc[m] = fmaf(s_w[m][s] * dl * hs[hb], (float)S, acc[m]);
+                    }
                 }
             }
         }

@@ -1,10 +1,9 @@
 // Router GEMV, top-k selection and renormalisation in one launch.
 //
 // Behaviour follows reference/model.py:399-403: logits = x . W_r^T in fp32,
-// softmax, top-k, weights divided by their sum.  Softmax is monotone, so the
-// k largest probabilities are the k largest logits, and the renormalised
-// weights equal exp(l_i - l_max) / sum_topk exp(l_j - l_max) because the
-// global softmax denominator cancels.  Ties go to the lower expert id, the
+// softmax, top-k, weights divided by their sum.  The global softmax
+// denominator is common to every expert, so ranking and renormalising use the
+// numerators exp(l_i - l_max) alone: w_i = p_i / sum_topk p_j.  Ties go to the lower expert id, the
 // rule of scripts/kernels/router_select.cpp:163-164 (EXACT_TOPK mode).
 //
 // Layout: every warp owns one router row (512 rows + the shared-expert gate
@@ -18,7 +17,7 @@
 namespace qmoe {
 namespace {
 
-constexpr int kRouteWarps = 8;
+constexpr int kRouteWarps = 4;
 constexpr int kCandCap = 192;  // candidate slots per warp before the tie fallback
 
 __device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
@@ -26,28 +25,42 @@ __device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
 }
 
 // Top-k of E logits (E % 32 == 0, E <= 1024, k <= 16) for one token, by one
-// warp.  Writes the k (logit, id) pairs in descending order to sv/si.
+// warp.  Selection is on p_i = exp(l_i - l_max), the softmax numerators: the
+// reference ranks fp32 softmax probabilities (reference/model.py:400-401),
+// so logits closer together than fp32 resolves after exp must tie there too
+// (they do when activations are tiny), and ties go to the lower id.  Writes
+// the k (p, id) pairs in descending order to sv/si; returns l_max.
 //
 // Every element of the top k is at least as good as T0, the k-th best of the
 // 32 per-lane maxima (those k maxima are k distinct elements not worse than
-// T0), so only elements not worse than T0 are ranked.  With distinct logits
+// T0), so only elements not worse than T0 are ranked.  With distinct values
 // that is typically k to 2k candidates; a run of ties larger than the
 // candidate buffer falls back to k rounds of warp arg-max.
-__device__ void warp_topk(const float* __restrict__ logits, int E, int k, float* cv, int* ci,
-                          float* sv, int* si) {
+__device__ float warp_topk(const float* __restrict__ logits, int E, int k, float* cv, int* ci,
+                           float* sv, int* si) {
     const int lane = threadIdx.x & 31;
     const int npl = E >> 5;
     float v[32];
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
+    float lmax = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         if (j < npl) {
             float t = __ldcg(logits + lane + 32 * j);
             if (t != t) t = -INFINITY;  // NaN ranks last
             v[j] = t;
-            if (better(t, lane + 32 * j, bv, bi)) {
-                bv = t;
+            lmax = fmaxf(lmax, t);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (j < npl) {
+            v[j] = expf(v[j] - lmax);
+            if (better(v[j], lane + 32 * j, bv, bi)) {
+                bv = v[j];
                 bi = lane + 32 * j;
             }
         }
@@ -98,10 +111,10 @@ __device__ void warp_topk(const float* __restrict__ logits, int E, int k, float*
             }
         }
         __syncwarp();
-        return;
+        return lmax;
     }
 
-    // Fallback for long runs of equal logits: k rounds of warp arg-max.
+    // Fallback for long runs of equal values: k rounds of warp arg-max.
     uint32_t taken = 0;
     for (int r = 0; r < k; ++r) {
         float lv = -INFINITY;
@@ -131,6 +144,7 @@ __device__ void warp_topk(const float* __restrict__ logits, int E, int k, float*
         if (li == wi && li != 0x7fffffff) taken |= 1u << ((wi - lane) >> 5);
     }
     __syncwarp();
+    return lmax;
 }
 
 template <int MAXM>
@@ -154,16 +168,27 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
         float acc[MAXM];
 #pragma unroll
         for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
-        for (int c = lane * 4; c < D; c += 128) {
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(w + c));
+        // 16 independent 128-bit loads in flight per lane before any use.
+        for (int c0 = 0; c0 < D; c0 += 16 * 128) {
+            float4 wv[16];
 #pragma unroll
-            for (int m = 0; m < MAXM; ++m) {
-                if (m < M) {
-                    const float4 xv = *reinterpret_cast<const float4*>(xs + m * D + c);
-                    acc[m] = fmaf(wv.x, xv.x, acc[m]);
-                    acc[m] = fmaf(wv.y, xv.y, acc[m]);
-                    acc[m] = fmaf(wv.z, xv.z, acc[m]);
-                    acc[m] = fmaf(wv.w, xv.w, acc[m]);
+            for (int i = 0; i < 16; ++i) {
+                const int c = c0 + i * 128 + lane * 4;
+                wv[i] = c < D ? __ldg(reinterpret_cast<const float4*>(w + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int c = c0 + i * 128 + lane * 4;
+                if (c >= D) break;
+#pragma unroll
+                for (int m = 0; m < MAXM; ++m) {
+                    if (m < M) {
+                        const float4 xv = *reinterpret_cast<const float4*>(xs + m * D + c);
+                        acc[m] = fmaf(wv[i].x, xv.x, acc[m]);
+                        acc[m] = fmaf(wv[i].y, xv.y, acc[m]);
+                        acc[m] = fmaf(wv[i].z, xv.z, acc[m]);
+                        acc[m] = fmaf(wv[i].w, xv.w, acc[m]);
+                    }
                 }
             }
         }
@@ -193,14 +218,11 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
             if (lane == 0 && a.shared_logit) a.shared_logit[m] = __ldcg(lg);
             continue;
         }
-        warp_topk(lg, E, a.k, s_cv[warp], s_ci[warp], s_sv[warp], s_si[warp]);
-        const float lmax = s_sv[warp][0];
-        float e = 0.0f;
-        if (lane < a.k) e = expf(s_sv[warp][lane] - lmax);
+        const float lmax = warp_topk(lg, E, a.k, s_cv[warp], s_ci[warp], s_sv[warp], s_si[warp]);
+        const float e = lane < a.k ? s_sv[warp][lane] : 0.0f;
         const float sum = warp_sum(e);
         if (lane < a.k) {
-            const float lv = s_sv[warp][lane];
-            if (!(fabsf(lv) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
+            if (!(fabsf(lmax) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
             a.ids[m * a.k + lane] = s_si[warp][lane];
             a.weights[m * a.k + lane] = e / sum;
         }
