@@ -166,6 +166,23 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
                       int n_layers, const qmoe_dims* dims, float* out, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* The MoE block for callers that cannot allocate device memory: the same
+ * computation as qmoe_moe_block, with no workspace argument.  No counterpart
+ * in the reference: it exists for hosts bound through a plain C ABI (cgo,
+ * JNI, N-API) without a device allocator, plug-ins whose process's device
+ * memory belongs to another framework's allocator, and serving loops that
+ * forbid allocation after start-up.  It calls no cudaMalloc, cudaFree or
+ * allocating library routine; its scratch is a file-scope device array of
+ * QMOE_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * the process exits.  Calls needing more scratch than that (see
+ * qmoe_workspace_bytes) return QMOE_ERR_WORKSPACE.  All calls on a device
+ * share the array: calls that overlap on the GPU race, so order them.  The
+ * first call on a device looks up the array's address and must come before
+ * any stream capture. */
+#define QMOE_NOALLOC_SCRATCH_BYTES (1u << 20)
+int qmoe_moe_block_noalloc(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                           const qmoe_dims* dims, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -99,6 +99,7 @@ _SIGS = {
                                    c_size_t, _P]),
     "qmoe_stack_decode": (c_int, [_P, c_int, POINTER(LayerWeights), c_int, POINTER(Dims), _P, _P,
                                   c_size_t, _P]),
+    "qmoe_moe_block_noalloc": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P]),
 }
 
 for _name, (_res, _args) in _SIGS.items():
