@@ -10,8 +10,10 @@ one replay of the CUDA graph of the whole stack.
   e2e       the same through the public API with host buffers: per step the
             pinned host x is copied in, the stack runs, the fp32 output is read
             back and the host waits for it
-  roofline  the dominant kernel (gate|up + SwiGLU): its algorithmic bytes per
-            launch / its average duration from CUDA events in this run
+  roofline  the dominant kernel -- the single-launch stack kernel when it
+            applies (one token, unsharded), else gate|up + SwiGLU: its
+            algorithmic bytes per launch / its average duration from CUDA
+            events in this run
   cpu_baseline  the CPU oracle (a restatement of reference/model.py:387-417
             with cold IQ4_XS dequant) on a bounded sample of layers, scaled
             to 48 layers
@@ -268,8 +270,16 @@ def main() -> None:
         ms_step = ms / args.steps
         us_tok = ms_step * 1000.0 / M
         bytes_tok = cfg.n_layers * cfg.layer_expert_bytes() / max(world, 1) if M == 1 else None
-        gu_bytes = (cfg.top_k + (1 if shard.has_shared() else 0)) * 2 * shard.dims(cfg).inter_local * cfg.gate_up_row_bytes
-        gu_gbs = gu_bytes / (stage["gateup_us"] * 1e-6) / 1e9
+        single = world == 1 and stack.single_launch(M)
+        if single:
+            # one persistent launch per step: its bytes are the whole stack's
+            rl_kernel, rl_bytes, rl_us = "stack_kernel", bytes_tok, ms_step * 1000.0
+        else:
+            rl_kernel = "gateup_swiglu"
+            rl_bytes = (cfg.top_k + (1 if shard.has_shared() else 0)) * 2 * shard.dims(cfg).inter_local \
+                * cfg.gate_up_row_bytes
+            rl_us = stage["gateup_us"]
+        rl_gbs = rl_bytes / (rl_us * 1e-6) / 1e9
         line = {
             "metric": METRIC, "value": round(us_tok, 3), "unit": "us/token", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -286,13 +296,14 @@ def main() -> None:
             },
             "e2e": {"value": round(ms_e2e / args.steps * 1000.0 / M, 3), "unit": "us/token",
                     "h2d_bytes_per_step": M * cfg.hidden * 2, "d2h_bytes_per_step": M * cfg.hidden * 4},
-            "gpu_launches": 3 * cfg.n_layers * args.steps,
+            "gpu_launches": (1 if single else 3 * cfg.n_layers) * args.steps,
             "roofline": {
-                "kernel": "gateup_swiglu", "bound": "hbm", "achieved": round(gu_gbs, 1), "peak": hbm,
-                "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(gu_gbs / hbm, 4), "traffic": None,
-                "bytes_per_launch": gu_bytes, "avg_launch_us": round(stage["gateup_us"], 3),
+                "kernel": rl_kernel, "bound": "hbm", "achieved": round(rl_gbs, 1), "peak": hbm,
+                "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(rl_gbs / hbm, 4), "traffic": None,
+                "bytes_per_launch": rl_bytes, "avg_launch_us": round(rl_us, 3),
+                "frac_of_nominal_8tbs": round(rl_gbs / NOMINAL_HBM_GBS, 4),
             },
-            "stage_us": {k: round(v, 3) for k, v in stage.items()},
+            "per_layer_path_stage_us": {k: round(v, 3) for k, v in stage.items()},
             "clocks": clocks,
         }
         if bytes_tok:

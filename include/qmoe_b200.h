@@ -39,7 +39,9 @@ enum qmoe_status_code {
     QMOE_ERR_WORKSPACE = 4,        /* workspace missing or too small               */
     QMOE_ERR_CUDA = 5,             /* a CUDA runtime call failed                   */
     QMOE_ERR_DEVICE_RANGE = 6,     /* a kernel saw an expert id out of range       */
-    QMOE_ERR_NOT_FINITE = 7        /* a kernel saw a non-finite router logit       */
+    QMOE_ERR_NOT_FINITE = 7,       /* a kernel saw a non-finite router logit       */
+    QMOE_ERR_TIMEOUT = 8           /* a bounded device wait (grid barrier or bulk
+                                      copy) ran out: the kernel stopped early     */
 };
 
 /* Activation element types accepted by the entry points. */
@@ -147,6 +149,26 @@ int qmoe_down_combine(const float* h, int h_stride, int n_tokens, const int32_t*
 int qmoe_moe_block(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
                    const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
                    void* stream);
+
+/* 1 when qmoe_stack_decode runs these shapes as one persistent launch (one
+ * token, hidden 1024 or 2048, inter 512 with a 512-row shared expert,
+ * unsharded, <= 64 layers, operands 16-byte aligned), else 0 (three launches
+ * per layer).  The whole-stack analogue of the traced step
+ * (tt/traced.py:261-277), which replays all 48 layers' MoE ops at once. */
+int qmoe_stack_single_launch(const qmoe_dims* dims, int n_tokens, int n_layers);
+
+/* Tracing: the single-launch stack kernel stamps its SM's cycle counter at 16
+ * points of every layer in CTA 0 into the workspace: phase A start, x
+ * loaded, x converted, router/shared rows resident, A computed, A done (0-5);
+ * after barrier 1, top-k done, routed copies issued, routed gate|up done, B
+ * done (6-10); after barrier 2, h converted, down rows resident, down done,
+ * C done (11-15); the last CTA stamps the same points.  Copies the
+ * n_layers x 16 stamps of CTA 0 and then those of the last CTA (2 x n_layers
+ * x 16 values) of the last launch made with this workspace and n_tokens to
+ * host_out (synchronises `stream`).  The
+ * reference's analogue is its section profiler (tt/bench.py:33-78). */
+int qmoe_read_stack_trace(void* workspace, const qmoe_dims* dims, int n_tokens, int n_layers,
+                          uint64_t* host_out, void* stream);
 
 /* The shared expert alone: sigmoid(x . gate_vec) * down(silu(gate x) * up x).
  * Replaces tt/moe.py:983-1044 (shared_expert) and reference/model.py:392-397.

@@ -220,6 +220,37 @@ def test_stack_matches_layer_chain_and_oracle(pkg, oracle):
     assert torch.equal(out_graph, act)
 
 
+def test_stack_kernel_matches_layer_chain(pkg, oracle):
+    """The single-launch stack kernel (one token, hidden 1024/2048, inter 512)
+    against the three-launch-per-layer path and the oracle, layer by layer."""
+    cfg = pkg.MoEConfig(hidden=1024, inter=512, n_experts=64, top_k=10, shared_inter=512, n_layers=3)
+    hls = [pkg.synth_host_layer(cfg, layer=l, seed=31, all_experts=True) for l in range(cfg.n_layers)]
+    dls = [pkg.upload_host_layer(h) for h in hls]
+    x = pkg.synth_x(cfg, 1, seed=31).cuda()
+    act = x
+    checked = 0
+    for n in range(1, cfg.n_layers + 1):
+        stack = pkg.MoEStack(dls[:n], max_tokens=1)
+        got = stack.decode(x).clone()
+        torch.cuda.synchronize()
+        stack.ws.raise_if_error("stack kernel")
+        # chain of per-layer launches up to layer n-1
+        ml = pkg.MoELayer(dls[n - 1])
+        want = ml(act)
+        ref = oracle.moe_forward(act.float().cpu().numpy(), oracle.ExpertSource.from_host_layer(hls[n - 1]),
+                                 cfg.top_k)
+        if well_conditioned(ref["probs"], cfg.top_k):
+            assert oracle.max_rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 2e-3, f"layers {n}"
+            assert oracle.max_rel_err(got.cpu().numpy(), ref["out"]) <= TOL, f"layers {n}"
+            checked += 1
+        act = want.to(torch.bfloat16)
+    assert checked >= 2
+    # repeated launches reuse the workspace: identical bits
+    again = stack.decode(x).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(again, got)
+
+
 def test_deterministic_reruns(pkg):
     g = load_golden("moe_c1_m8.npz")
     hl, dl = device_layer(pkg, g)

@@ -20,6 +20,7 @@ QMOE_ERR_WORKSPACE = 4
 QMOE_ERR_CUDA = 5
 QMOE_ERR_DEVICE_RANGE = 6
 QMOE_ERR_NOT_FINITE = 7
+QMOE_ERR_TIMEOUT = 8
 
 QMOE_ACT_BF16 = 0
 QMOE_ACT_F32 = 1
@@ -99,6 +100,8 @@ _SIGS = {
                                    c_size_t, _P]),
     "qmoe_stack_decode": (c_int, [_P, c_int, POINTER(LayerWeights), c_int, POINTER(Dims), _P, _P,
                                   c_size_t, _P]),
+    "qmoe_read_stack_trace": (c_int, [_P, POINTER(Dims), c_int, c_int, _P, _P]),
+    "qmoe_stack_single_launch": (c_int, [POINTER(Dims), c_int, c_int]),
     "qmoe_moe_block_noalloc": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P]),
 }
 

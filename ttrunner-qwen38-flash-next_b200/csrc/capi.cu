@@ -126,6 +126,9 @@ struct Ws {
     float* weights() const { return (float*)(base + L.weights); }
     float* shared() const { return (float*)(base + L.shared); }
     float* h() const { return (float*)(base + L.h); }
+    float* act() const { return (float*)(base + L.act); }
+    unsigned* sync() const { return (unsigned*)(base + L.sync); }
+    unsigned long long* trace() const { return (unsigned long long*)(base + L.trace); }
 };
 
 int get_ws(void* workspace, size_t bytes, const qmoe_dims* d, int M, Ws* ws) {
@@ -193,6 +196,12 @@ WsLayout ws_layout(const qmoe_dims& d, int max_tokens) {
     off = align_up(off + (size_t)M * 4, 256);
     L.h = off;
     off = align_up(off + (size_t)M * (d.top_k + 1) * L.h_stride * 4, 256);
+    L.act = off;
+    off = align_up(off + (size_t)M * d.hidden * 4, 256);
+    L.sync = off;
+    off = align_up(off + 1152, 256);
+    L.trace = off;
+    off = align_up(off + 2 * 64 * 16 * 8, 256);
     L.total = off;
     return L;
 }
@@ -220,6 +229,7 @@ const char* qmoe_status_string(int status) {
         case QMOE_ERR_CUDA: return "CUDA runtime error";
         case QMOE_ERR_DEVICE_RANGE: return "expert id out of range";
         case QMOE_ERR_NOT_FINITE: return "non-finite router logit";
+        case QMOE_ERR_TIMEOUT: return "a bounded device wait timed out";
         default: return "unknown status";
     }
 }
@@ -391,6 +401,26 @@ int qmoe_shared_expert(const void* x, int x_dtype, int n_tokens, const qmoe_laye
     return cuda_status(launch_down(a, s));
 }
 
+int qmoe_read_stack_trace(void* workspace, const qmoe_dims* dims, int n_tokens, int n_layers,
+                          uint64_t* host_out, void* stream) {
+    QMOE_TRY(check_dims(dims));
+    if (!workspace || !host_out || n_layers < 1 || n_layers > 64) return QMOE_ERR_INVALID_ARG;
+    const WsLayout L = ws_layout(*dims, n_tokens);
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t rows = (size_t)n_layers * 16 * sizeof(uint64_t);
+    QMOE_TRY(cuda_status(cudaMemcpyAsync(host_out, (unsigned char*)workspace + L.trace, rows,
+                                         cudaMemcpyDeviceToHost, s)));
+    QMOE_TRY(cuda_status(cudaMemcpyAsync(host_out + (size_t)n_layers * 16,
+                                         (unsigned char*)workspace + L.trace + 64 * 16 * sizeof(uint64_t), rows,
+                                         cudaMemcpyDeviceToHost, s)));
+    return cuda_status(cudaStreamSynchronize(s));
+}
+
+int qmoe_stack_single_launch(const qmoe_dims* dims, int n_tokens, int n_layers) {
+    if (check_dims(dims) != QMOE_OK) return 0;
+    return stack_kernel_supported(*dims, n_tokens, n_layers) ? 1 : 0;
+}
+
 int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* layers, int n_layers,
                       const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
                       void* stream) {
@@ -409,7 +439,19 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
                                    dims, ws.h(), ws.L.h_stride, out, nullptr);
     QMOE_TRY(check_smem(probe));
     cudaStream_t s = (cudaStream_t)stream;
-    // Layer L+1 reads `out` (layer L's result) in its router and gate|up
+    // One token, BASELINE-family shapes, unsharded, every operand 16-byte
+    // aligned: the whole stack is one persistent launch.
+    bool aligned16 = aligned(x, 16) && aligned(out, 16);
+    for (int l = 0; l < n_layers && aligned16; ++l) {
+        const qmoe_layer_weights& w = layers[l];
+        aligned16 = w.gate_vec && w.sh_gate_up && w.sh_down && aligned(w.router, 16) && aligned(w.gate_vec, 16) &&
+                    aligned(w.gate_up, 16) && aligned(w.down, 16) && aligned(w.sh_gate_up, 16) &&
+                    aligned(w.sh_down, 16);
+    }
+    if (aligned16 && stack_kernel_supported(*dims, n_tokens, n_layers))
+        return cuda_status(launch_stack_kernel(x, out, ws.act(), ws.logits(), ws.h(), ws.sync(), ws.trace(), ws.status(), layers,
+                                               n_layers, *dims, s));
+    // Otherwise three launches per layer. Layer L+1 reads `out` (layer L's result) in its router and gate|up
     // launches; its down launch overwrites `out` only after both, in stream
     // order, so one buffer carries the activation through the stack.
     for (int l = 0; l < n_layers; ++l) {

@@ -25,6 +25,9 @@ struct WsLayout {
     size_t weights;     // fp32 [max_tokens][top_k]
     size_t shared;      // fp32 [max_tokens]
     size_t h;           // fp32 [max_tokens][top_k + 1][h_stride]
+    size_t act;         // fp32 [max_tokens][hidden]: the stack kernel's layer activation
+    size_t sync;        // grid-barrier counters (8 x 128 B) and the abort word
+    size_t trace;       // u64 [64 layers][8]: the stack kernel's phase timestamps
     size_t total;
     int h_stride;
 };
@@ -84,6 +87,12 @@ cudaError_t launch_synth_f32(uint64_t seed, uint64_t sid, int64_t n, float std_d
                              cudaStream_t s);
 
 int device_sm_count();
+
+// The single-launch decode stack kernel (stack_kernel.cu).
+bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers);
+cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* logits, float* h, unsigned* sync,
+                                unsigned long long* trace, int* status, const qmoe_layer_weights* layers, int n_layers,
+                                const qmoe_dims& d, cudaStream_t stream);
 
 }  // namespace qmoe
 

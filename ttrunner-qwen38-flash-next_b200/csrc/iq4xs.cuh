@@ -237,28 +237,31 @@ __device__ __forceinline__ void qmoe_lut8(uint32_t w, uint32_t& lo, uint32_t& hi
 // bytes as words.  Exact in int32.
 __device__ __forceinline__ int qmoe_subblock_dot(uint32_t q0, uint32_t q1, uint32_t q2, uint32_t q3,
                                                  const int* xp, int acc) {
-    uint32_t lo, hi;
-    qmoe_lut8(q0, lo, hi);
-    acc = __dp2a_lo(xp[0], (int)lo, acc);
-    acc = __dp2a_hi(xp[1], (int)lo, acc);
-    acc = __dp2a_lo(xp[2], (int)hi, acc);
-    acc = __dp2a_hi(xp[3], (int)hi, acc);
-    qmoe_lut8(q1, lo, hi);
-    acc = __dp2a_lo(xp[4], (int)lo, acc);
-    acc = __dp2a_hi(xp[5], (int)lo, acc);
-    acc = __dp2a_lo(xp[6], (int)hi, acc);
-    acc = __dp2a_hi(xp[7], (int)hi, acc);
-    qmoe_lut8(q2, lo, hi);
-    acc = __dp2a_lo(xp[8], (int)lo, acc);
-    acc = __dp2a_hi(xp[9], (int)lo, acc);
-    acc = __dp2a_lo(xp[10], (int)hi, acc);
-    acc = __dp2a_hi(xp[11], (int)hi, acc);
-    qmoe_lut8(q3, lo, hi);
-    acc = __dp2a_lo(xp[12], (int)lo, acc);
-    acc = __dp2a_hi(xp[13], (int)lo, acc);
-    acc = __dp2a_lo(xp[14], (int)hi, acc);
-    acc = __dp2a_hi(xp[15], (int)hi, acc);
-    return acc;
+    // Four independent dp2a chains (one per qs word), summed at the end:
+    // integer addition is exact, so the order does not change the result,
+    // and the chains overlap instead of queueing on one accumulator.
+    uint32_t lo0, hi0, lo1, hi1, lo2, hi2, lo3, hi3;
+    qmoe_lut8(q0, lo0, hi0);
+    qmoe_lut8(q1, lo1, hi1);
+    qmoe_lut8(q2, lo2, hi2);
+    qmoe_lut8(q3, lo3, hi3);
+    int a0 = __dp2a_lo(xp[0], (int)lo0, 0);
+    int a1 = __dp2a_lo(xp[4], (int)lo1, 0);
+    int a2 = __dp2a_lo(xp[8], (int)lo2, 0);
+    int a3 = __dp2a_lo(xp[12], (int)lo3, 0);
+    a0 = __dp2a_hi(xp[1], (int)lo0, a0);
+    a1 = __dp2a_hi(xp[5], (int)lo1, a1);
+    a2 = __dp2a_hi(xp[9], (int)lo2, a2);
+    a3 = __dp2a_hi(xp[13], (int)lo3, a3);
+    a0 = __dp2a_lo(xp[2], (int)hi0, a0);
+    a1 = __dp2a_lo(xp[6], (int)hi1, a1);
+    a2 = __dp2a_lo(xp[10], (int)hi2, a2);
+    a3 = __dp2a_lo(xp[14], (int)hi3, a3);
+    a0 = __dp2a_hi(xp[3], (int)hi0, a0);
+    a1 = __dp2a_hi(xp[7], (int)hi1, a1);
+    a2 = __dp2a_hi(xp[11], (int)hi2, a2);
+    a3 = __dp2a_hi(xp[15], (int)hi3, a3);
+    return acc + ((a0 + a1) + (a2 + a3));
 }
 
 // Block floating point for an activation sub-block: the power-of-two step

@@ -13,140 +13,12 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "topk.cuh"
 
 namespace qmoe {
 namespace {
 
 constexpr int kRouteWarps = 4;
-constexpr int kCandCap = 192;  // candidate slots per warp before the tie fallback
-
-__device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
-    return a > b || (a == b && ia < ib);
-}
-
-// Top-k of E logits (E % 32 == 0, E <= 1024, k <= 16) for one token, by one
-// warp.  Selection is on p_i = exp(l_i - l_max), the softmax numerators: the
-// reference ranks fp32 softmax probabilities (reference/model.py:400-401),
-// so logits closer together than fp32 resolves after exp must tie there too
-// (they do when activations are tiny), and ties go to the lower id.  Writes
-// the k (p, id) pairs in descending order to sv/si; returns l_max.
-//
-// Every element of the top k is at least as good as T0, the k-th best of the
-// 32 per-lane maxima (those k maxima are k distinct elements not worse than
-// T0), so only elements not worse than T0 are ranked.  With distinct values
-// that is typically k to 2k candidates; a run of ties larger than the
-// candidate buffer falls back to k rounds of warp arg-max.
-__device__ float warp_topk(const float* __restrict__ logits, int E, int k, float* cv, int* ci,
-                           float* sv, int* si) {
-    const int lane = threadIdx.x & 31;
-    const int npl = E >> 5;
-    float v[32];
-    float lmax = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        if (j < npl) {
-            float t = __ldcg(logits + lane + 32 * j);
-            if (t != t) t = -INFINITY;  // NaN ranks last
-            v[j] = t;
-            lmax = fmaxf(lmax, t);
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        if (j < npl) {
-            v[j] = expf(v[j] - lmax);
-            if (better(v[j], lane + 32 * j, bv, bi)) {
-                bv = v[j];
-                bi = lane + 32 * j;
-            }
-        }
-    }
-    int rank = 0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const float ov = __shfl_sync(0xffffffffu, bv, j);
-        const int oi = __shfl_sync(0xffffffffu, bi, j);
-        rank += better(ov, oi, bv, bi) ? 1 : 0;
-    }
-    const unsigned sel = __ballot_sync(0xffffffffu, rank == k - 1);
-    const int src = __ffs(sel) - 1;
-    const float tv = __shfl_sync(0xffffffffu, bv, src);
-    const int ti = __shfl_sync(0xffffffffu, bi, src);
-
-    int c = 0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-        if (j < npl && !better(tv, ti, v[j], lane + 32 * j)) ++c;
-    int incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    const int total = __shfl_sync(0xffffffffu, incl, 31);
-
-    if (total <= kCandCap) {
-        int pos = incl - c;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            if (j < npl && !better(tv, ti, v[j], lane + 32 * j)) {
-                cv[pos] = v[j];
-                ci[pos] = lane + 32 * j;
-                ++pos;
-            }
-        }
-        __syncwarp();
-        for (int cc = lane; cc < total; cc += 32) {
-            const float mv = cv[cc];
-            const int mi = ci[cc];
-            int r = 0;
-            for (int j = 0; j < total; ++j) r += better(cv[j], ci[j], mv, mi) ? 1 : 0;
-            if (r < k) {
-                sv[r] = mv;
-                si[r] = mi;
-            }
-        }
-        __syncwarp();
-        return lmax;
-    }
-
-    // Fallback for long runs of equal values: k rounds of warp arg-max.
-    uint32_t taken = 0;
-    for (int r = 0; r < k; ++r) {
-        float lv = -INFINITY;
-        int li = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            if (j < npl && !((taken >> j) & 1u) && better(v[j], lane + 32 * j, lv, li)) {
-                lv = v[j];
-                li = lane + 32 * j;
-            }
-        }
-        float wv = lv;
-        int wi = li;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
-            if (better(ov, oi, wv, wi)) {
-                wv = ov;
-                wi = oi;
-            }
-        }
-        if (lane == 0) {
-            sv[r] = wv;
-            si[r] = wi;
-        }
-        if (li == wi && li != 0x7fffffff) taken |= 1u << ((wi - lane) >> 5);
-    }
-    __syncwarp();
-    return lmax;
-}
-
 template <int MAXM>
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
     extern __shared__ __align__(16) float xs[];  // [M][D]

@@ -43,6 +43,25 @@ class MoEStack:
     def n_layers(self) -> int:
         return len(self.layers)
 
+    TRACE_POINTS = ("A start", "x loaded", "x converted", "rows resident", "A computed", "A done",
+                    "after barrier 1", "top-k done", "copies issued", "gate|up done", "B done",
+                    "after barrier 2", "h converted", "down resident", "down done", "C done")
+
+    def phase_trace(self, m: int = 1):
+        """Raw SM cycle-counter stamps of the last single-launch step,
+        [2, n_layers, 16]: CTA 0 then the last CTA, in the order of
+        TRACE_POINTS."""
+        import numpy as np
+
+        buf = np.zeros((2, self.n_layers, 16), dtype=np.uint64)
+        check(lib.qmoe_read_stack_trace(self.ws.ptr, ctypes.byref(self.dims), m, self.n_layers,
+                                        buf.ctypes.data, _stream()), "qmoe_read_stack_trace")
+        return buf
+
+    def single_launch(self, m: int = 1) -> bool:
+        """True when a step of m tokens is one persistent kernel launch."""
+        return bool(lib.qmoe_stack_single_launch(ctypes.byref(self.dims), m, self.n_layers))
+
     def _launch(self, m: int) -> None:
         check(lib.qmoe_stack_decode(self.x_in.data_ptr(), m, self.c_layers, self.n_layers,
                                     ctypes.byref(self.dims), self.out.data_ptr(), self.ws.ptr,
