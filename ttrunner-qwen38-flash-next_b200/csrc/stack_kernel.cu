@@ -101,7 +101,7 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     s.suv = sk_take(o, s.NSQ * 4);
     s.rpart = sk_take(o, s.NR * 4 * 4);
     s.dpart = sk_take(o, (unsigned)s.NJ * (K + 1) * 4);
-    s.cand = sk_take(o, (unsigned)E * 8);
+    s.cand = sk_take(o, (unsigned)(E > 256 ? E : 256) * 8);  // the tie fallback keeps 16 x k
     s.wmax = sk_take(o, (kSKWarps + 1) * 8);
     s.red = sk_take(o, kSKWarps * 4);
     s.tkv = sk_take(o, kMaxTopK * 4);
@@ -192,10 +192,8 @@ __device__ bool grid_sync(unsigned* sync, unsigned gen, int* status, int* s_ok) 
     __syncthreads();
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        if (lane == 0) {
-            __threadfence();
+        if (lane == 0)  // release: orders this CTA's writes (after bar.sync) before the arrival
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(sync + 32 * (blockIdx.x & 7)) : "memory");
-        }
         const int i = lane & 7;
         const unsigned n = gridDim.x;
         const unsigned cnt = n > (unsigned)i ? (n - (unsigned)i + 7u) / 8u : 0u;

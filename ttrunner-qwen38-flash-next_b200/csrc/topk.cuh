@@ -147,7 +147,7 @@ namespace qmoe {
 //   3. keys >= T0 are the candidates (k..~2k for distinct logits, up to all
 //      of them for a long run of ties), each ranked against all candidates.
 // Results in tkv (p values) and tki (ids), descending.  Returns l_max.
-// Scratch (shared): cand[E] u64, wmax[nwarps + 1] u64, red[nwarps] u32, cnt.
+// Scratch (shared): cand[max(E, nwarps * k)] u64, wmax[nwarps + 1] u64, red[nwarps] u32, cnt.
 __device__ __forceinline__ unsigned topk_ord(float f) {
     const unsigned b = __float_as_uint(f);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
@@ -196,13 +196,55 @@ static __device__ __noinline__ float block_topk(const float* __restrict__ logits
     if (i1 < E && k1 >= T0) cand[atomicAdd(cnt, 1)] = k1;
     __syncthreads();
     const int C = *cnt;
-    for (int c = tid; c < C; c += nt) {
-        const unsigned long long v = cand[c];
-        int r = 0;
-        for (int j = 0; j < C; ++j) r += cand[j] > v ? 1 : 0;
-        if (r < k) {
-            tkv[r] = __uint_as_float((unsigned)(v >> 32));
-            tki[r] = (int)(0xFFFFFFFFu - (unsigned)v);
+    if (C <= 64) {
+        for (int c = tid; c < C; c += nt) {
+            const unsigned long long v = cand[c];
+            int r = 0;
+            for (int j = 0; j < C; ++j) r += cand[j] > v ? 1 : 0;
+            if (r < k) {
+                tkv[r] = __uint_as_float((unsigned)(v >> 32));
+                tki[r] = (int)(0xFFFFFFFFu - (unsigned)v);
+            }
+        }
+        __syncthreads();
+        return lmax;
+    }
+    // Many candidates: a long run of equal probabilities (activations small
+    // enough that exp rounds them together).  Each warp extracts its own top
+    // k by k rounds of warp arg-max (no block barrier), then warp 0 merges the
+    // nw * k survivors the same way -- cost independent of the ties.
+    unsigned long long a0 = i0 < E ? k0 : 0ull, a1 = i1 < E ? k1 : 0ull;
+    for (int r = 0; r < k; ++r) {
+        const unsigned long long b = a0 > a1 ? a0 : a1;
+        const unsigned bh = (unsigned)(b >> 32), bl = (unsigned)b;
+        const unsigned wh = __reduce_max_sync(0xffffffffu, bh);
+        const unsigned wl = __reduce_max_sync(0xffffffffu, bh == wh ? bl : 0u);
+        const unsigned long long m = ((unsigned long long)wh << 32) | wl;
+        if (lane == 0) cand[warp * k + r] = m;
+        if (a0 == m) a0 = 0ull;
+        if (a1 == m) a1 = 0ull;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int n = nw * k;  // <= 16 * 16 = 256: up to 8 per lane
+        unsigned long long c[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c[j] = (lane + 32 * j) < n ? cand[lane + 32 * j] : 0ull;
+        for (int r = 0; r < k; ++r) {
+            unsigned long long b = 0ull;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) b = c[j] > b ? c[j] : b;
+            const unsigned bh = (unsigned)(b >> 32), bl = (unsigned)b;
+            const unsigned wh = __reduce_max_sync(0xffffffffu, bh);
+            const unsigned wl = __reduce_max_sync(0xffffffffu, bh == wh ? bl : 0u);
+            const unsigned long long m = ((unsigned long long)wh << 32) | wl;
+            if (lane == 0) {
+                tkv[r] = __uint_as_float(wh);
+                tki[r] = (int)(0xFFFFFFFFu - wl);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (c[j] == m) c[j] = 0ull;
         }
     }
     __syncthreads();
