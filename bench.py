@@ -43,6 +43,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE decode µs/token (48 layers, batch 1); achieved HBM GB/s vs 8 TB/s peak"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per layer of the single-launch stack
+# kernel, from one ncu capture of a 2-layer stack of the same shape; traffic grows with the layer
+# count, so a launch of n layers moves n times this.
+STACK_TRAFFIC_PER_LAYER_B = 45_307_904 // 2
 
 
 def peaks() -> tuple[float, str]:
@@ -274,11 +278,13 @@ def main() -> None:
         if single:
             # one persistent launch per step: its bytes are the whole stack's
             rl_kernel, rl_bytes, rl_us = "stack_kernel", bytes_tok, ms_step * 1000.0
+            rl_traffic = STACK_TRAFFIC_PER_LAYER_B * cfg.n_layers
         else:
             rl_kernel = "gateup_swiglu"
             rl_bytes = (cfg.top_k + (1 if shard.has_shared() else 0)) * 2 * shard.dims(cfg).inter_local \
                 * cfg.gate_up_row_bytes
             rl_us = stage["gateup_us"]
+            rl_traffic = None
         rl_gbs = rl_bytes / (rl_us * 1e-6) / 1e9
         line = {
             "metric": METRIC, "value": round(us_tok, 3), "unit": "us/token", "n_gpus": world,
@@ -299,7 +305,7 @@ def main() -> None:
             "gpu_launches": (1 if single else 3 * cfg.n_layers) * args.steps,
             "roofline": {
                 "kernel": rl_kernel, "bound": "hbm", "achieved": round(rl_gbs, 1), "peak": hbm,
-                "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(rl_gbs / hbm, 4), "traffic": None,
+                "peak_kind": hbm_kind, "unit": "GB/s", "frac": round(rl_gbs / hbm, 4), "traffic": rl_traffic,
                 "bytes_per_launch": rl_bytes, "avg_launch_us": round(rl_us, 3),
                 "frac_of_nominal_8tbs": round(rl_gbs / NOMINAL_HBM_GBS, 4),
             },
