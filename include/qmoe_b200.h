@@ -205,6 +205,39 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
 int qmoe_moe_block_noalloc(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
                            const qmoe_dims* dims, float* out, void* stream);
 
+/* ---- Chunked prefill and large verify chunks: T tokens through one layer ----
+ * Replaces TTModel._prefill_ffn_half (tt/model.py:2812-2907): moe.route
+ * (tt/moe.py:308-327), apply_experts / expert_ffn (tt/moe.py:330-368,
+ * 1057-1152) and shared_expert (tt/moe.py:983) over a chunk.  Tokens are
+ * grouped per expert on the device; each group runs as an IQ4_XS -> bf16
+ * expansion in shared memory feeding tcgen05 tensor-core tiles (fp32
+ * accumulation), SwiGLU, then the down projection scatter-added into out
+ * with the routing weights.  Unsharded dims only (expert window = all
+ * experts, whole intermediate rows); hidden and inter multiples of 512;
+ * 1 <= n_tokens <= qmoe_prefill_max_tokens() and n_tokens * top_k <= 102400.
+ * Weight tensors 16-byte aligned.  Stream-ordered, no host sync.  Routed
+ * outputs are summed with fp32 atomics, so the low bits of `out` may differ
+ * between runs. */
+int qmoe_prefill_max_tokens(void);
+size_t qmoe_prefill_workspace_bytes(const qmoe_dims* dims, int n_tokens);
+/* ids [T, top_k] int32 and weights [T, top_k] fp32 (renormalised, descending,
+ * ties to the lower id); shared_logit [T] (x . gate_vec) or NULL. */
+int qmoe_prefill_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                       const qmoe_dims* dims, int32_t* ids, float* weights, float* shared_logit,
+                       void* workspace, size_t workspace_bytes, void* stream);
+/* out [T, hidden] fp32 = sum_s weights[t,s] * expert_{ids[t,s]}(x_t)
+ *                      + sigmoid(shared_logit[t]) * shared(x_t) (when the dims
+ * carry a shared expert; shared_logit is then required).  Out-of-range ids
+ * are skipped and set QMOE_ERR_DEVICE_RANGE in the workspace status word. */
+int qmoe_prefill_experts(const void* x, int x_dtype, int n_tokens, const int32_t* ids,
+                         const float* weights, const float* shared_logit,
+                         const qmoe_layer_weights* w, const qmoe_dims* dims, float* out,
+                         void* workspace, size_t workspace_bytes, void* stream);
+/* qmoe_prefill_route followed by qmoe_prefill_experts. */
+int qmoe_prefill(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                 const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,134 @@
+"""Chunked prefill (grouped tcgen05 GEMMs) vs the CPU oracle.
+
+one layer of the config-1 shape (hidden 2048, inter 512,
+512 experts, top-10 + shared), chunks of T = 128 and 2048 tokens, x ~ N(0,1)
+bf16; plus ragged chunk sizes (a partial tile, a shared group of three
+n-tiles), fp32 input, and externally supplied routing.  Bars: routed ids
+exact (rows whose 10th/11th probabilities are well separated: the router is
+an fp32 GEMM whose summation order differs from numpy's), output max relative
+error <= 1e-2 (bf16 weights and activations into fp32 tensor-core
+accumulation).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from test_gpu_parity import TOL, device_layer
+
+pytestmark = pytest.mark.gpu
+
+
+def _x(T: int, seed: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(T, 2048, generator=g).to(torch.bfloat16)
+
+
+def _oracle(oracle, hl, x_bf16: torch.Tensor, k: int) -> dict:
+    src = oracle.ExpertSource.from_host_layer(hl)
+    return oracle.moe_forward(x_bf16.float().numpy(), src, k)
+
+
+def _rows_ok(probs: np.ndarray, k: int) -> np.ndarray:
+    p = -np.sort(-probs, axis=-1)
+    return (p[:, k - 1] - p[:, k]) > 1e-5 * p[:, k - 1]
+
+
+@pytest.fixture(scope="module")
+def c1(pkg):
+    g = load_golden("moe_c1_m1.npz")
+    hl, dl = device_layer(pkg, g)
+    return hl, dl, pkg.MoELayer(dl)
+
+
+@pytest.mark.parametrize("T", [128, 2048, 37, 300])
+def test_prefill_matches_oracle(pkg, oracle, c1, T):
+    hl, dl, layer = c1
+    x = _x(T, seed=100 + T)
+    ref = _oracle(oracle, hl, x, hl.cfg.top_k)
+    ids, w, sl = layer.prefill_route(x.cuda())
+    ok = _rows_ok(ref["probs"], hl.cfg.top_k)
+    assert ok.mean() > 0.9
+    got_ids = ids.cpu().numpy()
+    assert np.array_equal(got_ids[ok], ref["ids"][ok]), "routed ids differ on well-separated rows"
+    np.testing.assert_allclose(w.cpu().numpy()[ok], ref["weights"][ok], rtol=1e-4, atol=1e-6)
+    out = layer.prefill(x.cuda())
+    torch.cuda.synchronize()
+    pkg.moe.prefill_workspace_for(layer.dims, T, out.device).raise_if_error("prefill")
+    err = oracle.max_rel_err(out.cpu().numpy(), ref["out"])
+    assert err <= TOL, f"T={T}: max rel err {err:.3e}"
+    # per token too: every row within the bar relative to its own scale
+    got = out.cpu().numpy().astype(np.float64)
+    r = ref["out"].astype(np.float64)
+    row_err = np.max(np.abs(got - r), axis=1) / np.max(np.abs(r), axis=1)
+    assert float(np.max(row_err)) <= 5 * TOL
+
+
+def test_prefill_fp32_input_and_repeat(pkg, oracle, c1):
+    hl, dl, layer = c1
+    x = _x(64, seed=5)
+    ref = _oracle(oracle, hl, x, hl.cfg.top_k)
+    out32 = layer.prefill(x.float().cuda())
+    out16 = layer.prefill(x.cuda())
+    torch.cuda.synchronize()
+    assert oracle.max_rel_err(out32.cpu().numpy(), ref["out"]) <= TOL
+    # fp32 input is rounded to bf16 first, so both are the same computation
+    assert oracle.max_rel_err(out32.cpu().numpy(), out16.cpu().numpy()) <= 1e-5
+
+
+def test_prefill_experts_given_routing(pkg, oracle, c1):
+    """apply_experts with the oracle's routing (tt/moe.py:330-368) + shared expert; an
+    out-of-range id is skipped and reported."""
+    hl, dl, layer = c1
+    T, k = 96, hl.cfg.top_k
+    x = _x(T, seed=9)
+    ref = _oracle(oracle, hl, x, k)
+    ids = torch.from_numpy(ref["ids"].astype(np.int32)).cuda()
+    w = torch.from_numpy(ref["weights"]).cuda()
+    sl = torch.from_numpy((x.float().numpy() @ hl.gate_vec.reshape(-1, 1)).reshape(-1).astype(np.float32)).cuda()
+    out = layer.prefill_experts(x.cuda(), ids, w, sl)
+    torch.cuda.synchronize()
+    pws = pkg.moe.prefill_workspace_for(layer.dims, T, out.device)
+    pws.raise_if_error("prefill_experts")
+    assert oracle.max_rel_err(out.cpu().numpy(), ref["out"]) <= TOL
+
+    bad = ids.clone()
+    bad[3, 0] = hl.cfg.n_experts + 5
+    w_bad = w.clone()
+    out_bad = layer.prefill_experts(x.cuda(), bad, w_bad, sl)
+    torch.cuda.synchronize()
+    assert pws.read_status() == pkg._lib.QMOE_ERR_DEVICE_RANGE
+    # the other tokens are untouched by the skipped pair
+    keep = np.ones(T, dtype=bool)
+    keep[3] = False
+    assert oracle.max_rel_err(out_bad.cpu().numpy()[keep], ref["out"][keep]) <= TOL
+
+
+def test_prefill_operator_api(pkg, oracle, c1):
+    """route / apply_experts on raw tensors take the chunked path above 16 tokens."""
+    hl, dl, layer = c1
+    T, k = 48, hl.cfg.top_k
+    x = _x(T, seed=21).cuda()
+    dense_w, keep = pkg.route(x, dl.router, k)
+    ref = _oracle(oracle, hl, x.cpu(), k)
+    ok = _rows_ok(ref["probs"], k)
+    ids = torch.topk(keep, k, dim=-1).indices.sort(dim=-1).values.cpu().numpy()
+    assert np.array_equal(ids[ok], np.sort(ref["ids"], axis=-1)[ok])
+    routed = pkg.apply_experts(x, dense_w, keep, dl.gate_up, None, dl.down, hl.cfg.n_experts,
+                               hl.cfg.hidden, hl.cfg.inter)
+    torch.cuda.synchronize()
+    assert oracle.max_rel_err(routed.cpu().numpy(), ref["routed"]) <= TOL
+
+
+def test_prefill_matches_decode_path(pkg, c1):
+    """At 16 tokens the prefill path and the decode kernels compute the same block."""
+    hl, dl, layer = c1
+    x = _x(16, seed=33).cuda()
+    a = layer.prefill(x)
+    b = layer(x)
+    torch.cuda.synchronize()
+    d = (a - b).abs().max().item() / b.abs().max().item()
+    assert d <= TOL

@@ -10,7 +10,16 @@ raises: there is no fallback.
 from . import _lib
 from ._lib import QMoEError
 from .config import C1, C2, MoEConfig, Shard
-from .moe import MoELayer, Workspace, apply_experts, moe_block, route, route_topk, shared_expert
+from .moe import (
+    MoELayer,
+    PrefillWorkspace,
+    Workspace,
+    apply_experts,
+    moe_block,
+    route,
+    route_topk,
+    shared_expert,
+)
 from .stack import MoEStack
 from .weights import (
     DeviceLayer,
@@ -22,7 +31,7 @@ from .weights import (
 )
 
 __all__ = [
-    "C1", "C2", "MoEConfig", "Shard", "QMoEError", "MoELayer", "MoEStack", "Workspace",
+    "C1", "C2", "MoEConfig", "Shard", "QMoEError", "MoELayer", "MoEStack", "Workspace", "PrefillWorkspace",
     "DeviceLayer", "HostLayer", "apply_experts", "moe_block", "route", "route_topk", "shared_expert",
     "synth_device_layer", "synth_host_layer", "synth_x", "upload_host_layer",
 ]

@@ -103,6 +103,13 @@ _SIGS = {
     "qmoe_read_stack_trace": (c_int, [_P, POINTER(Dims), c_int, c_int, _P, _P]),
     "qmoe_stack_single_launch": (c_int, [POINTER(Dims), c_int, c_int]),
     "qmoe_moe_block_noalloc": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P]),
+    "qmoe_prefill_max_tokens": (c_int, []),
+    "qmoe_prefill_workspace_bytes": (c_size_t, [POINTER(Dims), c_int]),
+    "qmoe_prefill_route": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P, _P, _P,
+                                   c_size_t, _P]),
+    "qmoe_prefill_experts": (c_int, [_P, c_int, c_int, _P, _P, _P, POINTER(LayerWeights), POINTER(Dims), _P,
+                                     _P, c_size_t, _P]),
+    "qmoe_prefill": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P, c_size_t, _P]),
 }
 
 for _name, (_res, _args) in _SIGS.items():

@@ -462,4 +462,95 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
     return QMOE_OK;
 }
 
+// ---- prefill / large verify chunks ------------------------------------------
+
+static int check_prefill(const qmoe_dims* dims, int n_tokens) {
+    QMOE_TRY(check_dims(dims));
+    if (!prefill_supported(*dims)) return QMOE_ERR_UNSUPPORTED;
+    if (n_tokens < 1 || n_tokens > prefill_max_tokens()) return QMOE_ERR_UNSUPPORTED;
+    // the grouping pass holds every routed id of the chunk in shared memory as int16
+    if ((size_t)n_tokens * dims->top_k * 2 > 200 * 1024) return QMOE_ERR_UNSUPPORTED;
+    return QMOE_OK;
+}
+
+static int check_prefill_experts_weights(const qmoe_layer_weights* w, const qmoe_dims* d) {
+    if (!w || !w->gate_up || !w->down) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(w->gate_up, 16) || !aligned(w->down, 16)) return QMOE_ERR_ALIGNMENT;
+    if (d->sh_inter_local > 0) {
+        if (!w->sh_gate_up || !w->sh_down) return QMOE_ERR_INVALID_ARG;
+        if (!aligned(w->sh_gate_up, 16) || !aligned(w->sh_down, 16)) return QMOE_ERR_ALIGNMENT;
+    }
+    return QMOE_OK;
+}
+
+static int get_prefill_ws(void* workspace, size_t bytes, const qmoe_dims* d, int T) {
+    if (!workspace) return QMOE_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return QMOE_ERR_ALIGNMENT;
+    if (bytes < prefill_workspace_bytes(*d, T)) return QMOE_ERR_WORKSPACE;
+    return QMOE_OK;
+}
+
+int qmoe_prefill_max_tokens(void) { return prefill_max_tokens(); }
+
+size_t qmoe_prefill_workspace_bytes(const qmoe_dims* dims, int n_tokens) {
+    if (check_dims(dims) != QMOE_OK || n_tokens < 1 || n_tokens > prefill_max_tokens()) return 0;
+    return prefill_workspace_bytes(*dims, n_tokens);
+}
+
+int qmoe_prefill_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                       const qmoe_dims* dims, int32_t* ids, float* weights, float* shared_logit,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+    // Routing alone needs only valid dims and a chunk size the workspace covers.
+    QMOE_TRY(check_dims(dims));
+    if (n_tokens < 1 || n_tokens > prefill_max_tokens()) return QMOE_ERR_UNSUPPORTED;
+    QMOE_TRY(check_act(x, x_dtype));
+    QMOE_TRY(check_weights_route(w));
+    if (!ids || !weights) return QMOE_ERR_INVALID_ARG;
+    QMOE_TRY(get_prefill_ws(workspace, workspace_bytes, dims, n_tokens));
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned char* ws = (unsigned char*)workspace;
+    const bool x_ok = x_dtype == QMOE_ACT_BF16 && aligned(x, 16);
+    const __nv_bfloat16* xb = prefill_act_bf16(x, x_dtype == QMOE_ACT_F32, x_ok, n_tokens, *dims, ws, s);
+    return cuda_status(launch_prefill_route(xb, n_tokens, *w, *dims, ws, ids, weights, shared_logit, s));
+}
+
+int qmoe_prefill_experts(const void* x, int x_dtype, int n_tokens, const int32_t* ids, const float* weights,
+                         const float* shared_logit, const qmoe_layer_weights* w, const qmoe_dims* dims, float* out,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+    QMOE_TRY(check_prefill(dims, n_tokens));
+    QMOE_TRY(check_act(x, x_dtype));
+    QMOE_TRY(check_prefill_experts_weights(w, dims));
+    if (!ids || !weights || !out) return QMOE_ERR_INVALID_ARG;
+    if (dims->sh_inter_local > 0 && !shared_logit) return QMOE_ERR_INVALID_ARG;
+    QMOE_TRY(get_prefill_ws(workspace, workspace_bytes, dims, n_tokens));
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned char* ws = (unsigned char*)workspace;
+    const bool x_ok = x_dtype == QMOE_ACT_BF16 && aligned(x, 16);
+    // out may alias an fp32 x: x is read (converted to bf16) before out is cleared.
+    const __nv_bfloat16* xb = prefill_act_bf16(x, x_dtype == QMOE_ACT_F32, x_ok, n_tokens, *dims, ws, s);
+    return cuda_status(launch_prefill_experts(xb, n_tokens, ids, weights, shared_logit, *w, *dims, out, ws, s));
+}
+
+int qmoe_prefill(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w, const qmoe_dims* dims,
+                 float* out, void* workspace, size_t workspace_bytes, void* stream) {
+    QMOE_TRY(check_prefill(dims, n_tokens));
+    QMOE_TRY(check_act(x, x_dtype));
+    QMOE_TRY(check_weights_route(w));
+    QMOE_TRY(check_prefill_experts_weights(w, dims));
+    if (!out) return QMOE_ERR_INVALID_ARG;
+    QMOE_TRY(get_prefill_ws(workspace, workspace_bytes, dims, n_tokens));
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned char* ws = (unsigned char*)workspace;
+    const bool x_ok = x_dtype == QMOE_ACT_BF16 && aligned(x, 16);
+    const __nv_bfloat16* xb = prefill_act_bf16(x, x_dtype == QMOE_ACT_F32, x_ok, n_tokens, *dims, ws, s);
+    int32_t* ids;
+    float* wts;
+    float* slog;
+    prefill_route_buffers(*dims, n_tokens, ws, &ids, &wts, &slog);
+    QMOE_TRY(cuda_status(launch_prefill_route(xb, n_tokens, *w, *dims, ws, ids, wts, slog, s)));
+    // An fp32 x that aliases out is safe: fp32 input is always read through its bf16 copy, made
+    // before out is cleared.
+    return cuda_status(launch_prefill_experts(xb, n_tokens, ids, wts, slog, *w, *dims, out, ws, s));
+}
+
 }  // extern "C"

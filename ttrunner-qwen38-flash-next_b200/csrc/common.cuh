@@ -94,6 +94,25 @@ cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* lo
                                 unsigned long long* trace, int* status, const qmoe_layer_weights* layers, int n_layers,
                                 const qmoe_dims& d, cudaStream_t stream);
 
+// Prefill / large verify chunks (prefill.cu).
+int prefill_max_tokens();
+bool prefill_supported(const qmoe_dims& d);
+struct PfLayout;
+size_t prefill_workspace_bytes(const qmoe_dims& d, int T);
+// The activations as bf16 [T][hidden], 16-byte aligned: x itself when it already is, else a copy
+// in the workspace.
+const __nv_bfloat16* prefill_act_bf16(const void* x, int x_f32, bool x_ok, int T, const qmoe_dims& d,
+                                      unsigned char* ws, cudaStream_t s);
+cudaError_t launch_prefill_route(const __nv_bfloat16* xb, int T, const qmoe_layer_weights& w, const qmoe_dims& d,
+                                 unsigned char* ws, int32_t* ids, float* weights, float* shared_logit,
+                                 cudaStream_t s);
+cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t* ids, const float* weights,
+                                   const float* shared_logit, const qmoe_layer_weights& w, const qmoe_dims& d,
+                                   float* out, unsigned char* ws, cudaStream_t s);
+// Device pointers to the prefill workspace's routing table (ids, weights, shared logit).
+void prefill_route_buffers(const qmoe_dims& d, int T, unsigned char* ws, int32_t** ids, float** weights,
+                           float** shared_logit);
+
 }  // namespace qmoe
 
 #if defined(__CUDACC__)

@@ -231,6 +231,28 @@ __device__ __forceinline__ void qmoe_lut8(uint32_t w, uint32_t& lo, uint32_t& hi
     hi = (r0 & ~m) | (r1 & m);
 }
 
+// The codebook shifted by +128 (entries 1..241, all unsigned bytes), packed
+// the same way: the prefill dequant places these bytes under an fp32
+// exponent to turn them into floats.
+#define QMOE_KVB_W0 0x3F2D1801u
+#define QMOE_KVB_W1 0x766A5D4Fu
+#define QMOE_KVB_W2 0xA6998D81u
+#define QMOE_KVB_W3 0xF1D9C5B5u
+
+// qmoe_lut8 with the +128-shifted codebook.
+__device__ __forceinline__ void qmoe_lut8_biased(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t a = w << 4;
+    const uint32_t wm = w & 0x77777777u;
+    uint32_t r0 = qmoe_prmt(QMOE_KVB_W0, QMOE_KVB_W1, w);
+    uint32_t r1 = qmoe_prmt(QMOE_KVB_W2, QMOE_KVB_W3, wm);
+    uint32_t m = qmoe_prmt(a, w, 0xD9C8u);
+    lo = (r0 & ~m) | (r1 & m);
+    r0 = qmoe_prmt(QMOE_KVB_W0, QMOE_KVB_W1, w >> 16);
+    r1 = qmoe_prmt(QMOE_KVB_W2, QMOE_KVB_W3, wm >> 16);
+    m = qmoe_prmt(a, w, 0xFBEAu);
+    hi = (r0 & ~m) | (r1 & m);
+}
+
 // Integer dot product of one 32-value sub-block with an activation block in
 // int16 pair form: xp[p] = x[p] | x[16+p] << 16 for p < 16 (the order in
 // which a qs byte holds its two codes).  q0..q3 are the sub-block's 16 qs

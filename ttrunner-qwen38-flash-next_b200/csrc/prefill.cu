@@ -1,0 +1,797 @@
+// Chunked prefill / large verify chunks: T tokens through one MoE layer.
+//
+// Reference: TTModel._prefill_ffn_half (tt/model.py:2812-2907), which calls
+// moe.route (tt/moe.py:308-327) and apply_experts / expert_ffn (tt/moe.py:
+// 330-368, 1057-1152); per token the arithmetic is reference/model.py:387-417
+// (router softmax top-k renormalised, SwiGLU experts, sigmoid-gated shared
+// expert).  Only here is the expert work a dense contraction: every selected
+// expert sees a group of tokens, so its IQ4_XS rows are expanded to bf16 once
+// per group in shared memory and fed to the 5th-generation tensor cores
+// (tcgen05.mma, accumulators in tensor memory).
+//
+// One stream, no host round trip:
+//   1. x -> bf16 copy, when x is fp32 or not 16-byte aligned;
+//   2. router logits [T][E + 1] in fp32 (row E: the shared-expert gate vector);
+//   3. top-k per token (warp per token, the decode path's selection rule);
+//   4. grouping: per-expert counts, offsets, n-tiles of <= 128 tokens, and slot
+//      rows ordered by token (deterministic);
+//   5. gate|up grouped GEMM + SwiGLU epilogue -> h [rows][I] bf16;
+//   6. out = 0, then the down grouped GEMM with a gate-weighted scatter-add.
+// The shared expert is group E: every token, weight sigmoid(x . gate_vec).
+#include <math.h>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "topk.cuh"
+
+namespace qmoe {
+namespace {
+
+constexpr int kPfMaxTokens = 8192;
+constexpr unsigned long long kPfTimeoutNs = 1000ull * 1000 * 1000;
+
+// ---- grouped GEMM geometry --------------------------------------------------
+constexpr int kGM = 128;            // MMA M: weight rows per tile
+constexpr int kGNMax = 128;         // tokens per n-tile (MMA N, padded to 16)
+constexpr int kGSlotK = 64;         // K per operand slot: one 128-byte swizzle row of bf16
+constexpr int kGSlots = 4;          // operand ring depth
+constexpr int kGStageK = 512;       // K per IQ4_XS stage: two super-blocks of every row
+constexpr int kGStageRowB = 2 * QMOE_SB_BYTES;  // 272 bytes of one row per stage
+constexpr int kGStages = 2;
+constexpr int kGSlotBytes = kGM * kGSlotK * 2;  // 16 KB (A and B slots alike: N <= 128)
+constexpr int kGStageBytes = kGM * kGStageRowB;  // 34,816
+constexpr int kGTmemCols = 256;     // two accumulator buffers of 128 columns
+// warp roles
+constexpr int kWLoad = 0, kWGather = 1, kWMma = 2, kWDq0 = 3, kNDq = 8, kWEp0 = 11, kNEp = 4;
+constexpr int kGWarps = kWEp0 + kNEp;  // 15
+constexpr int kGThreads = kGWarps * 32;
+
+// shared-memory carve-up from a 1024-aligned base
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kGSlots * kGSlotBytes;
+constexpr int kOffStage = kOffB + kGSlots * kGSlotBytes;
+constexpr int kOffBars = kOffStage + kGStages * kGStageBytes;
+constexpr int kNBars = 2 * kGStages + 2 * kGSlots + 2 * 2 + 1;
+constexpr int kOffMisc = kOffBars + kNBars * 8;
+constexpr int kGSmemBytes = kOffMisc + 64 + 1024;  // + slack to align the base
+static_assert(kOffStage % 1024 == 0 && kOffB % 1024 == 0, "operand tiles must be 1024-aligned");
+
+struct GemmArgs {
+    int mode;  // 0: gate|up + SwiGLU -> h; 1: down + weighted scatter-add -> out
+    int D, I, E, T;
+    const uint8_t* gate_up;
+    const uint8_t* down;
+    const uint8_t* sh_gate_up;
+    const uint8_t* sh_down;
+    size_t gu_expert_bytes, dn_expert_bytes;
+    const __nv_bfloat16* x;  // [T][D], 16-byte aligned
+    __nv_bfloat16* h;        // [rows][I]
+    const int* slot_tok;     // [rows]
+    const float* slot_w;     // [rows]
+    const int4* ntiles;      // {group, first token of the tile in the group, count, slot row}
+    const int* meta;         // meta[0]: number of n-tiles
+    float* out;              // [T][D]
+    int* status;
+};
+
+struct PfSmem {
+    unsigned char* base;
+    uint64_t* bars;
+    __device__ uint8_t* a_slot(int s) const { return base + kOffA + s * kGSlotBytes; }
+    __device__ uint8_t* b_slot(int s) const { return base + kOffB + s * kGSlotBytes; }
+    __device__ uint8_t* stage(int s) const { return base + kOffStage + s * kGStageBytes; }
+    __device__ uint64_t* iq_full(int s) const { return bars + s; }
+    __device__ uint64_t* iq_empty(int s) const { return bars + kGStages + s; }
+    __device__ uint64_t* s_full(int s) const { return bars + 2 * kGStages + s; }
+    __device__ uint64_t* s_empty(int s) const { return bars + 2 * kGStages + kGSlots + s; }
+    __device__ uint64_t* acc_full(int b) const { return bars + 2 * kGStages + 2 * kGSlots + b; }
+    __device__ uint64_t* acc_empty(int b) const { return bars + 2 * kGStages + 2 * kGSlots + 2 + b; }
+    __device__ uint64_t* fin() const { return bars + 2 * kGStages + 2 * kGSlots + 4; }
+    __device__ uint32_t* tmem_holder() const { return reinterpret_cast<uint32_t*>(base + kOffMisc); }
+    __device__ volatile int* abort_flag() const { return reinterpret_cast<volatile int*>(base + kOffMisc + 16); }
+};
+
+// Bounded wait on an mbarrier phase; false (and the CTA's abort flag set) on
+// timeout, or when another role already gave up (unless `honour_abort` is
+// false: the drains before exit wait for in-flight work regardless).
+__device__ bool pf_wait(uint64_t* bar, uint32_t par, volatile int* abort_flag, int* status,
+                        bool honour_abort = true) {
+    if (ptx::mbar_test(bar, par)) return true;
+    const unsigned long long t0 = ptx::now_ns();
+    for (unsigned it = 0;; ++it) {
+        if (ptx::mbar_test(bar, par)) return true;
+        if ((it & 63u) == 63u) {
+            if (honour_abort && *abort_flag) return false;
+            if (ptx::now_ns() - t0 > kPfTimeoutNs) {
+                *abort_flag = 1;
+                record_status(status, QMOE_ERR_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+// The same, by every lane of a warp, agreeing on the outcome.
+__device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, uint32_t par, volatile int* abort_flag, int* status) {
+    const bool ok = pf_wait(bar, par, abort_flag, status);
+    return __all_sync(0xffffffffu, ok);
+}
+
+struct TileInfo {
+    int g, cnt, row0, mt, N;
+    const uint8_t* w;  // this group's weight tensor for the mode
+};
+
+__device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, int t, int MT) {
+    TileInfo ti;
+    const int4 nd = __ldg(a.ntiles + t / MT);
+    ti.g = nd.x;
+    ti.cnt = nd.z;
+    ti.row0 = nd.w;
+    ti.mt = t % MT;
+    ti.N = (ti.cnt + 15) & ~15;
+    if (a.mode == 0)
+        ti.w = ti.g < a.E ? a.gate_up + (size_t)ti.g * a.gu_expert_bytes : a.sh_gate_up;
+    else
+        ti.w = ti.g < a.E ? a.down + (size_t)ti.g * a.dn_expert_bytes : a.sh_down;
+    return ti;
+}
+
+// One 32-value sub-block of IQ4_XS (header words h0/h1, qs words q0..q3) to
+// 32 bf16 in natural order, as four 16-byte chunks.  Each code's codebook
+// entry + 128 is placed under the exponent of 2^23 (an exact float 2^23 + b),
+// the bias removed exactly, the result scaled by d*(ls-32) and rounded to bf16.
+__device__ __forceinline__ void dequant_subblock_bf16(uint32_t h0, uint32_t h1, int ib, uint32_t q0, uint32_t q1,
+                                                      uint32_t q2, uint32_t q3, uint4 (&c)[4]) {
+    const float d = __half2float(__ushort_as_half((unsigned short)(h0 & 0xFFFFu)));
+    const float dl = d * (float)(qmoe_iq4xs_ls(h0, h1, ib) - 32);
+    const uint32_t q[4] = {q0, q1, q2, q3};
+    uint32_t pk[4][4];  // [word][lo-pair, hi-pair, lo-pair(high nibbles), hi-pair(high nibbles)]
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        uint32_t lo, hi;
+        qmoe_lut8_biased(q[w], lo, hi);
+        // lo bytes: values 4w, 16+4w, 4w+1, 16+4w+1; hi: 4w+2, 18+4w, 4w+3, 19+4w
+        float v[8];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            v[b] = (__uint_as_float(qmoe_prmt(lo, 0x4B000000u, 0x7540u + (uint32_t)b)) - 8388736.0f) * dl;
+            v[4 + b] = (__uint_as_float(qmoe_prmt(hi, 0x4B000000u, 0x7540u + (uint32_t)b)) - 8388736.0f) * dl;
+        }
+        const __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[2]);  // values 4w, 4w+1
+        const __nv_bfloat162 p1 = __floats2bfloat162_rn(v[4], v[6]);  // 4w+2, 4w+3
+        const __nv_bfloat162 p2 = __floats2bfloat162_rn(v[1], v[3]);  // 16+4w, 16+4w+1
+        const __nv_bfloat162 p3 = __floats2bfloat162_rn(v[5], v[7]);  // 16+4w+2, 16+4w+3
+        pk[w][0] = *reinterpret_cast<const uint32_t*>(&p0);
+        pk[w][1] = *reinterpret_cast<const uint32_t*>(&p1);
+        pk[w][2] = *reinterpret_cast<const uint32_t*>(&p2);
+        pk[w][3] = *reinterpret_cast<const uint32_t*>(&p3);
+    }
+    c[0] = make_uint4(pk[0][0], pk[0][1], pk[1][0], pk[1][1]);  // values 0..7
+    c[1] = make_uint4(pk[2][0], pk[2][1], pk[3][0], pk[3][1]);  // 8..15
+    c[2] = make_uint4(pk[0][2], pk[0][3], pk[1][2], pk[1][3]);  // 16..23
+    c[3] = make_uint4(pk[2][2], pk[2][3], pk[3][2], pk[3][3]);  // 24..31
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled
+// K-major tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Grouped GEMM, persistent: one CTA per SM walks tiles t = blockIdx.x,
+// + gridDim.x, ...; tile t = (n-tile t / MT, m-tile t % MT).  mode 0: M rows
+// interleave the gate and up rows of 64 intermediate rows (even = gate,
+// odd = up), K = D; mode 1: 128 down rows, K = I.
+__global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid_constant__ GemmArgs a) {
+    extern __shared__ unsigned char smem_raw[];
+    PfSmem S;
+    S.base = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    S.bars = reinterpret_cast<uint64_t*>(S.base + kOffBars);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    volatile int* abort_flag = S.abort_flag();
+
+    if (tid == 0) {
+        for (int s = 0; s < kGStages; ++s) {
+            ptx::mbar_init(S.iq_full(s), 1);
+            ptx::mbar_init(S.iq_empty(s), kNDq);
+        }
+        for (int s = 0; s < kGSlots; ++s) {
+            ptx::mbar_init(S.s_full(s), kNDq + 1);
+            ptx::mbar_init(S.s_empty(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            ptx::mbar_init(S.acc_full(b), 1);
+            ptx::mbar_init(S.acc_empty(b), kNEp);
+        }
+        ptx::mbar_init(S.fin(), 1);
+        *abort_flag = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == kWMma) {
+        ptx::tmem_alloc(S.tmem_holder(), kGTmemCols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *S.tmem_holder();
+
+    const int MT = a.mode == 0 ? a.I / 64 : a.D / kGM;
+    const int K = a.mode == 0 ? a.D : a.I;
+    const int nslots = K / kGSlotK;
+    const int n_tiles = __ldg(a.meta) * MT;
+    const int RB = (K / 256) * QMOE_SB_BYTES;  // bytes of one weight row
+
+    if (warp == kWLoad) {
+        // ---- IQ4_XS stage producer: 128 rows x 272 bytes per stage --------
+        int st_it = 0;
+        int last_issue[kGStages] = {-1, -1};
+        bool ok = true;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            const TileInfo ti = tile_info(a, t, MT);
+            for (int kst = 0; kst < K / kGStageK; ++kst) {
+                const int st = st_it % kGStages;
+                if (!pf_wait_warp(S.iq_empty(st), ((st_it / kGStages) & 1) ^ 1, abort_flag, a.status)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) ptx::mbar_expect_tx(S.iq_full(st), kGStageBytes);
+                __syncwarp();
+                uint8_t* dst = S.stage(st);
+                for (int m = lane; m < kGM; m += 32) {
+                    const int wrow = a.mode == 0 ? ((m & 1) ? a.I : 0) + ti.mt * 64 + (m >> 1) : ti.mt * kGM + m;
+                    ptx::bulk_g2s(dst + m * kGStageRowB, ti.w + (size_t)wrow * RB + kst * kGStageRowB, kGStageRowB,
+                                  S.iq_full(st));
+                }
+                last_issue[st] = st_it;
+                ++st_it;
+            }
+        }
+        // Copies still in flight land before the CTA leaves (bounded).
+        if (!ok && lane == 0) {
+            for (int s = 0; s < kGStages; ++s)
+                if (last_issue[s] >= 0)
+                    (void)pf_wait(S.iq_full(s), (last_issue[s] / kGStages) & 1, abort_flag, a.status, false);
+        }
+    } else if (warp == kWGather) {
+        // ---- B operand gather: N token rows x 128 bytes per slot ----------
+        int it = 0, prev = -1;
+        bool ok = true;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            const TileInfo ti = tile_info(a, t, MT);
+            const int c = lane & 7;
+            for (int ks = 0; ks < nslots; ++ks) {
+                const int slot = it % kGSlots;
+                if (!pf_wait_warp(S.s_empty(slot), ((it / kGSlots) & 1) ^ 1, abort_flag, a.status)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* dst = S.b_slot(slot);
+                for (int n = lane >> 3; n < ti.cnt; n += 4) {
+                    const __nv_bfloat16* src;
+                    if (a.mode == 0) {
+                        const int tok = __ldg(a.slot_tok + ti.row0 + n);
+                        if ((unsigned)tok >= (unsigned)a.T) continue;  // never: slot rows hold valid tokens
+                        src = a.x + (size_t)tok * a.D + ks * kGSlotK + c * 8;
+                    } else {
+                        src = a.h + (size_t)(ti.row0 + n) * a.I + ks * kGSlotK + c * 8;
+                    }
+                    ptx::cp_async16(dst + sw128_off(n, c), src);
+                }
+                ptx::cp_async_commit();
+                if (prev >= 0) {
+                    ptx::cp_async_wait<1>();
+                    ptx::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(S.s_full(prev));
+                }
+                prev = slot;
+                ++it;
+            }
+        }
+        ptx::cp_async_wait<0>();
+        if (prev >= 0 && ok) {
+            ptx::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(S.s_full(prev));
+        }
+    } else if (warp == kWMma) {
+        // ---- MMA issue: one thread --------------------------------------
+        if (lane == 0) {
+            int it = 0, tc = 0;
+            bool ok = true, issued = false;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const TileInfo ti = tile_info(a, t, MT);
+                const uint32_t idesc = ptx::idesc_bf16(kGM, ti.N);
+                const int ab = tc & 1;
+                if (!pf_wait(S.acc_empty(ab), ((tc >> 1) & 1) ^ 1, abort_flag, a.status)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(ab * kGNMax);
+                for (int ks = 0; ks < nslots; ++ks) {
+                    const int slot = it % kGSlots;
+                    if (!pf_wait(S.s_full(slot), (it / kGSlots) & 1, abort_flag, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const uint32_t a0 = ptx::smem_addr(S.a_slot(slot)), b0 = ptx::smem_addr(S.b_slot(slot));
+#pragma unroll
+                    for (int k = 0; k < kGSlotK / 16; ++k)
+                        ptx::mma_bf16(d_tmem, ptx::desc_sw128(a0 + k * 32), ptx::desc_sw128(b0 + k * 32), idesc,
+                                      (ks | k) != 0 ? 1u : 0u);
+                    ptx::mma_commit(S.s_empty(slot));
+                    issued = true;
+                    ++it;
+                }
+                if (!ok) break;
+                ptx::mma_commit(S.acc_full(ab));
+                ++tc;
+            }
+            // Every MMA issued completes before the tensor memory is released.
+            if (issued) {
+                ptx::mma_commit(S.fin());
+                (void)pf_wait(S.fin(), 0, abort_flag, a.status, false);
+            }
+        }
+        __syncwarp();
+    } else if (warp < kWEp0) {
+        // ---- dequant: IQ4_XS stage -> bf16 A slot -----------------------
+        const int d = (warp - kWDq0) * 32 + lane;  // 0..255
+        const int m = d & (kGM - 1), sub = d >> 7;
+        int it = 0, st_it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            for (int ks = 0; ks < nslots; ++ks) {
+                const int st = st_it % kGStages;
+                if ((ks & 7) == 0 &&
+                    !pf_wait_warp(S.iq_full(st), (st_it / kGStages) & 1, abort_flag, a.status)) {
+                    ok = false;
+                    break;
+                }
+                const int slot = it % kGSlots;
+                if (!pf_wait_warp(S.s_empty(slot), ((it / kGSlots) & 1) ^ 1, abort_flag, a.status)) {
+                    ok = false;
+                    break;
+                }
+                const int sbk = (ks & 7) * 2 + sub;  // sub-block of the row within the stage (0..15)
+                const uint8_t* blk = S.stage(st) + m * kGStageRowB + (sbk >> 3) * QMOE_SB_BYTES;
+                const int ib = sbk & 7;
+                const uint2 hd = *reinterpret_cast<const uint2*>(blk);
+                const uint2 qa = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
+                const uint2 qb = *reinterpret_cast<const uint2*>(blk + 16 + 16 * ib);
+                uint4 cv[4];
+                dequant_subblock_bf16(hd.x, hd.y, ib, qa.x, qa.y, qb.x, qb.y, cv);
+                uint8_t* dst = S.a_slot(slot);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + sw128_off(m, sub * 4 + j)) = cv[j];
+                ptx::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(S.s_full(slot));
+                ++it;
+                if ((ks & 7) == 7 || ks == nslots - 1) {
+                    if (lane == 0) ptx::mbar_arrive(S.iq_empty(st));
+                    ++st_it;
+                }
+            }
+        }
+    } else {
+        // ---- epilogue: TMEM -> registers -> h (mode 0) or out (mode 1) ---
+        const int q = warp & 3;          // TMEM lane quarter this warp may read
+        const int m = q * 32 + lane;     // M row of this thread
+        int tc = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+            const TileInfo ti = tile_info(a, t, MT);
+            const int ab = tc & 1;
+            if (!pf_wait_warp(S.acc_full(ab), (tc >> 1) & 1, abort_flag, a.status)) break;
+            ptx::tc_fence_after();
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * kGNMax);
+            for (int c0 = 0; c0 < ti.N; c0 += 16) {
+                float v[16];
+                ptx::tmem_ld16(tbase + (uint32_t)c0, v);
+                if (a.mode == 0) {
+                    const int r = ti.mt * 64 + (m >> 1);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
+                        const int n = c0 + j;
+                        if (!(m & 1) && n < ti.cnt)
+                            a.h[(size_t)(ti.row0 + n) * a.I + r] = __float2bfloat16_rn(silu(v[j]) * other);
+                    }
+                } else {
+                    const int row = ti.mt * kGM + m;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = c0 + j;
+                        if (n < ti.cnt) {
+                            const int tok = __ldg(a.slot_tok + ti.row0 + n);
+                            const float w = __ldg(a.slot_w + ti.row0 + n);
+                            if ((unsigned)tok < (unsigned)a.T) atomicAdd(a.out + (size_t)tok * a.D + row, w * v[j]);
+                        }
+                    }
+                }
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(S.acc_empty(ab));
+            ++tc;
+        }
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == kWMma) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem_base, kGTmemCols);
+    }
+}
+
+// ---- router, top-k, grouping -------------------------------------------------
+
+// bf16 copy of the activations (fp32 input is rounded to bf16, the activation
+// dtype between layers).
+__global__ void pf_convert_kernel(const void* x, int x_f32, size_t n, __nv_bfloat16* xb) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        xb[i] = __float2bfloat16_rn(load_act(x, x_f32, i));
+}
+
+// logits[t][e] = x_t . R_e in fp32 for e < E and the gate vector at e = E.
+// Tile: 64 tokens x 64 router rows, K step 32, 4 x 4 outputs per thread.
+__global__ void __launch_bounds__(256) pf_router_kernel(const __nv_bfloat16* __restrict__ xb, int T, int D,
+                                                        const float* __restrict__ router,
+                                                        const float* __restrict__ gate_vec, int E,
+                                                        float* __restrict__ logits) {
+    __shared__ float xs[32][64 + 4];
+    __shared__ float rs[32][64 + 4];
+    const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64, tid = threadIdx.x;
+    const int tr = tid >> 4, tcol = tid & 15;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < D; k0 += 32) {
+        for (int i = tid; i < 64 * 32; i += 256) {
+            const int r = i >> 5, kk = i & 31;
+            const int t = t0 + r, e = e0 + r;
+            xs[kk][r] = t < T ? __bfloat162float(xb[(size_t)t * D + k0 + kk]) : 0.0f;
+            float w = 0.0f;
+            if (e < E) w = __ldg(router + (size_t)e * D + k0 + kk);
+            else if (e == E && gate_vec) w = __ldg(gate_vec + k0 + kk);
+            rs[kk][r] = w;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < 32; ++kk) {
+            float xv[4], rv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                xv[i] = xs[kk][tr * 4 + i];
+                rv[i] = rs[kk][tcol * 4 + i];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i], rv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + tr * 4 + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + tcol * 4 + j;
+            if (e <= E) logits[(size_t)t * (E + 1) + e] = acc[i][j];
+        }
+    }
+}
+
+constexpr int kTopkWarps = 8;
+
+// Top-k per token, warp per token; weights renormalised over the k; the
+// shared-expert logit is the gate-vector row (0 without a gate vector).
+__global__ void __launch_bounds__(kTopkWarps * 32) pf_topk_kernel(const float* __restrict__ logits, int T, int E,
+                                                                  int k, int has_gate, int32_t* ids, float* weights,
+                                                                  float* shared_logit, int* status) {
+    __shared__ float cv[kTopkWarps][kCandCap];
+    __shared__ int ci[kTopkWarps][kCandCap];
+    __shared__ float sv[kTopkWarps][kMaxTopK];
+    __shared__ int si[kTopkWarps][kMaxTopK];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = blockIdx.x * kTopkWarps + warp;
+    if (t >= T) return;
+    const float* lg = logits + (size_t)t * (E + 1);
+    const float lmax = warp_topk(lg, E, k, cv[warp], ci[warp], sv[warp], si[warp]);
+    const float e = lane < k ? sv[warp][lane] : 0.0f;
+    const float sum = warp_sum(e);
+    if (lane < k) {
+        if (!(fabsf(lmax) <= 3.0e38f)) record_status(status, QMOE_ERR_NOT_FINITE);
+        ids[(size_t)t * k + lane] = si[warp][lane];
+        weights[(size_t)t * k + lane] = e / sum;
+    }
+    if (lane == 0 && shared_logit) shared_logit[t] = has_gate ? __ldcg(lg + E) : 0.0f;
+}
+
+// counts[g] += 1 for every in-range routed id; out-of-range ids are skipped
+// and reported.
+__global__ void pf_count_kernel(const int32_t* __restrict__ ids, int n, int E, int* counts, int* status) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int g = ids[i];
+    if (g >= 0 && g < E) atomicAdd(counts + g, 1);
+    else record_status(status, QMOE_ERR_DEVICE_RANGE);
+}
+
+// One CTA: counts[E] = shared-group size, exclusive scans of counts (slot rows)
+// and of the n-tile counts, and the n-tile table.
+constexpr int kScanThreads = 1024;
+__global__ void __launch_bounds__(kScanThreads) pf_scan_kernel(int* counts, int G, int shared_count, int* offsets,
+                                                               int4* ntiles, int* meta) {
+    __shared__ int s_rows[kScanThreads / 32], s_nt[kScanThreads / 32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // G <= 1025 groups: thread tid owns groups 2*tid and 2*tid + 1.
+    int c[2], nt[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int g = 2 * tid + j;
+        c[j] = 0;
+        if (g < G) c[j] = g == G - 1 ? shared_count : counts[g];
+        nt[j] = (c[j] + kGNMax - 1) / kGNMax;
+    }
+    if (2 * tid + 1 == G - 1 || 2 * tid == G - 1) counts[G - 1] = shared_count;
+    int r = c[0] + c[1], n = nt[0] + nt[1];
+    int ri = r, ni = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int yr = __shfl_up_sync(0xffffffffu, ri, o), yn = __shfl_up_sync(0xffffffffu, ni, o);
+        if (lane >= o) {
+            ri += yr;
+            ni += yn;
+        }
+    }
+    if (lane == 31) {
+        s_rows[warp] = ri;
+        s_nt[warp] = ni;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int vr = s_rows[lane], vn = s_nt[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int yr = __shfl_up_sync(0xffffffffu, vr, o), yn = __shfl_up_sync(0xffffffffu, vn, o);
+            if (lane >= o) {
+                vr += yr;
+                vn += yn;
+            }
+        }
+        s_rows[lane] = vr;
+        s_nt[lane] = vn;
+    }
+    __syncthreads();
+    const int wr = warp > 0 ? s_rows[warp - 1] : 0, wn = warp > 0 ? s_nt[warp - 1] : 0;
+    int row = wr + ri - r, nti = wn + ni - n;  // exclusive prefixes of this thread's first group
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int g = 2 * tid + j;
+        if (g < G) {
+            offsets[g] = row;
+            for (int q = 0; q < nt[j]; ++q) {
+                const int n0 = q * kGNMax;
+                ntiles[nti + q] = make_int4(g, n0, min(kGNMax, c[j] - n0), row + n0);
+            }
+        }
+        row += c[j];
+        nti += nt[j];
+    }
+    if (tid == kScanThreads - 1) {
+        meta[0] = nti;  // total n-tiles
+        meta[1] = row;  // total slot rows
+        offsets[G] = row;
+    }
+}
+
+// Slot rows in token order: warp per routed group scans every token's ids
+// (held in shared memory) and ranks its hits with a ballot; the shared group
+// lists every token.
+constexpr int kPlaceWarps = 16;
+__global__ void __launch_bounds__(kPlaceWarps * 32) pf_place_kernel(const int32_t* __restrict__ ids,
+                                                                    const float* __restrict__ weights,
+                                                                    const float* __restrict__ shared_logit, int T,
+                                                                    int k, int E, int has_shared,
+                                                                    const int* __restrict__ offsets, int* slot_tok,
+                                                                    float* slot_w) {
+    extern __shared__ short sid[];  // [T][k]
+    const int n = T * k;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int g = ids[i];
+        sid[i] = (short)((g >= 0 && g < E) ? g : -1);
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = blockIdx.x * kPlaceWarps + warp;
+    if (g < E) {
+        const int base = offsets[g];
+        int pos = 0;
+        // Every (token, slot) naming g is placed, so the rows match the counts even when a
+        // caller's routing repeats an expert within a token.
+        for (int t0 = 0; t0 < T; t0 += 32) {
+            const int t = t0 + lane;
+            for (int s = 0; s < k; ++s) {
+                const bool hit = t < T && sid[t * k + s] == g;
+                const unsigned b = __ballot_sync(0xffffffffu, hit);
+                if (hit) {
+                    const int r = base + pos + __popc(b & ((1u << lane) - 1u));
+                    slot_tok[r] = t;
+                    slot_w[r] = weights[(size_t)t * k + s];
+                }
+                pos += __popc(b);
+            }
+        }
+    } else if (g == E && has_shared) {
+        const int base = offsets[E];
+        for (int t = lane; t < T; t += 32) {
+            slot_tok[base + t] = t;
+            slot_w[base + t] = sigmoid(shared_logit[t]);
+        }
+    }
+}
+
+}  // namespace
+
+// ---- workspace and launches ---------------------------------------------------
+
+struct PfLayout {
+    size_t status, meta, xb, logits, ids, weights, slog, counts, offsets, ntiles, slot_tok, slot_w, h, total;
+    int max_ntiles, rows;
+};
+
+static size_t pf_align(size_t v) { return (v + 255) / 256 * 256; }
+
+PfLayout pf_layout(const qmoe_dims& d, int T) {
+    PfLayout L{};
+    const int E = d.n_experts, k = d.top_k, G = E + 1;
+    L.rows = T * (k + 1);
+    L.max_ntiles = G + L.rows / kGNMax + 1;
+    size_t o = 0;
+    L.status = 0;
+    L.meta = 64;
+    o = 256;
+    L.xb = o;
+    o = pf_align(o + (size_t)T * d.hidden * 2);
+    L.logits = o;
+    o = pf_align(o + (size_t)T * G * 4);
+    L.ids = o;
+    o = pf_align(o + (size_t)T * k * 4);
+    L.weights = o;
+    o = pf_align(o + (size_t)T * k * 4);
+    L.slog = o;
+    o = pf_align(o + (size_t)T * 4);
+    L.counts = o;
+    o = pf_align(o + (size_t)G * 4);
+    L.offsets = o;
+    o = pf_align(o + (size_t)(G + 1) * 4);
+    L.ntiles = o;
+    o = pf_align(o + (size_t)L.max_ntiles * 16);
+    L.slot_tok = o;
+    o = pf_align(o + (size_t)L.rows * 4);
+    L.slot_w = o;
+    o = pf_align(o + (size_t)L.rows * 4);
+    L.h = o;
+    o = pf_align(o + (size_t)L.rows * d.inter * 2);
+    L.total = o;
+    return L;
+}
+
+int prefill_max_tokens() { return kPfMaxTokens; }
+
+size_t prefill_workspace_bytes(const qmoe_dims& d, int T) { return pf_layout(d, T).total; }
+
+void prefill_route_buffers(const qmoe_dims& d, int T, unsigned char* ws, int32_t** ids, float** weights,
+                           float** shared_logit) {
+    const PfLayout L = pf_layout(d, T);
+    *ids = reinterpret_cast<int32_t*>(ws + L.ids);
+    *weights = reinterpret_cast<float*>(ws + L.weights);
+    *shared_logit = reinterpret_cast<float*>(ws + L.slog);
+}
+
+bool prefill_supported(const qmoe_dims& d) {
+    if (d.expert_lo != 0 || d.expert_hi != d.n_experts) return false;  // unsharded only
+    if (d.inter_local != d.inter || d.down_ib0 != 0 || d.down_nsub != 8 || d.down_nseg * 256 != d.inter)
+        return false;
+    if (d.hidden % kGStageK || d.inter % kGStageK) return false;
+    if (d.n_experts + 1 > 2 * kScanThreads) return false;
+    if (d.n_experts > 32767) return false;  // ids held as int16 while grouping
+    if (d.sh_inter_local != 0 &&
+        (d.sh_inter_local != d.inter || d.sh_down_ib0 != 0 || d.sh_down_nsub != 8 || d.sh_down_nseg * 256 != d.inter))
+        return false;
+    return true;
+}
+
+const __nv_bfloat16* prefill_act_bf16(const void* x, int x_f32, bool x_ok, int T, const qmoe_dims& d,
+                                      unsigned char* ws, cudaStream_t s) {
+    if (x_ok) return reinterpret_cast<const __nv_bfloat16*>(x);
+    const PfLayout L = pf_layout(d, T);
+    __nv_bfloat16* xc = reinterpret_cast<__nv_bfloat16*>(ws + L.xb);
+    const size_t n = (size_t)T * d.hidden;
+    const size_t blocks = (n + 255) / 256;
+    pf_convert_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(x, x_f32, n, xc);
+    return xc;
+}
+
+cudaError_t launch_prefill_route(const __nv_bfloat16* xb, int T, const qmoe_layer_weights& w, const qmoe_dims& d,
+                                 unsigned char* ws, int32_t* ids, float* weights, float* shared_logit,
+                                 cudaStream_t s) {
+    const PfLayout L = pf_layout(d, T);
+    int* status = reinterpret_cast<int*>(ws + L.status);
+    const int E = d.n_experts;
+    dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 1 + 63) / 64));
+    pf_router_kernel<<<grid, 256, 0, s>>>(xb, T, d.hidden, w.router, w.gate_vec, E,
+                                          reinterpret_cast<float*>(ws + L.logits));
+    pf_topk_kernel<<<(unsigned)((T + kTopkWarps - 1) / kTopkWarps), kTopkWarps * 32, 0, s>>>(
+        reinterpret_cast<const float*>(ws + L.logits), T, E, d.top_k, w.gate_vec ? 1 : 0, ids, weights,
+        shared_logit, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t* ids, const float* weights,
+                                   const float* shared_logit, const qmoe_layer_weights& w, const qmoe_dims& d,
+                                   float* out, unsigned char* ws, cudaStream_t s) {
+    const PfLayout L = pf_layout(d, T);
+    const int E = d.n_experts, k = d.top_k, G = E + 1;
+    const bool has_shared = d.sh_inter_local > 0;
+    int* status = reinterpret_cast<int*>(ws + L.status);
+    int* meta = reinterpret_cast<int*>(ws + L.meta);
+    int* counts = reinterpret_cast<int*>(ws + L.counts);
+    int* offsets = reinterpret_cast<int*>(ws + L.offsets);
+    int4* ntiles = reinterpret_cast<int4*>(ws + L.ntiles);
+    int* slot_tok = reinterpret_cast<int*>(ws + L.slot_tok);
+    float* slot_w = reinterpret_cast<float*>(ws + L.slot_w);
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(ws + L.h);
+
+    cudaError_t err = cudaMemsetAsync(counts, 0, (size_t)G * 4, s);
+    if (err != cudaSuccess) return err;
+    const int n = T * k;
+    pf_count_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ids, n, E, counts, status);
+    pf_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, G, has_shared ? T : 0, offsets, ntiles, meta);
+    const size_t place_smem = (size_t)n * sizeof(short);
+    err = cudaFuncSetAttribute(pf_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem);
+    if (err != cudaSuccess) return err;
+    pf_place_kernel<<<(unsigned)((G + kPlaceWarps - 1) / kPlaceWarps), kPlaceWarps * 32, place_smem, s>>>(
+        ids, weights, shared_logit, T, k, E, has_shared ? 1 : 0, offsets, slot_tok, slot_w);
+
+    GemmArgs a{};
+    a.D = d.hidden;
+    a.I = d.inter;
+    a.E = E;
+    a.T = T;
+    a.gate_up = reinterpret_cast<const uint8_t*>(w.gate_up);
+    a.down = reinterpret_cast<const uint8_t*>(w.down);
+    a.sh_gate_up = reinterpret_cast<const uint8_t*>(w.sh_gate_up);
+    a.sh_down = reinterpret_cast<const uint8_t*>(w.sh_down);
+    a.gu_expert_bytes = (size_t)2 * d.inter * (d.hidden / 256) * QMOE_SB_BYTES;
+    a.dn_expert_bytes = (size_t)d.hidden * (d.inter / 256) * QMOE_SB_BYTES;
+    a.x = xb;
+    a.h = h;
+    a.slot_tok = slot_tok;
+    a.slot_w = slot_w;
+    a.ntiles = ntiles;
+    a.meta = meta;
+    a.out = out;
+    a.status = status;
+    err = cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemBytes);
+    if (err != cudaSuccess) return err;
+    const int n_sm = device_sm_count();
+    a.mode = 0;
+    grouped_gemm_kernel<<<(unsigned)n_sm, kGThreads, kGSmemBytes, s>>>(a);
+    err = cudaMemsetAsync(out, 0, (size_t)T * d.hidden * 4, s);
+    if (err != cudaSuccess) return err;
+    a.mode = 1;
+    grouped_gemm_kernel<<<(unsigned)n_sm, kGThreads, kGSmemBytes, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace qmoe

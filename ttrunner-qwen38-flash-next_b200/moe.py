@@ -83,6 +83,33 @@ def workspace_for(dims: Dims, max_tokens: int, device: torch.device) -> Workspac
     return ws
 
 
+class PrefillWorkspace(Workspace):
+    """Device scratch of the chunked-prefill path for chunks of up to `max_tokens` tokens: bf16 copy
+    of x, router logits, routing table, per-expert groups, h [T * (k + 1), inter] bf16."""
+
+    def __init__(self, dims: Dims, max_tokens: int, device: torch.device):
+        self.dims = dims
+        self.max_tokens = max_tokens
+        nbytes = lib.qmoe_prefill_workspace_bytes(ctypes.byref(dims), max_tokens)
+        if nbytes == 0:
+            raise QMoEError(_lib.QMOE_ERR_UNSUPPORTED, "qmoe_prefill_workspace_bytes")
+        self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        check(lib.qmoe_workspace_init(self.buf.data_ptr(), nbytes, _stream()), "qmoe_workspace_init")
+
+
+_PWS: dict[tuple, PrefillWorkspace] = {}
+
+
+def prefill_workspace_for(dims: Dims, n_tokens: int, device: torch.device) -> PrefillWorkspace:
+    """A prefill workspace covering n_tokens (grown in powers of two, kept per shape and device)."""
+    key = (_dims_key(dims), str(device))
+    ws = _PWS.get(key)
+    if ws is None or ws.max_tokens < n_tokens:
+        cap = min(max(128, 1 << (n_tokens - 1).bit_length()), lib.qmoe_prefill_max_tokens())
+        ws = _PWS[key] = PrefillWorkspace(dims, max(cap, n_tokens), device)
+    return ws
+
+
 def _act(x: torch.Tensor) -> tuple[torch.Tensor, int]:
     """[.., M, D] bf16/fp32 -> contiguous [M, D] and its act dtype code."""
     if not x.is_cuda:
@@ -120,6 +147,49 @@ class MoELayer:
             out = torch.empty(m, self.cfg.hidden, dtype=torch.float32, device=x2.device)
         check(lib.qmoe_moe_block(x2.data_ptr(), dt, m, ctypes.byref(self.weights), ctypes.byref(self.dims),
                                  out.data_ptr(), self.ws.ptr, self.ws.nbytes, _stream()), "qmoe_moe_block")
+        return out
+
+    # ---- chunked prefill (tt/model.py:2812-2907 _prefill_ffn_half) ------------
+    def prefill(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """x [T, hidden] bf16/fp32 -> [T, hidden] fp32: route, group tokens per expert, tcgen05
+        grouped GEMMs (gate|up + SwiGLU, down + weighted scatter-add), shared expert."""
+        x2, dt = _act(x)
+        t = x2.shape[0]
+        ws = prefill_workspace_for(self.dims, t, x2.device)
+        if out is None:
+            out = torch.empty(t, self.cfg.hidden, dtype=torch.float32, device=x2.device)
+        check(lib.qmoe_prefill(x2.data_ptr(), dt, t, ctypes.byref(self.weights), ctypes.byref(self.dims),
+                               out.data_ptr(), ws.ptr, ws.nbytes, _stream()), "qmoe_prefill")
+        return out
+
+    def prefill_route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(ids [T, k] int32, weights [T, k] fp32, shared_logit [T] fp32) for a chunk of T tokens."""
+        x2, dt = _act(x)
+        t = x2.shape[0]
+        k = self.cfg.top_k
+        ws = prefill_workspace_for(self.dims, t, x2.device)
+        ids = torch.empty(t, k, dtype=torch.int32, device=x2.device)
+        w = torch.empty(t, k, dtype=torch.float32, device=x2.device)
+        sl = torch.empty(t, dtype=torch.float32, device=x2.device)
+        check(lib.qmoe_prefill_route(x2.data_ptr(), dt, t, ctypes.byref(self.weights), ctypes.byref(self.dims),
+                                     ids.data_ptr(), w.data_ptr(), sl.data_ptr(), ws.ptr, ws.nbytes, _stream()),
+              "qmoe_prefill_route")
+        return ids, w, sl
+
+    def prefill_experts(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                        shared_logit: torch.Tensor | None) -> torch.Tensor:
+        """Routed experts (+ the shared expert) of a chunk for a given routing table."""
+        x2, dt = _act(x)
+        t = x2.shape[0]
+        ws = prefill_workspace_for(self.dims, t, x2.device)
+        ids = ids.to(torch.int32).contiguous()
+        weights = weights.to(torch.float32).contiguous()
+        sl = None if shared_logit is None else shared_logit.to(torch.float32).contiguous()
+        out = torch.empty(t, self.cfg.hidden, dtype=torch.float32, device=x2.device)
+        check(lib.qmoe_prefill_experts(x2.data_ptr(), dt, t, ids.data_ptr(), weights.data_ptr(),
+                                       None if sl is None else sl.data_ptr(), ctypes.byref(self.weights),
+                                       ctypes.byref(self.dims), out.data_ptr(), ws.ptr, ws.nbytes, _stream()),
+              "qmoe_prefill_experts")
         return out
 
     def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
@@ -243,9 +313,14 @@ def route_topk(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[tor
     dims = _raw_dims(D, 256, E, top_k)
     r_w = router_w.float().contiguous()
     w = LayerWeights(router=r_w.data_ptr())
-    ws = workspace_for(dims, max(m, 1), x2.device)
     ids = torch.empty(m, top_k, dtype=torch.int32, device=x2.device)
     wt = torch.empty(m, top_k, dtype=torch.float32, device=x2.device)
+    if m > lib.qmoe_max_tokens():  # a prefill chunk
+        pws = prefill_workspace_for(dims, m, x2.device)
+        check(lib.qmoe_prefill_route(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), ids.data_ptr(),
+                                     wt.data_ptr(), None, pws.ptr, pws.nbytes, _stream()), "route")
+        return ids, wt
+    ws = workspace_for(dims, max(m, 1), x2.device)
     check(lib.qmoe_route(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), ids.data_ptr(),
                          wt.data_ptr(), None, ws.ptr, ws.nbytes, _stream()), "route")
     return ids, wt
@@ -279,6 +354,15 @@ def apply_experts(x: torch.Tensor, weights: torch.Tensor, keep: torch.Tensor, ga
     dims = _raw_dims(hidden_size, intermediate_size, num_experts, k)
     d_w = down_w.contiguous()
     lw = LayerWeights(gate_up=gu.data_ptr(), down=d_w.data_ptr())
+    if m > lib.qmoe_max_tokens():  # a prefill chunk: grouped tensor-core path
+        pws = prefill_workspace_for(dims, m, x2.device)
+        ids32 = ids.to(torch.int32).contiguous()
+        wt = wt.contiguous()
+        out = torch.empty(m, hidden_size, dtype=torch.float32, device=x2.device)
+        check(lib.qmoe_prefill_experts(x2.data_ptr(), dt, m, ids32.data_ptr(), wt.data_ptr(), None, ctypes.byref(lw),
+                                       ctypes.byref(dims), out.data_ptr(), pws.ptr, pws.nbytes, _stream()),
+              "apply_experts")
+        return out
     ws = workspace_for(dims, max(m, 1), x2.device)
     hs = intermediate_size
     h = torch.empty(m, k + 1, hs, dtype=torch.float32, device=x2.device)
