@@ -267,7 +267,14 @@ def main() -> None:
         t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ms_e2e = t.tolist()
+        # Every CUDA graph holding NCCL work is released before the process group is destroyed
+        # (a live one makes destroy_process_group wait forever).
+        torch.cuda.synchronize(dev)
+        del g
         stack.release()
+        import gc
+
+        gc.collect()
 
     if rank == 0:
         hbm, hbm_kind = peaks()

@@ -245,10 +245,11 @@ def test_stack_kernel_matches_layer_chain(pkg, oracle):
             checked += 1
         act = want.to(torch.bfloat16)
     assert checked >= 2
-    # repeated launches reuse the workspace: identical bits
+    # Repeated launches reuse the workspace.  The single launch sums each layer's router logits
+    # from per-CTA partials with fp32 atomics, so reruns agree to fp32 rounding, not bit for bit.
     again = stack.decode(x).clone()
     torch.cuda.synchronize()
-    assert torch.equal(again, got)
+    assert oracle.max_rel_err(again.cpu().numpy(), got.cpu().numpy()) <= 1e-4
 
 
 def test_deterministic_reruns(pkg):
@@ -290,6 +291,21 @@ def test_device_family_full_stack_c2(pkg, oracle):
     torch.cuda.synchronize()
     stack.ws.raise_if_error("c2 stack")
     assert torch.isfinite(out).all()
+    # The single launch at the config-2 shape against the per-layer launches, 1-3 layers deep.
+    act = x
+    for n in (1, 2, 3):
+        st = pkg.MoEStack(dls[:n], max_tokens=1)
+        assert st.single_launch(1)
+        got = st.decode(x).clone()
+        want = pkg.MoELayer(dls[n - 1])(act)
+        torch.cuda.synchronize()
+        st.ws.raise_if_error("c2 single launch")
+        hv = pkg.weights.device_layer_host_view(dls[n - 1])
+        ref = oracle.moe_forward(act.float().cpu().numpy(), oracle.ExpertSource.from_host_layer(hv), cfg.top_k)
+        if well_conditioned(ref["probs"], cfg.top_k):
+            assert oracle.max_rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 2e-3, f"{n} layers"
+        act = want.to(torch.bfloat16)
+        del st
     act = x
     for l in range(2):  # the literal chain stays well conditioned this deep
         y = pkg.MoELayer(dls[l])(act)

@@ -199,7 +199,7 @@ WsLayout ws_layout(const qmoe_dims& d, int max_tokens) {
     L.act = off;
     off = align_up(off + (size_t)M * d.hidden * 4, 256);
     L.sync = off;
-    off = align_up(off + 1152, 256);
+    off = align_up(off + stack_sync_bytes(d.n_experts), 256);
     L.trace = off;
     off = align_up(off + 2 * 64 * 16 * 8, 256);
     L.total = off;

@@ -26,13 +26,20 @@ struct WsLayout {
     size_t shared;      // fp32 [max_tokens]
     size_t h;           // fp32 [max_tokens][top_k + 1][h_stride]
     size_t act;         // fp32 [max_tokens][hidden]: the stack kernel's layer activation
-    size_t sync;        // grid-barrier counters (8 x 128 B) and the abort word
+    size_t sync;        // grid-barrier counters (8 x 128 B), the abort word, then the stack
+                        // kernel's two router-logit accumulators (stack_sync_bytes)
     size_t trace;       // u64 [64 layers][8]: the stack kernel's phase timestamps
     size_t total;
     int h_stride;
 };
 
 WsLayout ws_layout(const qmoe_dims& d, int max_tokens);
+
+// The stack kernel's zero-initialised words: 8 barrier counters 128 B apart and
+// the abort word (1152 B), then two accumulators of E + 1 router logits, four
+// logits per 128-byte line so that the CTAs' atomic adds spread over lines.
+inline size_t stack_logit_groups(int E) { return (size_t)(E + 1 + 3) / 4; }
+inline size_t stack_sync_bytes(int E) { return 1152 + 2 * stack_logit_groups(E) * 128; }
 
 // Launch arguments of the routing kernel.
 struct RouteArgs {

@@ -2,28 +2,34 @@
 //
 // One CTA per SM (cooperative launch, so all CTAs are co-resident), looping
 // over the layers.  Every layer is the reference's `_moe` (reference/model.py
-// :387-417) in three phases separated by grid barriers:
+// :387-417) in two phases separated by grid barriers:
 //
-//   A  x (bf16) -> block floating point in shared memory; this CTA's router
-//      rows (fp32, already in shared memory) -> logits; this CTA's shared-
-//      expert gate|up rows (already in shared memory) -> shared h.
-//   B  every CTA ranks the 512 logits itself (warp top-k, lower id on ties),
-//      then TMA bulk copies (cp.async.bulk, one thread issuing, mbarrier
-//      completion) bring only its slice of the selected experts' gate|up rows
-//      and down rows into shared memory; gate|up rows are decoded as their
-//      4-pair chunks land -> routed h.
-//   C  the full h (11 x 512) -> block floating point; this CTA's output rows
-//      of every selected expert's down (already in shared memory) and of the
-//      shared expert -> out[j] = sum_s w_s D_s[j].h_s + sigmoid(g.x) D_sh[j].h_sh.
-//      Meanwhile the next layer's router rows and shared-expert rows stream
-//      in, so phase A of the next layer starts on resident data.
+//   B  every CTA ranks the E router logits itself (block top-k, lower id on
+//      ties) and starts bulk copies (cp.async.bulk, mbarrier completion) of
+//      only its slice of the selected experts' gate|up rows and down rows;
+//      meanwhile it converts x to block floating point and computes its rows
+//      of the shared expert's gate|up (prefetched); routed gate|up rows are
+//      decoded as their 4-pair chunks land -> h slice.
+//   C  the full h (k + 1 slots) -> block floating point; this CTA's output
+//      rows of every selected expert's down (resident since phase B) and of
+//      the shared expert -> out[j] = sum_s w_s D_s[j].h_s + sigmoid(g.x) D_sh[j].h_sh;
+//      then the NEXT layer's router logits restricted to these rows,
+//      sum_j R[e][j] x[j] over this CTA's j (router columns prefetched during
+//      phase B), added into a logit accumulator with vector fp32 atomics.
 //
-// The layer output is written in fp32 and rounded to bf16 when the next layer
-// loads it (bf16 activations, fp32 accumulation).  All waits are bounded in
-// time (%globaltimer): a grid barrier or copy that does not complete sets
-// QMOE_ERR_TIMEOUT and an abort word, every CTA waits (bounded) for its own
+// The barrier after C therefore publishes both the next layer's input and
+// its complete router logits: two grid barriers per layer.  The router
+// logits are sums of per-CTA partials in arrival order (fp32 atomics), so
+// their last bits may vary between runs; selection reads them only after
+// the barrier.  A prologue computes layer 0's logits the same way.
+//
+// Activations between layers are fp32 rounded to bf16 where they are read
+// (bf16 activations, fp32 accumulation).  All waits are bounded in time
+// (%globaltimer): a grid barrier or copy that does not complete sets
+// QMOE_ERR_TIMEOUT and an abort word; every CTA waits (bounded) for its own
 // copies in flight and returns.  No trap, no unbounded spin.
 #include "common.cuh"
+#include "ptx.cuh"
 #include "topk.cuh"
 
 namespace qmoe {
@@ -52,7 +58,7 @@ struct SKArgs {
     const __nv_bfloat16* x;  // [D] layer-0 input
     float* out;              // [D] last layer's output
     float* act;              // [D] layer activation (workspace)
-    float* logits;           // [E + 1] (workspace); row E is the shared-expert gate
+    float* logits;           // two accumulators of G lines x 32 floats (logits 4g..4g+3 at a line's front)
     float* h;                // [(K + 1) * I] (workspace)
     unsigned* sync;          // 8 counters, 128 B apart, then the abort word
     unsigned long long* trace;  // [2][64][16] phase stamps of CTA 0 and the last CTA, or null
@@ -63,9 +69,9 @@ struct SKArgs {
 
 // Shared-memory carve-up (byte offsets), a function of the shape and grid.
 struct SKLayout {
-    int NR, NSQ, NP, NJ, NCH;
-    unsigned xf, xq, xs, rbuf, sgu, sdn, gbuf, ubuf, dbuf, hq, hs, gv, uv, sgv, suv, rpart, dpart,
-        cand, wmax, red, tkv, tki, misc, issued, bars, total;
+    int NSQ, NP, NJ, RJ, NCH;
+    unsigned xq, xs, rcol, xo, sgu, sdn, gbuf, ubuf, dbuf, hq, hs, gv, uv, sgv, suv, dpart, cand, red, tkv, tki,
+        misc, issued, bars, total;
 };
 
 __host__ __device__ constexpr unsigned sk_take(unsigned& o, unsigned bytes) {
@@ -78,16 +84,16 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     SKLayout s{};
     const unsigned RB = (unsigned)(D / 256) * 136, DRB = (unsigned)(I / 256) * 136;
     const unsigned NSB = D / 32, NSBH = I / 32;
-    s.NR = (E + 1 + n - 1) / n;
     s.NSQ = (I + n - 1) / n;
     s.NP = (K * I + n - 1) / n;
     s.NJ = (D + n - 1) / n;
+    s.RJ = s.NJ | 1;  // odd pitch: a warp's 32 router rows hit 32 banks
     s.NCH = (s.NP + kSKChunk - 1) / kSKChunk;
     unsigned o = 0;
-    s.xf = sk_take(o, D * 4);
     s.xq = sk_take(o, NSB * 64);
     s.xs = sk_take(o, NSB * 4);
-    s.rbuf = sk_take(o, (unsigned)s.NR * D * 4);
+    s.rcol = sk_take(o, (unsigned)(E + 1) * s.RJ * 4);
+    s.xo = sk_take(o, (unsigned)s.NJ * 4);
     s.sgu = sk_take(o, 2u * s.NSQ * RB);
     s.sdn = sk_take(o, (unsigned)s.NJ * DRB);
     s.gbuf = sk_take(o, (unsigned)s.NP * RB);
@@ -99,16 +105,14 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     s.uv = sk_take(o, s.NP * 4);
     s.sgv = sk_take(o, s.NSQ * 4);
     s.suv = sk_take(o, s.NSQ * 4);
-    s.rpart = sk_take(o, s.NR * 4 * 4);
     s.dpart = sk_take(o, (unsigned)s.NJ * (K + 1) * 4);
-    s.cand = sk_take(o, (unsigned)(E > 256 ? E : 256) * 8);  // the tie fallback keeps 16 x k
-    s.wmax = sk_take(o, (kSKWarps + 1) * 8);
+    s.cand = sk_take(o, (unsigned)(E / 32) * K * 8);
     s.red = sk_take(o, kSKWarps * 4);
     s.tkv = sk_take(o, kMaxTopK * 4);
     s.tki = sk_take(o, kMaxTopK * 4);
     s.misc = sk_take(o, 64);
-    s.issued = sk_take(o, (4 + kSKMaxChunks) * 4);
-    s.bars = sk_take(o, (4 + kSKMaxChunks) * 8);
+    s.issued = sk_take(o, (3 + kSKMaxChunks) * 4);
+    s.bars = sk_take(o, (3 + kSKMaxChunks) * 8);
     s.total = o;
     return s;
 }
@@ -120,48 +124,16 @@ template <int D_, int E_, int K_, int NSM_>
 struct SKShape {
     static constexpr int D = D_, E = E_, K = K_, NSM = NSM_, I = 512;
     static constexpr SKLayout S = sk_layout(D_, 512, E_, K_, NSM_);
+    static_assert(E_ <= kSKThreads && E_ % 32 == 0, "one router row per thread");
+    static_assert((D_ + NSM_ - 1) / NSM_ <= 16, "router column slice: at most 16 per CTA");
 };
 
 namespace {
 
-// ---- PTX wrappers: mbarrier, bulk copy, proxy fence, timer ---------------
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Global -> shared bulk copy into this CTA's own shared memory; dst, src 16-byte aligned, bytes % 16 == 0.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_addr(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ unsigned long long now_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
+using ptx::mbar_expect_tx;
+using ptx::mbar_init;
+using ptx::mbar_test;
+using ptx::now_ns;
 
 // Bounded wait for the phase of `bar` with parity `par`; false on timeout.
 __device__ bool mbar_wait(uint64_t* bar, uint32_t par) {
@@ -192,7 +164,7 @@ __device__ bool grid_sync(unsigned* sync, unsigned gen, int* status, int* s_ok) 
     __syncthreads();
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        if (lane == 0)  // release: orders this CTA's writes (after bar.sync) before the arrival
+        if (lane == 0)  // release: orders this CTA's writes and atomics (after bar.sync) before the arrival
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(sync + 32 * (blockIdx.x & 7)) : "memory");
         const int i = lane & 7;
         const unsigned n = gridDim.x;
@@ -251,8 +223,7 @@ __device__ __forceinline__ float row_dot(const uint8_t* row, const int (&xr)[SBL
     return warp_sum(acc);
 }
 
-// One 32-value block to block floating point (out of line: one copy of the
-// code serves the x and the h conversions).
+// One 32-value block to block floating point, lane j holding value j.
 __device__ __forceinline__ void convert_block(float v, int* q16, float* step, int lane) {
     float st;
     const int pw = warp_block_fp(v, &st);
@@ -293,7 +264,7 @@ __device__ __forceinline__ float down_unit(const uint8_t* row, const int* hq, co
 struct SKPart {
     int D, I, E, K, RB, DRB, NSBH;
     size_t GUE, DNE;
-    int rr_lo, rr_hi, sq_lo, sq_hi, p_lo, p_hi, j_lo, j_hi;
+    int sq_lo, sq_hi, p_lo, p_hi, j_lo, j_hi;
 };
 
 template <class SH>
@@ -310,9 +281,7 @@ __device__ __forceinline__ SKPart sk_part() {
     p.NSBH = SH::I >> 5;
     p.GUE = (size_t)2 * SH::I * p.RB;
     p.DNE = (size_t)SH::D * p.DRB;
-    constexpr int R = SH::E + 1, P = SH::K * SH::I;
-    p.rr_lo = c * R / n;
-    p.rr_hi = (c + 1) * R / n;
+    constexpr int P = SH::K * SH::I;
     p.sq_lo = c * SH::I / n;
     p.sq_hi = (c + 1) * SH::I / n;
     p.p_lo = c * P / n;
@@ -322,30 +291,66 @@ __device__ __forceinline__ SKPart sk_part() {
     return p;
 }
 
-// Router rows + shared-expert gate|up rows of one layer (thread 0 only).
-__device__ __forceinline__ void issue_phase_a(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
-                              uint64_t* bar_r, uint64_t* bar_sgu) {
-    const int nr = p.rr_hi - p.rr_lo, nsq = p.sq_hi - p.sq_lo;
-    float* rbuf = reinterpret_cast<float*>(sm + S.rbuf);
-    mbar_expect_tx(bar_r, (uint32_t)(nr * p.D * 4));
-    const int r_end = p.rr_hi < p.E ? p.rr_hi : p.E;
-    if (r_end > p.rr_lo)
-        bulk_g2s(rbuf, W.router + (size_t)p.rr_lo * p.D, (uint32_t)((r_end - p.rr_lo) * p.D * 4), bar_r);
-    if (p.rr_hi > p.E) bulk_g2s(rbuf + (size_t)(p.E - p.rr_lo) * p.D, W.gate_vec, (uint32_t)(p.D * 4), bar_r);
+// Shared-expert gate|up rows of this CTA's slice (thread 0 only).
+__device__ __forceinline__ void issue_sgu(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
+                                          uint64_t* bar) {
+    const int nsq = p.sq_hi - p.sq_lo;
     uint8_t* sgu = sm + S.sgu;
-    mbar_expect_tx(bar_sgu, (uint32_t)(2 * nsq * p.RB));
+    mbar_expect_tx(bar, (uint32_t)(2 * nsq * p.RB));
     if (nsq > 0) {
-        bulk_g2s(sgu, W.sh_gate_up + (size_t)p.sq_lo * p.RB, (uint32_t)(nsq * p.RB), bar_sgu);
-        bulk_g2s(sgu + (size_t)S.NSQ * p.RB, W.sh_gate_up + (size_t)(p.I + p.sq_lo) * p.RB,
-                 (uint32_t)(nsq * p.RB), bar_sgu);
+        ptx::bulk_g2s(sgu, W.sh_gate_up + (size_t)p.sq_lo * p.RB, (uint32_t)(nsq * p.RB), bar);
+        ptx::bulk_g2s(sgu + (size_t)S.NSQ * p.RB, W.sh_gate_up + (size_t)(p.I + p.sq_lo) * p.RB,
+                      (uint32_t)(nsq * p.RB), bar);
     }
 }
 
 // Shared-expert down rows of this CTA's output slice (thread 0 only).
-__device__ __forceinline__ void issue_sdn(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm, uint64_t* bar) {
+__device__ __forceinline__ void issue_sdn(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
+                                          uint64_t* bar) {
     const int nj = p.j_hi - p.j_lo;
     mbar_expect_tx(bar, (uint32_t)(nj * p.DRB));
-    if (nj > 0) bulk_g2s(sm + S.sdn, W.sh_down + (size_t)p.j_lo * p.DRB, (uint32_t)(nj * p.DRB), bar);
+    if (nj > 0) ptx::bulk_g2s(sm + S.sdn, W.sh_down + (size_t)p.j_lo * p.DRB, (uint32_t)(nj * p.DRB), bar);
+}
+
+// Router columns j_lo..j_hi of every router row and of the gate vector
+// (row E), 4-byte asynchronous copies: lanes 0-15 take one row, 16-31 the
+// next, so each instruction touches two rows' contiguous slices.
+__device__ __forceinline__ void issue_rcol(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm) {
+    float* rcol = reinterpret_cast<float*>(sm + S.rcol);
+    const int nj = p.j_hi - p.j_lo, jj = threadIdx.x & 15;
+    if (jj < nj) {
+        for (int e = threadIdx.x >> 4; e <= p.E; e += kSKThreads / 16) {
+            const float* src = (e < p.E ? W.router + (size_t)e * p.D : W.gate_vec) + p.j_lo + jj;
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ptx::smem_addr(rcol + e * S.RJ + jj)),
+                         "l"(src)
+                         : "memory");
+        }
+    }
+    ptx::cp_async_commit();
+}
+
+// This CTA's share of the router logits: thread e (and thread 0 for the gate
+// row E) sums rcol[e][j] * x[j_lo + j] over its j; four consecutive experts
+// combine into one vector atomic add on their accumulator line.
+__device__ __forceinline__ void router_partial(const SKPart& p, const SKLayout& S, const unsigned char* sm,
+                                               float* acc_buf) {
+    const float* rcol = reinterpret_cast<const float*>(sm + S.rcol);
+    const float* xo = reinterpret_cast<const float*>(sm + S.xo);
+    const int nj = p.j_hi - p.j_lo, e = threadIdx.x, lane = threadIdx.x & 31;
+    float v = 0.0f;
+    if (e < p.E)
+        for (int j = 0; j < nj; ++j) v = fmaf(rcol[e * S.RJ + j], xo[j], v);
+    const float v1 = __shfl_down_sync(0xffffffffu, v, 1), v2 = __shfl_down_sync(0xffffffffu, v, 2),
+                v3 = __shfl_down_sync(0xffffffffu, v, 3);
+    if (e < p.E && (lane & 3) == 0)
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(acc_buf + (e >> 2) * 32), "f"(v), "f"(v1),
+                     "f"(v2), "f"(v3)
+                     : "memory");
+    if (e == 0) {
+        float g = 0.0f;
+        for (int j = 0; j < nj; ++j) g = fmaf(rcol[p.E * S.RJ + j], xo[j], g);
+        atomicAdd(acc_buf + (p.E >> 2) * 32 + (p.E & 3), g);
+    }
 }
 
 // The selected experts' slices, issued by warp 0: lane 0 first posts every
@@ -353,10 +358,10 @@ __device__ __forceinline__ void issue_sdn(const SKLayer& W, const SKPart& p, con
 // and, for i < K, expert slot i's down rows.  Chunks are kSKChunk row pairs
 // with their own mbarrier so decoding starts on the first chunk to land.
 __device__ __forceinline__ void issue_routed(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
-                             const int* ids, uint64_t* bar_ch, uint64_t* bar_dn, int lane) {
+                                             const int* ids, uint64_t* bar_ch, uint64_t* bar_dn, int lane) {
     const int np = p.p_hi - p.p_lo, nj = p.j_hi - p.j_lo;
     if (lane == 0) {
-        fence_proxy_async();
+        ptx::fence_proxy_async();
         for (int ch = 0; ch < S.NCH; ++ch) {
             const int u0 = ch * kSKChunk;
             const int u1 = (u0 + kSKChunk < np) ? u0 + kSKChunk : np;
@@ -376,16 +381,16 @@ __device__ __forceinline__ void issue_routed(const SKLayer& W, const SKPart& p, 
             const int s = pp / p.I, r = pp - s * p.I;
             const int seg = (u1 - u) < (p.I - r) ? (u1 - u) : (p.I - r);
             const uint8_t* eb = W.gate_up + (size_t)ids[s] * p.GUE;
-            bulk_g2s(gbuf + (size_t)u * p.RB, eb + (size_t)r * p.RB, (uint32_t)(seg * p.RB), bar_ch + ch);
-            bulk_g2s(ubuf + (size_t)u * p.RB, eb + (size_t)(p.I + r) * p.RB, (uint32_t)(seg * p.RB), bar_ch + ch);
+            ptx::bulk_g2s(gbuf + (size_t)u * p.RB, eb + (size_t)r * p.RB, (uint32_t)(seg * p.RB), bar_ch + ch);
+            ptx::bulk_g2s(ubuf + (size_t)u * p.RB, eb + (size_t)(p.I + r) * p.RB, (uint32_t)(seg * p.RB), bar_ch + ch);
             u += seg;
         }
     }
     if (nj > 0) {
         uint8_t* dbuf = sm + S.dbuf;
         for (int s = lane; s < p.K; s += 32)
-            bulk_g2s(dbuf + (size_t)s * S.NJ * p.DRB, W.down + (size_t)ids[s] * p.DNE + (size_t)p.j_lo * p.DRB,
-                     (uint32_t)(nj * p.DRB), bar_dn);
+            ptx::bulk_g2s(dbuf + (size_t)s * S.NJ * p.DRB, W.down + (size_t)ids[s] * p.DNE + (size_t)p.j_lo * p.DRB,
+                          (uint32_t)(nj * p.DRB), bar_dn);
     }
 }
 
@@ -396,14 +401,13 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     const SKPart p = sk_part<SH>();
     constexpr SKLayout S = SH::S;
     constexpr int SBL2 = SH::D / 1024;
-    constexpr int NSB = 32 * SBL2;
     constexpr int D = SH::D, I = SH::I, E = SH::E, K = SH::K;
-    const int nr = p.rr_hi - p.rr_lo, nsq = p.sq_hi - p.sq_lo, np = p.p_hi - p.p_lo, nj = p.j_hi - p.j_lo;
+    const int nsq = p.sq_hi - p.sq_lo, np = p.p_hi - p.p_lo, nj = p.j_hi - p.j_lo;
+    constexpr int G = (E + 1 + 3) / 4;  // accumulator lines per logit buffer
 
-    float* xf = reinterpret_cast<float*>(sm + S.xf);
     int* xq = reinterpret_cast<int*>(sm + S.xq);
     float* xs = reinterpret_cast<float*>(sm + S.xs);
-    const float* rbuf = reinterpret_cast<const float*>(sm + S.rbuf);
+    float* xo = reinterpret_cast<float*>(sm + S.xo);
     const uint8_t* sgu = sm + S.sgu;
     const uint8_t* sdn = sm + S.sdn;
     const uint8_t* gbuf = sm + S.gbuf;
@@ -415,67 +419,90 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     float* uv = reinterpret_cast<float*>(sm + S.uv);
     float* sgv = reinterpret_cast<float*>(sm + S.sgv);
     float* suv = reinterpret_cast<float*>(sm + S.suv);
-    float* rpart = reinterpret_cast<float*>(sm + S.rpart);
     float* dpart = reinterpret_cast<float*>(sm + S.dpart);
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(sm + S.cand);
-    unsigned long long* wmax = reinterpret_cast<unsigned long long*>(sm + S.wmax);
     unsigned* red = reinterpret_cast<unsigned*>(sm + S.red);
     float* tkv = reinterpret_cast<float*>(sm + S.tkv);
     int* tki = reinterpret_cast<int*>(sm + S.tki);
     int* s_ok = reinterpret_cast<int*>(sm + S.misc);
     float* s_gate = reinterpret_cast<float*>(sm + S.misc) + 4;
-    int* s_cnt = reinterpret_cast<int*>(sm + S.misc) + 8;
-    float* s_glogit = reinterpret_cast<float*>(sm + S.misc) + 12;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S.bars);
-    uint64_t* bar_r = bars;
-    uint64_t* bar_sgu = bars + 1;
-    uint64_t* bar_sdn = bars + 2;
-    uint64_t* bar_dn = bars + 3;
-    uint64_t* bar_ch = bars + 4;
-    const int nbars = 4 + S.NCH;
+    uint64_t* bar_sgu = bars;
+    uint64_t* bar_sdn = bars + 1;
+    uint64_t* bar_dn = bars + 2;
+    uint64_t* bar_ch = bars + 3;
+    const int nbars = 3 + S.NCH;
 
     if (tid == 0) {
         for (int i = 0; i < nbars; ++i) mbar_init(bars + i, 1);
-        fence_mbar_init();
+        ptx::fence_mbar_init();
     }
     __syncthreads();
     // Phases issued per barrier (kept by thread 0), for the bounded drain.
     int* issued = reinterpret_cast<int*>(sm + S.issued);
     if (tid == 0) {
         for (int i = 0; i < nbars; ++i) issued[i] = 0;
-        issue_phase_a(a.L[0], p, S, sm, bar_r, bar_sgu);
+        issue_sgu(a.L[0], p, S, sm, bar_sgu);
         issue_sdn(a.L[0], p, S, sm, bar_sdn);
-        issued[0] = issued[1] = issued[2] = 1;
+        issued[0] = issued[1] = 1;
     }
 
+    // ---------------- prologue: layer 0's router logits --------------------
+    issue_rcol(a.L[0], p, S, sm);
+    if (tid < nj) xo[tid] = __bfloat162float(a.x[p.j_lo + tid]);
+    ptx::cp_async_wait<0>();
+    __syncthreads();
+    router_partial(p, S, sm, a.logits);
     unsigned gen = 0;
-    bool ok = true;
+    bool ok = grid_sync(a.sync, ++gen, a.status, s_ok);
+
     for (int L = 0; L < a.n_layers && ok; ++L) {
         const SKLayer& W = a.L[L];
         const uint32_t par = (uint32_t)(L & 1);
         const bool last = L + 1 == a.n_layers;
+        const float* lg = a.logits + (size_t)(L & 1) * G * 32;
+        float* lg_next = a.logits + (size_t)((L + 1) & 1) * G * 32;
 
-        // ---------------- phase A: x, router rows, shared gate|up --------
+        // ---------------- phase B: top-k, gate|up ----------------------------
         trace_mark(a, L, 0);
-        {
-            // every load of x issued before any store (D <= 4 * kSKThreads)
-            float v[4];
+        // x loads first (they complete under the top-k): thread t holds
+        // elements t + 512 k4, i.e. lane `lane` of blocks warp + 16 k4.
+        float v[4];
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-                const int i = tid + k4 * kSKThreads;
-                v[k4] = 0.0f;
-                if (i < D) v[k4] = L == 0 ? __bfloat162float(a.x[i]) : __ldcg(a.act + i);
-            }
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-                const int i = tid + k4 * kSKThreads;
-                if (i < D) xf[i] = L == 0 ? v[k4] : __bfloat162float(__float2bfloat16_rn(v[k4]));
-            }
+        for (int k4 = 0; k4 < 4; ++k4) {
+            const int i = tid + k4 * kSKThreads;
+            v[k4] = 0.0f;
+            if (i < D)
+                v[k4] = L == 0 ? __bfloat162float(a.x[i]) : __bfloat162float(__float2bfloat16_rn(__ldcg(a.act + i)));
         }
-        __syncthreads();
+        const float lmax =
+            block_topk_ranked([&](int i) { return lg + (i >> 2) * 32 + (i & 3); }, E, K, cand, red, tkv, tki);
         trace_mark(a, L, 1);
-#pragma unroll 1
-        for (int b = warp; b < NSB; b += kSKWarps) convert_block(xf[b * 32 + lane], xq + b * 16, xs + b, lane);
+        if (warp == 0) {
+            const float e = lane < K ? tkv[lane] : 0.0f;
+            const float sum = warp_sum(e);
+            if (lane < K) tkv[lane] = e / sum;
+            if (lane == 0) {
+                *s_gate = sigmoid(__ldcg(lg + (E >> 2) * 32 + (E & 3)));
+                if (!(fabsf(lmax) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
+            }
+            issue_routed(W, p, S, sm, tki, bar_ch, bar_dn, lane);
+            if (tid == 0)
+                for (int i = 2; i < nbars; ++i) ++issued[i];
+        }
+        trace_mark(a, L, 2);
+        // x -> block floating point (each warp its own 4 blocks, from registers)
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+            const int b = warp + k4 * kSKWarps;
+            if (b * 32 < D) convert_block(v[k4], xq + b * 16, xs + b, lane);
+        }
+        // CTA 0 clears the other logit accumulator for the next layer's sums
+        // (read last in the previous layer's phase B; first added to after
+        // this layer's second barrier).
+        if (blockIdx.x == 0 && !last)
+            for (int g = tid; g < G; g += kSKThreads)
+                *reinterpret_cast<float4*>(lg_next + g * 32) = make_float4(0.f, 0.f, 0.f, 0.f);
         __syncthreads();
         int xr[SBL2][16];
         float xsr[SBL2];
@@ -484,19 +511,20 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             const int b = lane * SBL2 + i;
             const int4* src = reinterpret_cast<const int4*>(xq + b * 16);
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-                const int4 w4 = src[v];
-                xr[i][4 * v] = w4.x;
-                xr[i][4 * v + 1] = w4.y;
-                xr[i][4 * v + 2] = w4.z;
-                xr[i][4 * v + 3] = w4.w;
+            for (int q = 0; q < 4; ++q) {
+                const int4 w4 = src[q];
+                xr[i][4 * q] = w4.x;
+                xr[i][4 * q + 1] = w4.y;
+                xr[i][4 * q + 2] = w4.z;
+                xr[i][4 * q + 3] = w4.w;
             }
             xsr[i] = xs[b];
         }
-        trace_mark(a, L, 2);
+        trace_mark(a, L, 3);
+        // shared expert gate|up rows (prefetched)
         {
-            const bool w_ok = mbar_wait(bar_r, par) && mbar_wait(bar_sgu, par);
-            if (__syncthreads_or(!w_ok)) {  // block-uniform decision
+            const bool w_ok = mbar_wait(bar_sgu, par);
+            if (__syncthreads_or(!w_ok)) {
                 if (tid == 0) {
                     record_status(a.status, QMOE_ERR_TIMEOUT);
                     atomicExch(abort_word(a.sync), 1u);
@@ -505,65 +533,23 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 break;
             }
         }
-        trace_mark(a, L, 3);
-        // router: work item = (row, quarter of the columns)
-        for (int it = warp; it < nr * 4; it += kSKWarps) {
-            const int r = it >> 2, q = it & 3;
-            const float* wr = rbuf + (size_t)r * D;
-            const int cols = D >> 2;
-            float acc = 0.0f;
-            for (int c4 = q * cols + lane * 4; c4 < (q + 1) * cols; c4 += 128) {
-                const float4 w4 = *reinterpret_cast<const float4*>(wr + c4);
-                const float4 x4 = *reinterpret_cast<const float4*>(xf + c4);
-                acc = fmaf(w4.x, x4.x, acc);
-                acc = fmaf(w4.y, x4.y, acc);
-                acc = fmaf(w4.z, x4.z, acc);
-                acc = fmaf(w4.w, x4.w, acc);
-            }
-            acc = warp_sum(acc);
-            if (lane == 0) rpart[it] = acc;
-        }
-        // shared expert gate|up rows
         for (int t = warp; t < 2 * nsq; t += kSKWarps) {
             const uint8_t* row = sgu + (size_t)((t & 1) ? (S.NSQ + (t >> 1)) : (t >> 1)) * p.RB;
-            const float v = row_dot<SBL2>(row, xr, xsr, lane);
-            if (lane == 0) ((t & 1) ? suv : sgv)[t >> 1] = v;
+            const float r = row_dot<SBL2>(row, xr, xsr, lane);
+            if (lane == 0) ((t & 1) ? suv : sgv)[t >> 1] = r;
         }
         __syncthreads();
-        trace_mark(a, L, 4);
-        if (tid < nr) a.logits[p.rr_lo + tid] = (rpart[4 * tid] + rpart[4 * tid + 1]) + (rpart[4 * tid + 2] + rpart[4 * tid + 3]);
-        if (tid >= 64 && tid - 64 < nsq) {
-            const int q = tid - 64;
-            a.h[(size_t)K * I + p.sq_lo + q] = silu(sgv[q]) * suv[q];
-        }
-        trace_mark(a, L, 5);
-        if (!grid_sync(a.sync, ++gen, a.status, s_ok)) {
-            ok = false;
-            break;
-        }
-        trace_mark(a, L, 6);
-
-        // ---------------- phase B: top-k, routed gate|up ------------------
-        if (tid == kSKThreads - 1) *s_glogit = __ldcg(a.logits + E);  // overlaps the top-k's loads
-        const float lmax = block_topk(a.logits, E, K, cand, wmax, red, s_cnt, tkv, tki);
-        if (warp == 0) {
-            const float e = lane < K ? tkv[lane] : 0.0f;
-            const float sum = warp_sum(e);
-            if (lane < K) tkv[lane] = e / sum;
-            if (lane == 0) {
-                *s_gate = sigmoid(*s_glogit);
-                if (!(fabsf(lmax) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
+        if (!last) {
+            // The next layer's shared rows and router columns stream in behind.
+            if (tid == 0) {
+                ptx::fence_proxy_async();
+                issue_sgu(a.L[L + 1], p, S, sm, bar_sgu);
+                ++issued[0];
             }
-            trace_mark(a, L, 7);
+            issue_rcol(a.L[L + 1], p, S, sm);
         }
-        __syncthreads();
-
-        if (warp == 0) {
-            issue_routed(W, p, S, sm, tki, bar_ch, bar_dn, lane);
-            if (tid == 0)
-                for (int i = 3; i < nbars; ++i) ++issued[i];
-        }
-        trace_mark(a, L, 8);
+        trace_mark(a, L, 4);
+        // routed gate|up rows as their chunks land
         for (int t = warp; t < 2 * np; t += kSKWarps) {
             const int u = t >> 1;
             if (!mbar_wait(bar_ch + u / kSKChunk, par)) {
@@ -571,8 +557,8 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 break;
             }
             const uint8_t* row = ((t & 1) ? ubuf : gbuf) + (size_t)u * p.RB;
-            const float v = row_dot<SBL2>(row, xr, xsr, lane);
-            if (lane == 0) ((t & 1) ? uv : gv)[u] = v;
+            const float r = row_dot<SBL2>(row, xr, xsr, lane);
+            if (lane == 0) ((t & 1) ? uv : gv)[u] = r;
         }
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
@@ -582,38 +568,33 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             ok = false;
             break;
         }
-        trace_mark(a, L, 9);
+        trace_mark(a, L, 5);
         for (int u = tid; u < np; u += kSKThreads) a.h[p.p_lo + u] = silu(gv[u]) * uv[u];
-        trace_mark(a, L, 10);
+        if (tid < nsq) a.h[(size_t)K * I + p.sq_lo + tid] = silu(sgv[tid]) * suv[tid];
+        trace_mark(a, L, 6);
         if (!grid_sync(a.sync, ++gen, a.status, s_ok)) {
             ok = false;
             break;
         }
-        trace_mark(a, L, 11);
+        trace_mark(a, L, 7);
 
-        // ---------------- phase C: down + combine --------------------------
-        if (tid == 0 && !last) {
-            fence_proxy_async();
-            issue_phase_a(a.L[L + 1], p, S, sm, bar_r, bar_sgu);
-            ++issued[0];
-            ++issued[1];
-        }
+        // ---------------- phase C: down + combine, next layer's logits -------
         {
             const int nbh = (K + 1) * p.NSBH;
             constexpr int NB = 12;
             for (int b0 = warp; b0 < nbh; b0 += NB * kSKWarps) {
-                float v[NB];
+                float hv[NB];
 #pragma unroll
                 for (int i = 0; i < NB; ++i) {
                     const int b = b0 + i * kSKWarps;
-                    v[i] = b < nbh ? __ldcg(a.h + (size_t)b * 32 + lane) : 0.0f;
+                    hv[i] = b < nbh ? __ldcg(a.h + (size_t)b * 32 + lane) : 0.0f;
                 }
 #pragma unroll
                 for (int i = 0; i < NB; ++i) {
                     const int b = b0 + i * kSKWarps;
                     if (b < nbh) {
                         float st;
-                        const int pw = warp_block_fp(v[i], &st);
+                        const int pw = warp_block_fp(hv[i], &st);
                         const int slot = b / p.NSBH, t = b - slot * p.NSBH;
                         // word w = 4*quad + (w & 3) of block t of the slot
                         if (lane < 16) hq[slot * p.NSBH * 16 + ((lane >> 2) * p.NSBH + t) * 4 + (lane & 3)] = pw;
@@ -623,7 +604,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             }
         }
         __syncthreads();
-        trace_mark(a, L, 12);
+        trace_mark(a, L, 8);
         {
             const bool w_ok = mbar_wait(bar_dn, par) && mbar_wait(bar_sdn, par);
             if (__syncthreads_or(!w_ok)) {
@@ -635,7 +616,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 break;
             }
         }
-        trace_mark(a, L, 13);
+        trace_mark(a, L, 9);
         {
             // (output row j, expert slot s) per half-warp; slot K is the shared expert
             const int K1 = K + 1, nu = nj * K1, half = lane >> 4, hl = lane & 15;
@@ -653,29 +634,35 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             }
         }
         __syncthreads();
-        trace_mark(a, L, 14);
+        trace_mark(a, L, 10);
         for (int j = tid; j < nj; j += kSKThreads) {
             const float* dp = dpart + j * (K + 1);
             float o = 0.0f;
             for (int s = 0; s < K; ++s) o = fmaf(tkv[s], dp[s], o);
             o = fmaf(*s_gate, dp[K], o);
             (last ? a.out : a.act)[p.j_lo + j] = o;
+            xo[j] = __bfloat162float(__float2bfloat16_rn(o));
         }
+        if (!last) ptx::cp_async_wait<0>();  // this thread's router-column copies
         __syncthreads();
         if (tid == 0 && !last) {
-            fence_proxy_async();
+            ptx::fence_proxy_async();
             issue_sdn(a.L[L + 1], p, S, sm, bar_sdn);
-            ++issued[2];
+            ++issued[1];
         }
-        trace_mark(a, L, 15);
-        if (!last && !grid_sync(a.sync, ++gen, a.status, s_ok)) {
-            ok = false;
-            break;
+        trace_mark(a, L, 11);
+        if (!last) {
+            router_partial(p, S, sm, lg_next);
+            trace_mark(a, L, 12);
+            if (!grid_sync(a.sync, ++gen, a.status, s_ok)) {
+                ok = false;
+                break;
+            }
         }
-
     }
 
     // Stopped early: let this CTA's copies in flight land (bounded) before exit.
+    ptx::cp_async_wait<0>();
     if (!ok && tid == 0) {
         for (int i = 0; i < nbars; ++i)
             if (issued[i] > 0) (void)mbar_wait(bars + i, (uint32_t)((issued[i] - 1) & 1));
@@ -717,12 +704,13 @@ bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers) {
 cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* logits, float* h, unsigned* sync,
                                 unsigned long long* trace, int* status, const qmoe_layer_weights* layers, int n_layers,
                                 const qmoe_dims& d, cudaStream_t stream) {
+    (void)logits;  // the single launch keeps its logits in the accumulators behind the barrier words
     SKArgs a{};
     a.trace = trace;
     a.x = reinterpret_cast<const __nv_bfloat16*>(x);
     a.out = out;
     a.act = act;
-    a.logits = logits;
+    a.logits = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(sync) + 1152);
     a.h = h;
     a.sync = sync;
     a.status = status;
@@ -745,8 +733,9 @@ cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* lo
     if (!kern) return cudaErrorInvalidValue;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    // Barrier counters and the abort word start at zero for every launch.
-    err = cudaMemsetAsync(sync, 0, 1152, stream);
+    // Barrier counters, the abort word and both logit accumulators start at
+    // zero for every launch.
+    err = cudaMemsetAsync(sync, 0, stack_sync_bytes(d.n_experts), stream);
     if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)n);

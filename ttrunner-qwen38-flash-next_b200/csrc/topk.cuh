@@ -153,6 +153,60 @@ __device__ __forceinline__ unsigned topk_ord(float f) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+// Top-k of E <= blockDim.x logits (E % 32 == 0, k <= 16) by the whole CTA in a
+// fixed number of steps, whatever the ties: one logit per thread; the block
+// maximum; unique keys (p bits << 32 | ~id) on p = exp(l - l_max); every warp
+// ranks its 32 keys (shuffles) and keeps its k best in rank order; then each of
+// the E/32 * k survivors counts the survivors of the other warps above it
+// (broadcast reads) -- its global rank.  `logit(i)` gives logit i's address.
+// Results: tkv (p values) and tki (ids), descending.  Returns l_max.
+// Scratch (shared): cand[E/32 * k] u64, red[nwarps] u32.
+template <class LogitAt>
+__device__ __forceinline__ float block_topk_ranked(LogitAt logit, int E, int k, unsigned long long* cand,
+                                                   unsigned* red, float* tkv, int* tki) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    float l = -INFINITY;
+    if (tid < E) {
+        l = __ldcg(logit(tid));
+        if (l != l) l = -INFINITY;  // NaN ranks last
+    }
+    const unsigned m = __reduce_max_sync(0xffffffffu, topk_ord(l));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    unsigned mm = 0;
+    for (int w = 0; w < nw; ++w) mm = max(mm, red[w]);
+    const float lmax = __uint_as_float((mm & 0x80000000u) ? (mm & 0x7FFFFFFFu) : ~mm);
+    const unsigned long long key =
+        tid < E ? ((unsigned long long)__float_as_uint(expf(l - lmax)) << 32) | (0xFFFFFFFFu - (unsigned)tid) : 0ull;
+    const unsigned kh = (unsigned)(key >> 32), kl = (unsigned)key;
+    int rank = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const unsigned oh = __shfl_sync(0xffffffffu, kh, j), ol = __shfl_sync(0xffffffffu, kl, j);
+        rank += (oh > kh || (oh == kh && ol > kl)) ? 1 : 0;
+    }
+    const int nl = E >> 5;  // lists: one per warp holding logits
+    if (warp < nl && rank < k) cand[warp * k + rank] = key;
+    __syncthreads();
+    const int nc = nl * k;
+    for (int i = tid; i < nc; i += blockDim.x) {
+        const unsigned long long c = cand[i];
+        const int w = i / k;
+        int r = i - w * k;
+        for (int w2 = 0; w2 < nl; ++w2) {
+            if (w2 == w) continue;
+            const unsigned long long* L = cand + w2 * k;
+            for (int j = 0; j < k; ++j) r += L[j] > c ? 1 : 0;
+        }
+        if (r < k) {
+            tkv[r] = __uint_as_float((unsigned)(c >> 32));
+            tki[r] = (int)(0xFFFFFFFFu - (unsigned)c);
+        }
+    }
+    __syncthreads();
+    return lmax;
+}
+
 static __device__ __noinline__ float block_topk(const float* __restrict__ logits, int E, int k,
                                                 unsigned long long* cand, unsigned long long* wmax,
                                                 unsigned* red, int* cnt, float* tkv, int* tki) {
