@@ -174,6 +174,7 @@ def main() -> None:
     ap.add_argument("--variant", default="B", choices=["A", "B"])
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill timings")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -262,6 +263,7 @@ def main() -> None:
 
     # ---- per-kernel durations for the roofline (eager, events per stage) ----
     stage = stage_timings(pkg, layers, xs[0], M, dev, reps=2)
+    prefill = prefill_timings(pkg, layers[0], cfg, dev) if world == 1 and not args.no_prefill else None
 
     if world > 1:
         t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
@@ -317,6 +319,7 @@ def main() -> None:
                 "frac_of_nominal_8tbs": round(rl_gbs / NOMINAL_HBM_GBS, 4),
             },
             "per_layer_path_stage_us": {k: round(v, 3) for k, v in stage.items()},
+            "prefill_config4": prefill,
             "clocks": clocks,
         }
         if bytes_tok:
@@ -333,6 +336,60 @@ def main() -> None:
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
+
+
+def prefill_timings(pkg, layer, cfg, dev, chunks=(128, 2048), steps: int = 10, warmup: int = 3) -> list:
+    """one layer, chunks of T tokens (x ~ N(0,1) bf16) through the chunked-prefill
+    path (router GEMM + top-k + grouping + tcgen05 grouped GEMMs).  Device time per chunk from CUDA
+    events, split into routing and experts; bytes = the IQ4_XS rows of the experts the chunk touches
+    (+ router), FLOPs = 2 x T x (k + 1) x (2I x D + D x I)."""
+    import torch
+
+    peaks_all = {}
+    pp = ROOT / "MEASURED_PEAKS.json"
+    if pp.exists():
+        try:
+            peaks_all = json.loads(pp.read_text())
+        except ValueError:
+            peaks_all = {}
+    hbm = float(peaks_all.get("hbm_gbs", FALLBACK_HBM_GBS))
+    tflops_peak = float(peaks_all.get("bf16_tflops", 1590.0))
+    ml = pkg.MoELayer(layer)
+    out = []
+    for T in chunks:
+        xs = [pkg.synth_x(cfg, T, seed=5000 + i).to(dev) for i in range(warmup + steps)]
+        ids, _, _ = ml.prefill_route(xs[0])
+        uniq = int(torch.unique(ids).numel())
+        for i in range(warmup):
+            ml.prefill(xs[i])
+        torch.cuda.synchronize(dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record()
+        for i in range(steps):
+            ml.prefill(xs[warmup + i])
+        ev[1].record()
+        torch.cuda.synchronize(dev)
+        us = ev[0].elapsed_time(ev[1]) * 1000.0 / steps
+        # routing alone (router GEMM + top-k), to split the time
+        ev[0].record()
+        for i in range(steps):
+            ml.prefill_route(xs[warmup + i])
+        ev[1].record()
+        torch.cuda.synchronize(dev)
+        us_route = ev[0].elapsed_time(ev[1]) * 1000.0 / steps
+        expert_b = cfg.gate_up_row_bytes * 2 * cfg.inter + cfg.hidden * cfg.down_row_bytes
+        nbytes = (uniq + 1) * expert_b + cfg.router_bytes
+        flops = 2.0 * T * (cfg.top_k + 1) * (2 * cfg.inter * cfg.hidden + cfg.hidden * cfg.inter)
+        out.append({
+            "tokens": T, "us_per_chunk": round(us, 2), "tokens_per_s": round(T / (us * 1e-6), 1),
+            "us_routing": round(us_route, 2), "us_experts": round(us - us_route, 2),
+            "experts_touched": uniq, "bytes": nbytes, "achieved_gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "frac_of_measured_hbm": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4),
+            "tflops": round(flops / (us * 1e-6) / 1e12, 2),
+            "frac_of_measured_bf16": round(flops / (us * 1e-6) / 1e12 / tflops_peak, 4),
+        })
+        del xs
+    return out
 
 
 def stage_timings(pkg, layers, x, M: int, dev, reps: int = 2) -> dict:

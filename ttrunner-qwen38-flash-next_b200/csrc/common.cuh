@@ -36,10 +36,12 @@ struct WsLayout {
 WsLayout ws_layout(const qmoe_dims& d, int max_tokens);
 
 // The stack kernel's zero-initialised words: 8 barrier counters 128 B apart and
-// the abort word (1152 B), then two accumulators of E + 1 router logits, four
+// the abort word (1152 B), then two accumulators of E + 1 router logits, each
+// in kStackLogitReplicas replicas (CTA c adds into replica c % replicas), four
 // logits per 128-byte line so that the CTAs' atomic adds spread over lines.
+constexpr int kStackLogitReplicas = 1;
 inline size_t stack_logit_groups(int E) { return (size_t)(E + 1 + 3) / 4; }
-inline size_t stack_sync_bytes(int E) { return 1152 + 2 * stack_logit_groups(E) * 128; }
+inline size_t stack_sync_bytes(int E) { return 1152 + 2 * (size_t)kStackLogitReplicas * stack_logit_groups(E) * 128; }
 
 // Launch arguments of the routing kernel.
 struct RouteArgs {

@@ -44,6 +44,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_addr(bar))
                  : "memory");
 }
+// 2-D tiled tensor copy (TMA) global -> this CTA's shared memory, completing
+// on `bar`; x is the innermost coordinate (its byte offset a multiple of 16),
+// out-of-range elements read as zero.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
 // 16-byte global -> shared copy through L2 only.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");

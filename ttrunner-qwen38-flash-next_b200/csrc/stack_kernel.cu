@@ -4,18 +4,19 @@
 // over the layers.  Every layer is the reference's `_moe` (reference/model.py
 // :387-417) in two phases separated by grid barriers:
 //
-//   B  every CTA ranks the E router logits itself (block top-k, lower id on
-//      ties) and starts bulk copies (cp.async.bulk, mbarrier completion) of
-//      only its slice of the selected experts' gate|up rows and down rows;
-//      meanwhile it converts x to block floating point and computes its rows
-//      of the shared expert's gate|up (prefetched); routed gate|up rows are
-//      decoded as their 4-pair chunks land -> h slice.
-//   C  the full h (k + 1 slots) -> block floating point; this CTA's output
-//      rows of every selected expert's down (resident since phase B) and of
-//      the shared expert -> out[j] = sum_s w_s D_s[j].h_s + sigmoid(g.x) D_sh[j].h_sh;
-//      then the NEXT layer's router logits restricted to these rows,
-//      sum_j R[e][j] x[j] over this CTA's j (router columns prefetched during
-//      phase B), added into a logit accumulator with vector fp32 atomics.
+//   B  warp 0 ranks the E router logits (warp top-k, lower id on ties) and
+//      starts bulk copies (cp.async.bulk, mbarrier completion) of only this
+//      CTA's slice of the selected experts' gate|up rows and down rows; warps
+//      1-15 meanwhile convert x to block floating point and compute the CTA's
+//      rows of the shared expert's gate|up (prefetched); then all warps decode
+//      routed gate|up rows as their 4-pair chunks land -> h slice.
+//   C  while the next layer's shared rows and router columns stream in (HBM
+//      is otherwise idle here): the full h (k + 1 slots) -> block floating
+//      point; this CTA's output rows of every selected expert's down (resident
+//      since phase B) and of the shared expert, a warp per row ->
+//      out[j] = sum_s w_s D_s[j].h_s + sigmoid(g.x) D_sh[j].h_sh; then the NEXT
+//      layer's router logits restricted to these rows, sum_j R[e][j] x[j] over
+//      this CTA's j, added into a logit accumulator with vector fp32 atomics.
 //
 // The barrier after C therefore publishes both the next layer's input and
 // its complete router logits: two grid barriers per layer.  The router
@@ -28,6 +29,8 @@
 // (%globaltimer): a grid barrier or copy that does not complete sets
 // QMOE_ERR_TIMEOUT and an abort word; every CTA waits (bounded) for its own
 // copies in flight and returns.  No trap, no unbounded spin.
+#include <cuda.h>  // CUtensorMap
+
 #include "common.cuh"
 #include "ptx.cuh"
 #include "topk.cuh"
@@ -37,9 +40,11 @@ namespace {
 
 constexpr int kSKWarps = 16;
 constexpr int kSKThreads = kSKWarps * 32;
-constexpr int kSKChunk = 4;        // routed row pairs per bulk-copy chunk
-constexpr int kSKMaxChunks = 32;
 constexpr unsigned long long kTimeoutNs = 200ull * 1000 * 1000;
+constexpr int kSKChunk = 8;      // routed row pairs per gate|up bulk-copy chunk
+constexpr int kSKMaxChunks = 6;  // chunks of a CTA's pairs (<= 40 pairs per CTA)
+constexpr int kRColW = 20;      // router columns per tensor-copy box (80 B): covers 16 from a 16-byte-aligned start
+constexpr int kRBoxRows = 256;  // router rows per tensor-copy box
 
 struct SKLayer {
     const float* router;
@@ -65,13 +70,17 @@ struct SKArgs {
     int* status;
     int n_layers, D, I, E, K;
     SKLayer L[kSKMaxLayers];
+    // Per layer: the router [E][D] and the gate vector [1][D] as 2-D tensors
+    // for TMA copies of this CTA's column slice (boxes of kRColW columns).
+    CUtensorMap rmap[kSKMaxLayers];
+    CUtensorMap gmap[kSKMaxLayers];
 };
 
 // Shared-memory carve-up (byte offsets), a function of the shape and grid.
 struct SKLayout {
-    int NSQ, NP, NJ, RJ, NCH;
-    unsigned xq, xs, rcol, xo, sgu, sdn, gbuf, ubuf, dbuf, hq, hs, gv, uv, sgv, suv, dpart, cand, red, tkv, tki,
-        misc, issued, bars, total;
+    int NSQ, NP, NJ, RJ;
+    unsigned xq, xs, rcol, xo, sgu, sdn, gbuf, ubuf, dbuf, hq, hs, gv, uv, sgv, suv, cand, wmax, red, tkv, tki, misc, bars,
+        total;
 };
 
 __host__ __device__ constexpr unsigned sk_take(unsigned& o, unsigned bytes) {
@@ -87,12 +96,11 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     s.NSQ = (I + n - 1) / n;
     s.NP = (K * I + n - 1) / n;
     s.NJ = (D + n - 1) / n;
-    s.RJ = s.NJ | 1;  // odd pitch: a warp's 32 router rows hit 32 banks
-    s.NCH = (s.NP + kSKChunk - 1) / kSKChunk;
+    s.RJ = kRColW;  // the tensor-copy box's row pitch
     unsigned o = 0;
     s.xq = sk_take(o, NSB * 64);
     s.xs = sk_take(o, NSB * 4);
-    s.rcol = sk_take(o, (unsigned)(E + 1) * s.RJ * 4);
+    s.rcol = sk_take(o, (unsigned)(((E + kRBoxRows - 1) / kRBoxRows) * kRBoxRows + 1) * kRColW * 4);
     s.xo = sk_take(o, (unsigned)s.NJ * 4);
     s.sgu = sk_take(o, 2u * s.NSQ * RB);
     s.sdn = sk_take(o, (unsigned)s.NJ * DRB);
@@ -105,14 +113,13 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     s.uv = sk_take(o, s.NP * 4);
     s.sgv = sk_take(o, s.NSQ * 4);
     s.suv = sk_take(o, s.NSQ * 4);
-    s.dpart = sk_take(o, (unsigned)s.NJ * (K + 1) * 4);
-    s.cand = sk_take(o, (unsigned)(E / 32) * K * 8);
+    s.cand = sk_take(o, 256 * 8);
+    s.wmax = sk_take(o, (kSKWarps + 1) * 8);
     s.red = sk_take(o, kSKWarps * 4);
     s.tkv = sk_take(o, kMaxTopK * 4);
     s.tki = sk_take(o, kMaxTopK * 4);
     s.misc = sk_take(o, 64);
-    s.issued = sk_take(o, (3 + kSKMaxChunks) * 4);
-    s.bars = sk_take(o, (3 + kSKMaxChunks) * 8);
+    s.bars = sk_take(o, (4 + kSKMaxChunks) * 8);
     s.total = o;
     return s;
 }
@@ -125,7 +132,9 @@ struct SKShape {
     static constexpr int D = D_, E = E_, K = K_, NSM = NSM_, I = 512;
     static constexpr SKLayout S = sk_layout(D_, 512, E_, K_, NSM_);
     static_assert(E_ <= kSKThreads && E_ % 32 == 0, "one router row per thread");
-    static_assert((D_ + NSM_ - 1) / NSM_ <= 16, "router column slice: at most 16 per CTA");
+    static_assert(K_ * 512 / NSM_ + 1 <= 512, "a CTA's routed rows span at most two experts");
+    static_assert((K_ * 512 + NSM_ - 1) / NSM_ <= kSKChunk * (kSKMaxChunks - 1), "chunks of a CTA's pairs");
+    static_assert((D_ + NSM_ - 1) / NSM_ + 3 <= kRColW, "router column slice: one box per CTA");
 };
 
 namespace {
@@ -147,12 +156,21 @@ __device__ bool mbar_wait(uint64_t* bar, uint32_t par) {
 
 __device__ __forceinline__ unsigned* abort_word(unsigned* sync) { return sync + 8 * 32; }
 
-// Phase trace: thread 0 of CTA 0 and of the last CTA stamp their SM's cycle
-// counter (clock64) at each phase boundary.
-__device__ __forceinline__ void trace_mark(const SKArgs& a, int L, int k) {
-    if (a.trace && threadIdx.x == 0) {
+// Phase trace: thread `rec` (0 unless stated) of CTA 0 and of the last CTA
+// stamp their SM's cycle counter (clock64) at each phase boundary.
+__device__ __forceinline__ void trace_mark(const SKArgs& a, int L, int k, int rec = 0) {
+    if (a.trace && (int)threadIdx.x == rec) {
         if (blockIdx.x == 0) a.trace[L * 16 + k] = (unsigned long long)clock64();
         else if (blockIdx.x == gridDim.x - 1) a.trace[(64 + L) * 16 + k] = (unsigned long long)clock64();
+    }
+}
+
+// trace_mark taken only once `dep` has been computed (the clock read consumes it).
+__device__ __forceinline__ void trace_mark_after(const SKArgs& a, int L, int k, unsigned dep) {
+    if (a.trace && threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1)) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%clock64;" : "=l"(t) : "r"(dep));
+        a.trace[(blockIdx.x == 0 ? L : 64 + L) * 16 + k] = t;
     }
 }
 
@@ -231,33 +249,48 @@ __device__ __forceinline__ void convert_block(float v, int* q16, float* step, in
     if (lane == 0) *step = st;
 }
 
-// One (output row, expert slot) down unit, lanes 0-15 or 16-31 of a warp
-// each taking sub-blocks hl, hl+16, ...; returns the lane's share.  hq holds
-// the slot's activation blocks as [word quad v][sub-block t][4 words], so the
-// 16 lanes of a unit read 16 consecutive 16-byte chunks per quad.
-__device__ __forceinline__ float down_unit(const uint8_t* row, const int* hq, const float* hs, int nsbh, int hl) {
-    float acc = 0.0f;
-    for (int t = hl; t < nsbh; t += 16) {
-        const uint8_t* blk = row + (t >> 3) * QMOE_SB_BYTES;
-        const int ib = t & 7;
-        const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
-        const uint2 q0 = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
-        const uint2 q1 = *reinterpret_cast<const uint2*>(blk + 16 + 16 * ib);
-        int xp[16];
+// The activation's block-floating-point words and steps for row_dot: lane l
+// takes sub-blocks l*SBL2 .. l*SBL2+SBL2-1.
+template <int SBL2>
+__device__ __forceinline__ void load_xr(const int* xq, const float* xs, int lane, int (&xr)[SBL2][16],
+                                        float (&xsr)[SBL2]) {
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-            const int4 w4 = *reinterpret_cast<const int4*>(hq + (v * nsbh + t) * 4);
-            xp[4 * v] = w4.x;
-            xp[4 * v + 1] = w4.y;
-            xp[4 * v + 2] = w4.z;
-            xp[4 * v + 3] = w4.w;
+    for (int i = 0; i < SBL2; ++i) {
+        const int b = lane * SBL2 + i;
+        const int4* src = reinterpret_cast<const int4*>(xq + b * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int4 w4 = src[q];
+            xr[i][4 * q] = w4.x;
+            xr[i][4 * q + 1] = w4.y;
+            xr[i][4 * q + 2] = w4.z;
+            xr[i][4 * q + 3] = w4.w;
         }
-        const int Sd = qmoe_subblock_dot(q0.x, q0.y, q1.x, q1.y, xp, 0);
-        const float dl = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu))) *
-                         (float)(qmoe_iq4xs_ls(hdr.x, hdr.y, ib) - 32);
-        acc = fmaf(dl * hs[t], (float)Sd, acc);
+        xsr[i] = xs[b];
     }
-    return acc;
+}
+
+// Sub-block t of one down row dotted with its slot's activation block (hq in
+// the [quad][sub-block][4 words] layout), scaled: d*(ls-32) * step * S.
+__device__ __forceinline__ float down_unit_one(const uint8_t* row, const int* hq, const float* hs, int nsbh, int t) {
+    const uint8_t* blk = row + (t >> 3) * QMOE_SB_BYTES;
+    const int ib = t & 7;
+    const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
+    const uint2 q0 = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
+    const uint2 q1 = *reinterpret_cast<const uint2*>(blk + 16 + 16 * ib);
+    int xp[16];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        const int4 w4 = *reinterpret_cast<const int4*>(hq + (v * nsbh + t) * 4);
+        xp[4 * v] = w4.x;
+        xp[4 * v + 1] = w4.y;
+        xp[4 * v + 2] = w4.z;
+        xp[4 * v + 3] = w4.w;
+    }
+    const int Sd = qmoe_subblock_dot(q0.x, q0.y, q1.x, q1.y, xp, 0);
+    const float dl = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu))) *
+                     (float)(qmoe_iq4xs_ls(hdr.x, hdr.y, ib) - 32);
+    return dl * hs[t] * (float)Sd;
 }
 
 // Shape-derived constants and this CTA's static slices.
@@ -312,21 +345,18 @@ __device__ __forceinline__ void issue_sdn(const SKLayer& W, const SKPart& p, con
     if (nj > 0) ptx::bulk_g2s(sm + S.sdn, W.sh_down + (size_t)p.j_lo * p.DRB, (uint32_t)(nj * p.DRB), bar);
 }
 
-// Router columns j_lo..j_hi of every router row and of the gate vector
-// (row E), 4-byte asynchronous copies: lanes 0-15 take one row, 16-31 the
-// next, so each instruction touches two rows' contiguous slices.
-__device__ __forceinline__ void issue_rcol(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm) {
+// Router columns of this CTA's output rows, for every router row and the gate
+// vector (row E), as 2-D tensor copies (thread 0 only): boxes of kRColW
+// columns from j_lo rounded down to a 16-byte boundary, kRBoxRows rows each;
+// rcol row e at e * kRColW floats, the gate vector after the last box.
+__device__ __forceinline__ void issue_rcol(const CUtensorMap* rmap, const CUtensorMap* gmap, const SKPart& p,
+                                           const SKLayout& S, unsigned char* sm, uint64_t* bar) {
     float* rcol = reinterpret_cast<float*>(sm + S.rcol);
-    const int nj = p.j_hi - p.j_lo, jj = threadIdx.x & 15;
-    if (jj < nj) {
-        for (int e = threadIdx.x >> 4; e <= p.E; e += kSKThreads / 16) {
-            const float* src = (e < p.E ? W.router + (size_t)e * p.D : W.gate_vec) + p.j_lo + jj;
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ptx::smem_addr(rcol + e * S.RJ + jj)),
-                         "l"(src)
-                         : "memory");
-        }
-    }
-    ptx::cp_async_commit();
+    const int nbox = (p.E + kRBoxRows - 1) / kRBoxRows, rows = p.E < kRBoxRows ? p.E : kRBoxRows;
+    const int x = p.j_lo & ~3;
+    mbar_expect_tx(bar, (uint32_t)((nbox * rows + 1) * kRColW * 4));
+    for (int b = 0; b < nbox; ++b) ptx::tma_load_2d(rcol + b * rows * kRColW, rmap, x, b * rows, bar);
+    ptx::tma_load_2d(rcol + nbox * kRBoxRows * kRColW, gmap, x, 0, bar);
 }
 
 // This CTA's share of the router logits: thread e (and thread 0 for the gate
@@ -334,9 +364,10 @@ __device__ __forceinline__ void issue_rcol(const SKLayer& W, const SKPart& p, co
 // combine into one vector atomic add on their accumulator line.
 __device__ __forceinline__ void router_partial(const SKPart& p, const SKLayout& S, const unsigned char* sm,
                                                float* acc_buf) {
-    const float* rcol = reinterpret_cast<const float*>(sm + S.rcol);
     const float* xo = reinterpret_cast<const float*>(sm + S.xo);
+    const float* rcol = reinterpret_cast<const float*>(sm + S.rcol) + (p.j_lo & 3);  // column j_lo of row 0
     const int nj = p.j_hi - p.j_lo, e = threadIdx.x, lane = threadIdx.x & 31;
+    const int gate_row = ((p.E + kRBoxRows - 1) / kRBoxRows) * kRBoxRows;
     float v = 0.0f;
     if (e < p.E)
         for (int j = 0; j < nj; ++j) v = fmaf(rcol[e * S.RJ + j], xo[j], v);
@@ -348,50 +379,70 @@ __device__ __forceinline__ void router_partial(const SKPart& p, const SKLayout& 
                      : "memory");
     if (e == 0) {
         float g = 0.0f;
-        for (int j = 0; j < nj; ++j) g = fmaf(rcol[p.E * S.RJ + j], xo[j], g);
+        for (int j = 0; j < nj; ++j) g = fmaf(rcol[gate_row * S.RJ + j], xo[j], g);
         atomicAdd(acc_buf + (p.E >> 2) * 32 + (p.E & 3), g);
     }
 }
 
-// The selected experts' slices, issued by warp 0: lane 0 first posts every
-// barrier's expected bytes, then lane i issues chunk i's gate|up row copies
-// and, for i < K, expert slot i's down rows.  Chunks are kSKChunk row pairs
-// with their own mbarrier so decoding starts on the first chunk to land.
-__device__ __forceinline__ void issue_routed(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
-                                             const int* ids, uint64_t* bar_ch, uint64_t* bar_dn, int lane) {
-    const int np = p.p_hi - p.p_lo, nj = p.j_hi - p.j_lo;
-    if (lane == 0) {
-        ptx::fence_proxy_async();
-        for (int ch = 0; ch < S.NCH; ++ch) {
-            const int u0 = ch * kSKChunk;
-            const int u1 = (u0 + kSKChunk < np) ? u0 + kSKChunk : np;
-            mbar_expect_tx(bar_ch + ch, u1 > u0 ? (uint32_t)(2 * (u1 - u0) * p.RB) : 0u);
-        }
-        mbar_expect_tx(bar_dn, (uint32_t)(p.K * nj * p.DRB));
+// This CTA's routed pairs [p_lo, p_hi) fall in at most two expert slots: the
+// first len0 pairs in the first.
+__device__ __forceinline__ int seg0_len(const SKPart& p) {
+    const int np = p.p_hi - p.p_lo, r0 = p.p_lo % p.I;
+    return np < p.I - r0 ? np : p.I - r0;
+}
+
+// The selected experts' gate|up rows, issued by warp 0 in chunks of kSKChunk
+// pairs, each chunk with its own mbarrier so decoding starts as the first
+// chunk lands; a chunk that crosses the expert boundary is two pieces.  Lane c
+// posts chunk c's expected bytes; then lane 2q / 2q + 1 copies piece q's gate /
+// up rows (contiguous in the expert).
+__device__ __forceinline__ void issue_gate_up(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
+                                              const int* ids, uint64_t* bar_ch, int lane) {
+    const int np = p.p_hi - p.p_lo, len0 = seg0_len(p);
+    const int nch = (np + kSKChunk - 1) / kSKChunk;
+    if (lane < kSKMaxChunks) {
+        const int u0 = lane * kSKChunk, u1 = min(u0 + kSKChunk, np);
+        mbar_expect_tx(bar_ch + lane, u1 > u0 ? (uint32_t)(2 * (u1 - u0) * p.RB) : 0u);
     }
     __syncwarp();
-    uint8_t* gbuf = sm + S.gbuf;
-    uint8_t* ubuf = sm + S.ubuf;
-    for (int ch = lane; ch < S.NCH; ch += 32) {
-        const int u0 = ch * kSKChunk;
-        const int u1 = (u0 + kSKChunk < np) ? u0 + kSKChunk : np;
-        int u = u0;
-        while (u < u1) {
-            const int pp = p.p_lo + u;
-            const int s = pp / p.I, r = pp - s * p.I;
-            const int seg = (u1 - u) < (p.I - r) ? (u1 - u) : (p.I - r);
-            const uint8_t* eb = W.gate_up + (size_t)ids[s] * p.GUE;
-            ptx::bulk_g2s(gbuf + (size_t)u * p.RB, eb + (size_t)r * p.RB, (uint32_t)(seg * p.RB), bar_ch + ch);
-            ptx::bulk_g2s(ubuf + (size_t)u * p.RB, eb + (size_t)(p.I + r) * p.RB, (uint32_t)(seg * p.RB), bar_ch + ch);
-            u += seg;
+    // piece q: chunk c = the q-th chunk, except that the chunk holding the
+    // boundary contributes two pieces
+    const int cb = len0 < np ? len0 / kSKChunk : nch;  // chunk that contains pair len0 (if len0 is interior)
+    const bool split = len0 < np && len0 % kSKChunk != 0;
+    const int npieces = nch + (split ? 1 : 0);
+    const int q = lane >> 1, up = lane & 1;
+    if (q < npieces) {
+        int c, u0, u1;
+        if (!split || q <= cb) {
+            c = q;
+            u0 = c * kSKChunk;
+            u1 = min(u0 + kSKChunk, np);
+            if (split && q == cb) u1 = len0;  // first piece of the boundary chunk
+        } else {
+            c = q - 1;
+            u0 = c == cb ? len0 : c * kSKChunk;
+            u1 = min(c * kSKChunk + kSKChunk, np);
+        }
+        if (u1 > u0) {
+            const int pp = p.p_lo + u0, s = pp / p.I, r = pp - s * p.I;
+            const uint8_t* src = W.gate_up + (size_t)ids[s] * p.GUE + (size_t)(up ? p.I + r : r) * p.RB;
+            ptx::bulk_g2s(sm + (up ? S.ubuf : S.gbuf) + (size_t)u0 * p.RB, src, (uint32_t)((u1 - u0) * p.RB),
+                          bar_ch + c);
         }
     }
-    if (nj > 0) {
-        uint8_t* dbuf = sm + S.dbuf;
-        for (int s = lane; s < p.K; s += 32)
-            ptx::bulk_g2s(dbuf + (size_t)s * S.NJ * p.DRB, W.down + (size_t)ids[s] * p.DNE + (size_t)p.j_lo * p.DRB,
-                          (uint32_t)(nj * p.DRB), bar_dn);
-    }
+}
+
+// The selected experts' rows of this CTA's output slice of their down, one
+// copy per slot (issued by warp 1 beside warp 0's gate|up copies; needed only
+// in phase C).
+__device__ __forceinline__ void issue_down(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
+                                           const int* ids, uint64_t* bar_dn, int lane) {
+    const int nj = p.j_hi - p.j_lo;
+    if (lane == 0) mbar_expect_tx(bar_dn, (uint32_t)(p.K * nj * p.DRB));
+    __syncwarp();
+    if (lane < p.K && nj > 0)
+        ptx::bulk_g2s(sm + S.dbuf + (size_t)lane * S.NJ * p.DRB,
+                      W.down + (size_t)ids[lane] * p.DNE + (size_t)p.j_lo * p.DRB, (uint32_t)(nj * p.DRB), bar_dn);
 }
 
 template <class SH>
@@ -419,146 +470,130 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     float* uv = reinterpret_cast<float*>(sm + S.uv);
     float* sgv = reinterpret_cast<float*>(sm + S.sgv);
     float* suv = reinterpret_cast<float*>(sm + S.suv);
-    float* dpart = reinterpret_cast<float*>(sm + S.dpart);
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(sm + S.cand);
+    unsigned long long* wmax = reinterpret_cast<unsigned long long*>(sm + S.wmax);
     unsigned* red = reinterpret_cast<unsigned*>(sm + S.red);
     float* tkv = reinterpret_cast<float*>(sm + S.tkv);
     int* tki = reinterpret_cast<int*>(sm + S.tki);
     int* s_ok = reinterpret_cast<int*>(sm + S.misc);
-    float* s_gate = reinterpret_cast<float*>(sm + S.misc) + 4;
+    int* s_cnt = reinterpret_cast<int*>(sm + S.misc) + 8;
+    float* s_glogit = reinterpret_cast<float*>(sm + S.misc) + 12;
+    float* s_psum = reinterpret_cast<float*>(sm + S.misc) + 13;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S.bars);
     uint64_t* bar_sgu = bars;
     uint64_t* bar_sdn = bars + 1;
-    uint64_t* bar_dn = bars + 2;
-    uint64_t* bar_ch = bars + 3;
-    const int nbars = 3 + S.NCH;
+    uint64_t* bar_rc = bars + 2;
+    uint64_t* bar_dn = bars + 3;
+    uint64_t* bar_ch = bars + 4;
+    constexpr int nbars = 4 + kSKMaxChunks;
 
     if (tid == 0) {
         for (int i = 0; i < nbars; ++i) mbar_init(bars + i, 1);
         ptx::fence_mbar_init();
     }
     __syncthreads();
-    // Phases issued per barrier (kept by thread 0), for the bounded drain.
-    int* issued = reinterpret_cast<int*>(sm + S.issued);
+    // Phases issued (kept by thread 0 in registers), for the bounded drain:
+    // the prefetch barriers (shared rows, shared down rows, router columns) and
+    // the per-layer routed copies (chunks and down rows, issued together).
+    int iss_pre = 0, iss_sdn = 0, iss_routed = 0;
     if (tid == 0) {
-        for (int i = 0; i < nbars; ++i) issued[i] = 0;
         issue_sgu(a.L[0], p, S, sm, bar_sgu);
         issue_sdn(a.L[0], p, S, sm, bar_sdn);
-        issued[0] = issued[1] = 1;
+        issue_rcol(&a.rmap[0], &a.gmap[0], p, S, sm, bar_rc);
+        iss_pre = iss_sdn = 1;
     }
 
     // ---------------- prologue: layer 0's router logits --------------------
-    issue_rcol(a.L[0], p, S, sm);
     if (tid < nj) xo[tid] = __bfloat162float(a.x[p.j_lo + tid]);
-    ptx::cp_async_wait<0>();
-    __syncthreads();
-    router_partial(p, S, sm, a.logits);
+    bool ok = !__syncthreads_or(!mbar_wait(bar_rc, 0));
+    if (ok) router_partial(p, S, sm, a.logits + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32);
+    else if (tid == 0) {
+        record_status(a.status, QMOE_ERR_TIMEOUT);
+        atomicExch(abort_word(a.sync), 1u);
+    }
     unsigned gen = 0;
-    bool ok = grid_sync(a.sync, ++gen, a.status, s_ok);
+    ok = grid_sync(a.sync, ++gen, a.status, s_ok) && ok;
 
     for (int L = 0; L < a.n_layers && ok; ++L) {
         const SKLayer& W = a.L[L];
         const uint32_t par = (uint32_t)(L & 1);
         const bool last = L + 1 == a.n_layers;
-        const float* lg = a.logits + (size_t)(L & 1) * G * 32;
-        float* lg_next = a.logits + (size_t)((L + 1) & 1) * G * 32;
+        const float* lg = a.logits + (size_t)(L & 1) * kStackLogitReplicas * G * 32;
+        float* lg_next = a.logits + (size_t)((L + 1) & 1) * kStackLogitReplicas * G * 32;
 
         // ---------------- phase B: top-k, gate|up ----------------------------
         trace_mark(a, L, 0);
-        // x loads first (they complete under the top-k): thread t holds
-        // elements t + 512 k4, i.e. lane `lane` of blocks warp + 16 k4.
-        float v[4];
+        // x loads, then the selection's logit loads; x converts to block
+        // floating point while the logits are in flight (each warp 4 blocks).
+        constexpr int NXB = D / 32, XPW = (NXB + kSKWarps - 1) / kSKWarps;
+        float xv[XPW];
 #pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-            const int i = tid + k4 * kSKThreads;
-            v[k4] = 0.0f;
-            if (i < D)
-                v[k4] = L == 0 ? __bfloat162float(a.x[i]) : __bfloat162float(__float2bfloat16_rn(__ldcg(a.act + i)));
+        for (int i = 0; i < XPW; ++i) {
+            const int b = warp + i * kSKWarps;
+            xv[i] = 0.0f;
+            if (b < NXB)
+                xv[i] = L == 0 ? __bfloat162float(a.x[b * 32 + lane])
+                               : __bfloat162float(__float2bfloat16_rn(__ldcg(a.act + b * 32 + lane)));
         }
-        const float lmax =
-            block_topk_ranked([&](int i) { return lg + (i >> 2) * 32 + (i & 3); }, E, K, cand, red, tkv, tki);
+        if (tid == 0) *s_glogit = __ldcg(lg + (E >> 2) * 32 + (E & 3));
+        const float lmax = block_topk_threshold(
+            [&](int i) { return __ldcg(lg + (i >> 2) * 32 + (i & 3)); }, E, K, cand, wmax, red, s_cnt, tkv, tki,
+            s_psum, [&]() {
+#pragma unroll
+                for (int i = 0; i < XPW; ++i) {
+                    const int b = warp + i * kSKWarps;
+                    if (b < NXB) convert_block(xv[i], xq + b * 16, xs + b, lane);
+                }
+            });
         trace_mark(a, L, 1);
+        // Warps 0 and 1 issue the routed copies; the others stay off the
+        // shared-memory pipe meanwhile (traffic there slows the issue).
         if (warp == 0) {
-            const float e = lane < K ? tkv[lane] : 0.0f;
-            const float sum = warp_sum(e);
-            if (lane < K) tkv[lane] = e / sum;
             if (lane == 0) {
-                *s_gate = sigmoid(__ldcg(lg + (E >> 2) * 32 + (E & 3)));
+                ptx::fence_proxy_async();
                 if (!(fabsf(lmax) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
             }
-            issue_routed(W, p, S, sm, tki, bar_ch, bar_dn, lane);
-            if (tid == 0)
-                for (int i = 2; i < nbars; ++i) ++issued[i];
-        }
-        trace_mark(a, L, 2);
-        // x -> block floating point (each warp its own 4 blocks, from registers)
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-            const int b = warp + k4 * kSKWarps;
-            if (b * 32 < D) convert_block(v[k4], xq + b * 16, xs + b, lane);
-        }
-        // CTA 0 clears the other logit accumulator for the next layer's sums
-        // (read last in the previous layer's phase B; first added to after
-        // this layer's second barrier).
-        if (blockIdx.x == 0 && !last)
-            for (int g = tid; g < G; g += kSKThreads)
+            issue_gate_up(W, p, S, sm, tki, bar_ch, lane);
+            if (tid == 0) ++iss_routed;
+            trace_mark(a, L, 2);
+        } else if (warp == 1) {
+            if (lane == 0) ptx::fence_proxy_async();
+            issue_down(W, p, S, sm, tki, bar_dn, lane);
+            trace_mark(a, L, 3, 32);
+        } else if (blockIdx.x == 0 && !last) {
+            // CTA 0 clears the other logit accumulator for the next layer's sums
+            // (read last in the previous layer's phase B; first added to after
+            // this layer's second barrier).
+            for (int g = tid - 64; g < kStackLogitReplicas * G; g += kSKThreads - 64)
                 *reinterpret_cast<float4*>(lg_next + g * 32) = make_float4(0.f, 0.f, 0.f, 0.f);
-        __syncthreads();
-        int xr[SBL2][16];
-        float xsr[SBL2];
-#pragma unroll
-        for (int i = 0; i < SBL2; ++i) {
-            const int b = lane * SBL2 + i;
-            const int4* src = reinterpret_cast<const int4*>(xq + b * 16);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int4 w4 = src[q];
-                xr[i][4 * q] = w4.x;
-                xr[i][4 * q + 1] = w4.y;
-                xr[i][4 * q + 2] = w4.z;
-                xr[i][4 * q + 3] = w4.w;
-            }
-            xsr[i] = xs[b];
-        }
-        trace_mark(a, L, 3);
-        // shared expert gate|up rows (prefetched)
-        {
-            const bool w_ok = mbar_wait(bar_sgu, par);
-            if (__syncthreads_or(!w_ok)) {
-                if (tid == 0) {
-                    record_status(a.status, QMOE_ERR_TIMEOUT);
-                    atomicExch(abort_word(a.sync), 1u);
-                }
-                ok = false;
-                break;
-            }
-        }
-        for (int t = warp; t < 2 * nsq; t += kSKWarps) {
-            const uint8_t* row = sgu + (size_t)((t & 1) ? (S.NSQ + (t >> 1)) : (t >> 1)) * p.RB;
-            const float r = row_dot<SBL2>(row, xr, xsr, lane);
-            if (lane == 0) ((t & 1) ? suv : sgv)[t >> 1] = r;
         }
         __syncthreads();
-        if (!last) {
-            // The next layer's shared rows and router columns stream in behind.
-            if (tid == 0) {
-                ptx::fence_proxy_async();
-                issue_sgu(a.L[L + 1], p, S, sm, bar_sgu);
-                ++issued[0];
-            }
-            issue_rcol(a.L[L + 1], p, S, sm);
-        }
         trace_mark(a, L, 4);
-        // routed gate|up rows as their chunks land
-        for (int t = warp; t < 2 * np; t += kSKWarps) {
-            const int u = t >> 1;
-            if (!mbar_wait(bar_ch + u / kSKChunk, par)) {
-                ok = false;
-                break;
+        {
+            int xr[SBL2][16];
+            float xsr[SBL2];
+            load_xr<SBL2>(xq, xs, lane, xr, xsr);
+            // Row tasks: the shared expert's 2 * nsq rows (prefetched), then the
+            // routed pairs' gate and up rows as their chunks land.
+            const bool w_ok = mbar_wait(bar_sgu, par);
+            const int ns = 2 * nsq;
+            for (int t = warp; t < ns + 2 * np && ok && w_ok; t += kSKWarps) {
+                if (t < ns) {
+                    const uint8_t* row = sgu + (size_t)((t & 1) ? (S.NSQ + (t >> 1)) : (t >> 1)) * p.RB;
+                    const float r = row_dot<SBL2>(row, xr, xsr, lane);
+                    if (lane == 0) ((t & 1) ? suv : sgv)[t >> 1] = r;
+                } else {
+                    const int tt = t - ns, u = tt >> 1;
+                    if (!mbar_wait(bar_ch + u / kSKChunk, par)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint8_t* row = ((tt & 1) ? ubuf : gbuf) + (size_t)u * p.RB;
+                    const float r = row_dot<SBL2>(row, xr, xsr, lane);
+                    if (lane == 0) ((tt & 1) ? uv : gv)[u] = r;
+                }
             }
-            const uint8_t* row = ((t & 1) ? ubuf : gbuf) + (size_t)u * p.RB;
-            const float r = row_dot<SBL2>(row, xr, xsr, lane);
-            if (lane == 0) ((t & 1) ? uv : gv)[u] = r;
+            if (!w_ok) ok = false;
         }
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
@@ -579,6 +614,14 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
         trace_mark(a, L, 7);
 
         // ---------------- phase C: down + combine, next layer's logits -------
+        // The next layer's shared rows and router columns stream in now, while
+        // HBM is otherwise idle (their buffers were last read before the barrier).
+        if (!last && tid == 0) {
+            ptx::fence_proxy_async();
+            issue_sgu(a.L[L + 1], p, S, sm, bar_sgu);
+            issue_rcol(&a.rmap[L + 1], &a.gmap[L + 1], p, S, sm, bar_rc);
+            ++iss_pre;
+        }
         {
             const int nbh = (K + 1) * p.NSBH;
             constexpr int NB = 12;
@@ -606,8 +649,8 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
         __syncthreads();
         trace_mark(a, L, 8);
         {
-            const bool w_ok = mbar_wait(bar_dn, par) && mbar_wait(bar_sdn, par);
-            if (__syncthreads_or(!w_ok)) {
+            const bool d_ok = mbar_wait(bar_dn, par) && mbar_wait(bar_sdn, par);
+            if (__syncthreads_or(!d_ok)) {
                 if (tid == 0) {
                     record_status(a.status, QMOE_ERR_TIMEOUT);
                     atomicExch(abort_word(a.sync), 1u);
@@ -617,43 +660,43 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             }
         }
         trace_mark(a, L, 9);
-        {
-            // (output row j, expert slot s) per half-warp; slot K is the shared expert
-            const int K1 = K + 1, nu = nj * K1, half = lane >> 4, hl = lane & 15;
-            for (int u0 = 2 * warp; u0 < nu; u0 += 2 * kSKWarps) {
-                const int u = u0 + half;
-                float acc = 0.0f;
-                if (u < nu) {
-                    const int j = u / K1, s = u - j * K1;
-                    const uint8_t* row = s < K ? dbuf + ((size_t)s * S.NJ + j) * p.DRB : sdn + (size_t)j * p.DRB;
-                    acc = down_unit(row, hq + s * p.NSBH * 16, hs + s * p.NSBH, p.NSBH, hl);
-                }
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                if (u < nu && hl == 0) dpart[u] = acc;
+        // Down + combine: a warp per output row j; its lanes walk the row's
+        // (slot, sub-block) pairs of all k + 1 slots with the slot weight folded
+        // in, so one reduction per row.  Slot K is the shared expert.
+        const float inv_psum = 1.0f / *s_psum, gate = sigmoid(*s_glogit);
+        for (int j = warp; j < nj; j += kSKWarps) {
+            float acc = 0.0f;
+            constexpr int NT = (K + 1) * (I / 32);
+            for (int t = lane; t < NT; t += 32) {
+                const int s = t / (I / 32), b = t - s * (I / 32);
+                const uint8_t* row = s < K ? dbuf + ((size_t)s * S.NJ + j) * p.DRB : sdn + (size_t)j * p.DRB;
+                const float wgt = s < K ? tkv[s] * inv_psum : gate;
+                acc += wgt * down_unit_one(row, hq + s * p.NSBH * 16, hs + s * p.NSBH, p.NSBH, b);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) {
+                (last ? a.out : a.act)[p.j_lo + j] = acc;
+                xo[j] = __bfloat162float(__float2bfloat16_rn(acc));
             }
         }
-        __syncthreads();
-        trace_mark(a, L, 10);
-        for (int j = tid; j < nj; j += kSKThreads) {
-            const float* dp = dpart + j * (K + 1);
-            float o = 0.0f;
-            for (int s = 0; s < K; ++s) o = fmaf(tkv[s], dp[s], o);
-            o = fmaf(*s_gate, dp[K], o);
-            (last ? a.out : a.act)[p.j_lo + j] = o;
-            xo[j] = __bfloat162float(__float2bfloat16_rn(o));
+        // the next layer's router columns
+        if (__syncthreads_or(!last && !mbar_wait(bar_rc, (uint32_t)((L + 1) & 1)))) {
+            if (tid == 0) {
+                record_status(a.status, QMOE_ERR_TIMEOUT);
+                atomicExch(abort_word(a.sync), 1u);
+            }
+            ok = false;
+            break;
         }
-        if (!last) ptx::cp_async_wait<0>();  // this thread's router-column copies
-        __syncthreads();
+        trace_mark(a, L, 10);
         if (tid == 0 && !last) {
             ptx::fence_proxy_async();
             issue_sdn(a.L[L + 1], p, S, sm, bar_sdn);
-            ++issued[1];
+            ++iss_sdn;
         }
-        trace_mark(a, L, 11);
         if (!last) {
-            router_partial(p, S, sm, lg_next);
-            trace_mark(a, L, 12);
+            router_partial(p, S, sm, lg_next + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32);
+            trace_mark(a, L, 11);
             if (!grid_sync(a.sync, ++gen, a.status, s_ok)) {
                 ok = false;
                 break;
@@ -662,10 +705,17 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     }
 
     // Stopped early: let this CTA's copies in flight land (bounded) before exit.
-    ptx::cp_async_wait<0>();
     if (!ok && tid == 0) {
-        for (int i = 0; i < nbars; ++i)
-            if (issued[i] > 0) (void)mbar_wait(bars + i, (uint32_t)((issued[i] - 1) & 1));
+        if (iss_pre > 0) {
+            (void)mbar_wait(bar_sgu, (uint32_t)((iss_pre - 1) & 1));
+            (void)mbar_wait(bar_rc, (uint32_t)((iss_pre - 1) & 1));
+        }
+        if (iss_sdn > 0) (void)mbar_wait(bar_sdn, (uint32_t)((iss_sdn - 1) & 1));
+        if (iss_routed > 0) {
+            const uint32_t q = (uint32_t)((iss_routed - 1) & 1);
+            (void)mbar_wait(bar_dn, q);
+            for (int c = 0; c < kSKMaxChunks; ++c) (void)mbar_wait(bar_ch + c, q);
+        }
     }
 }
 
@@ -690,6 +740,40 @@ void (*pick_kernel(const qmoe_dims& d, int n_sm, unsigned* smem))(SKArgs) {
 }
 
 }  // namespace
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (EncodeTiledFn) nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// fp32 [rows][cols] row-major (cols * 4 bytes a multiple of 16, base 16-byte
+// aligned) as a 2-D tensor with boxes of kRColW columns x min(rows, kRBoxRows)
+// rows; reads past the last column return zeros.
+static cudaError_t encode_rows_map(CUtensorMap* m, const float* base, int cols, int rows) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)kRColW, (cuuint32_t)(rows < kRBoxRows ? rows : kRBoxRows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
 
 bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers) {
     if (M != 1 || n_layers < 1 || n_layers > kSKMaxLayers) return false;
@@ -731,6 +815,11 @@ cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* lo
     unsigned smem = 0;
     void (*kern)(SKArgs) = pick_kernel(d, n, &smem);
     if (!kern) return cudaErrorInvalidValue;
+    for (int l = 0; l < n_layers; ++l) {
+        cudaError_t e = encode_rows_map(&a.rmap[l], layers[l].router, d.hidden, d.n_experts);
+        if (e == cudaSuccess) e = encode_rows_map(&a.gmap[l], layers[l].gate_vec, d.hidden, 1);
+        if (e != cudaSuccess) return e;
+    }
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     // Barrier counters, the abort word and both logit accumulators start at

@@ -138,104 +138,55 @@ static __device__ __noinline__ float warp_topk(const float* __restrict__ logits,
 
 namespace qmoe {
 
-// Top-k of E <= 2 * blockDim.x logits by the whole CTA (k <= blockDim.x / 32),
-// same selection rule as warp_topk: rank p_i = exp(l_i - l_max) descending,
-// lower id on ties, via unique 64-bit keys (p bits << 32 | ~id).
-//   1. block max of the logits (order-preserving integer keys, redux.sync);
-//   2. each warp's largest key; T0 = the k-th largest warp maximum, which is
-//      not above the k-th largest key overall (k distinct keys reach it);
-//   3. keys >= T0 are the candidates (k..~2k for distinct logits, up to all
-//      of them for a long run of ties), each ranked against all candidates.
-// Results in tkv (p values) and tki (ids), descending.  Returns l_max.
-// Scratch (shared): cand[max(E, nwarps * k)] u64, wmax[nwarps + 1] u64, red[nwarps] u32, cnt.
+// Order-preserving map of a float to an unsigned integer (for redux.sync max).
 __device__ __forceinline__ unsigned topk_ord(float f) {
     const unsigned b = __float_as_uint(f);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// Top-k of E <= blockDim.x logits (E % 32 == 0, k <= 16) by the whole CTA in a
-// fixed number of steps, whatever the ties: one logit per thread; the block
-// maximum; unique keys (p bits << 32 | ~id) on p = exp(l - l_max); every warp
-// ranks its 32 keys (shuffles) and keeps its k best in rank order; then each of
-// the E/32 * k survivors counts the survivors of the other warps above it
-// (broadcast reads) -- its global rank.  `logit(i)` gives logit i's address.
-// Results: tkv (p values) and tki (ids), descending.  Returns l_max.
-// Scratch (shared): cand[E/32 * k] u64, red[nwarps] u32.
-template <class LogitAt>
-__device__ __forceinline__ float block_topk_ranked(LogitAt logit, int E, int k, unsigned long long* cand,
-                                                   unsigned* red, float* tkv, int* tki) {
+// Top-k of E logits (E <= blockDim.x, E a multiple of the warp count, k <= 16)
+// by the whole CTA in a fixed number of steps.  Same selection rule as
+// warp_topk: unique keys (p bits << 32 | ~id) on p = exp(l - l_max).  Thread
+// (warp w, lane l) holds expert l * nw + w, so every warp sees experts spread
+// over the whole id range:
+//   1. the block maximum of the logits;
+//   2. each warp's largest key; T0 = the k-th largest of the nw warp maxima.
+//      Every member of the top k is >= T0 (k distinct keys reach it);
+//   3. keys >= T0 are the candidates: about k for distinct probabilities, and
+//      still about k when many tie (each warp's maximum is then its lowest
+//      tied id, so T0 is the k-th lowest tied id); each candidate is ranked
+//      against all, up to 256 of them; beyond that (adversarial ties), k
+//      rounds of block arg-max.
+// `logit(i)` loads logit i (from L2: it is read once); `between()` runs while
+// the loads are in flight.  Shared scratch: cand[256] u64, wmax[nw + 1] u64,
+// red[nw] u32, cnt (int).  Writes tkv (p values, not normalised), tki (ids),
+// descending, and *psum = their sum; returns l_max.  Every thread of the CTA
+// must call it.
+template <class LogitAt, class Between>
+__device__ __forceinline__ float block_topk_threshold(LogitAt logit, int E, int k, unsigned long long* cand,
+                                                      unsigned long long* wmax, unsigned* red, int* cnt, float* tkv,
+                                                      int* tki, float* psum, Between between) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int e = lane * nw + warp;
     float l = -INFINITY;
-    if (tid < E) {
-        l = __ldcg(logit(tid));
-        if (l != l) l = -INFINITY;  // NaN ranks last
-    }
+    if (e < E) l = logit(e);
+    between();  // caller's work that overlaps the logit loads
+    if (l != l) l = -INFINITY;  // NaN ranks last
     const unsigned m = __reduce_max_sync(0xffffffffu, topk_ord(l));
     if (lane == 0) red[warp] = m;
+    if (tid == 0) {
+        *cnt = 0;
+        *psum = 0.0f;
+    }
     __syncthreads();
     unsigned mm = 0;
     for (int w = 0; w < nw; ++w) mm = max(mm, red[w]);
     const float lmax = __uint_as_float((mm & 0x80000000u) ? (mm & 0x7FFFFFFFu) : ~mm);
     const unsigned long long key =
-        tid < E ? ((unsigned long long)__float_as_uint(expf(l - lmax)) << 32) | (0xFFFFFFFFu - (unsigned)tid) : 0ull;
+        e < E ? ((unsigned long long)__float_as_uint(expf(l - lmax)) << 32) | (0xFFFFFFFFu - (unsigned)e) : 0ull;
     const unsigned kh = (unsigned)(key >> 32), kl = (unsigned)key;
-    int rank = 0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const unsigned oh = __shfl_sync(0xffffffffu, kh, j), ol = __shfl_sync(0xffffffffu, kl, j);
-        rank += (oh > kh || (oh == kh && ol > kl)) ? 1 : 0;
-    }
-    const int nl = E >> 5;  // lists: one per warp holding logits
-    if (warp < nl && rank < k) cand[warp * k + rank] = key;
-    __syncthreads();
-    const int nc = nl * k;
-    for (int i = tid; i < nc; i += blockDim.x) {
-        const unsigned long long c = cand[i];
-        const int w = i / k;
-        int r = i - w * k;
-        for (int w2 = 0; w2 < nl; ++w2) {
-            if (w2 == w) continue;
-            const unsigned long long* L = cand + w2 * k;
-            for (int j = 0; j < k; ++j) r += L[j] > c ? 1 : 0;
-        }
-        if (r < k) {
-            tkv[r] = __uint_as_float((unsigned)(c >> 32));
-            tki[r] = (int)(0xFFFFFFFFu - (unsigned)c);
-        }
-    }
-    __syncthreads();
-    return lmax;
-}
-
-static __device__ __noinline__ float block_topk(const float* __restrict__ logits, int E, int k,
-                                                unsigned long long* cand, unsigned long long* wmax,
-                                                unsigned* red, int* cnt, float* tkv, int* tki) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = blockDim.x, nw = nt >> 5;
-    float l0 = -INFINITY, l1 = -INFINITY;
-    if (tid < E) {
-        l0 = __ldcg(logits + tid);
-        if (l0 != l0) l0 = -INFINITY;
-    }
-    if (tid + nt < E) {
-        l1 = __ldcg(logits + tid + nt);
-        if (l1 != l1) l1 = -INFINITY;
-    }
-    unsigned m = __reduce_max_sync(0xffffffffu, max(topk_ord(l0), topk_ord(l1)));
-    if (lane == 0) red[warp] = m;
-    if (tid == 0) *cnt = 0;
-    __syncthreads();
-    unsigned mm = 0;
-    for (int w = 0; w < nw; ++w) mm = max(mm, red[w]);
-    const float lmax = __uint_as_float((mm & 0x80000000u) ? (mm & 0x7FFFFFFFu) : ~mm);
-    const int i0 = tid, i1 = tid + nt;
-    const unsigned long long k0 =
-        i0 < E ? ((unsigned long long)__float_as_uint(expf(l0 - lmax)) << 32) | (0xFFFFFFFFu - (unsigned)i0) : 0ull;
-    const unsigned long long k1 =
-        i1 < E ? ((unsigned long long)__float_as_uint(expf(l1 - lmax)) << 32) | (0xFFFFFFFFu - (unsigned)i1) : 0ull;
-    const unsigned long long best = k0 > k1 ? k0 : k1;
-    const unsigned hi = (unsigned)(best >> 32), lo = (unsigned)best;
-    const unsigned mh = __reduce_max_sync(0xffffffffu, hi);
-    const unsigned ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+    const unsigned mh = __reduce_max_sync(0xffffffffu, kh);
+    const unsigned ml = __reduce_max_sync(0xffffffffu, kh == mh ? kl : 0u);
     if (lane == 0) wmax[warp] = ((unsigned long long)mh << 32) | ml;
     __syncthreads();
     if (tid < nw) {
@@ -246,62 +197,48 @@ static __device__ __noinline__ float block_topk(const float* __restrict__ logits
     }
     __syncthreads();
     const unsigned long long T0 = wmax[nw];
-    if (i0 < E && k0 >= T0) cand[atomicAdd(cnt, 1)] = k0;
-    if (i1 < E && k1 >= T0) cand[atomicAdd(cnt, 1)] = k1;
+    const bool is_c = e < E && key >= T0;
+    const unsigned bal = __ballot_sync(0xffffffffu, is_c);
+    int base = 0;
+    if (lane == 0 && bal) base = atomicAdd(cnt, __popc(bal));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    const int pos = base + __popc(bal & ((1u << lane) - 1u));
+    if (is_c && pos < 256) cand[pos] = key;
     __syncthreads();
     const int C = *cnt;
-    if (C <= 64) {
-        for (int c = tid; c < C; c += nt) {
-            const unsigned long long v = cand[c];
+    if (C <= 256) {
+        for (int i = tid; i < C; i += blockDim.x) {
+            const unsigned long long ci = cand[i];
             int r = 0;
-            for (int j = 0; j < C; ++j) r += cand[j] > v ? 1 : 0;
+            for (int j = 0; j < C; ++j) r += cand[j] > ci ? 1 : 0;
             if (r < k) {
-                tkv[r] = __uint_as_float((unsigned)(v >> 32));
-                tki[r] = (int)(0xFFFFFFFFu - (unsigned)v);
+                const float pv = __uint_as_float((unsigned)(ci >> 32));
+                tkv[r] = pv;
+                tki[r] = (int)(0xFFFFFFFFu - (unsigned)ci);
+                atomicAdd(psum, pv);
             }
         }
         __syncthreads();
         return lmax;
     }
-    // Many candidates: a long run of equal probabilities (activations small
-    // enough that exp rounds them together).  Each warp extracts its own top
-    // k by k rounds of warp arg-max (no block barrier), then warp 0 merges the
-    // nw * k survivors the same way -- cost independent of the ties.
-    unsigned long long a0 = i0 < E ? k0 : 0ull, a1 = i1 < E ? k1 : 0ull;
+    // Adversarial ties: k rounds of block arg-max over the keys.
+    unsigned long long mine = key;
     for (int r = 0; r < k; ++r) {
-        const unsigned long long b = a0 > a1 ? a0 : a1;
-        const unsigned bh = (unsigned)(b >> 32), bl = (unsigned)b;
-        const unsigned wh = __reduce_max_sync(0xffffffffu, bh);
-        const unsigned wl = __reduce_max_sync(0xffffffffu, bh == wh ? bl : 0u);
-        const unsigned long long m = ((unsigned long long)wh << 32) | wl;
-        if (lane == 0) cand[warp * k + r] = m;
-        if (a0 == m) a0 = 0ull;
-        if (a1 == m) a1 = 0ull;
-    }
-    __syncthreads();
-    if (warp == 0) {
-        const int n = nw * k;  // <= 16 * 16 = 256: up to 8 per lane
-        unsigned long long c[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) c[j] = (lane + 32 * j) < n ? cand[lane + 32 * j] : 0ull;
-        for (int r = 0; r < k; ++r) {
-            unsigned long long b = 0ull;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) b = c[j] > b ? c[j] : b;
-            const unsigned bh = (unsigned)(b >> 32), bl = (unsigned)b;
-            const unsigned wh = __reduce_max_sync(0xffffffffu, bh);
-            const unsigned wl = __reduce_max_sync(0xffffffffu, bh == wh ? bl : 0u);
-            const unsigned long long m = ((unsigned long long)wh << 32) | wl;
-            if (lane == 0) {
-                tkv[r] = __uint_as_float(wh);
-                tki[r] = (int)(0xFFFFFFFFu - wl);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (c[j] == m) c[j] = 0ull;
+        const unsigned h = (unsigned)(mine >> 32), lo = (unsigned)mine;
+        const unsigned wh = __reduce_max_sync(0xffffffffu, h);
+        const unsigned wl = __reduce_max_sync(0xffffffffu, h == wh ? lo : 0u);
+        if (lane == 0) cand[warp] = ((unsigned long long)wh << 32) | wl;
+        __syncthreads();
+        unsigned long long best = 0ull;
+        for (int w = 0; w < nw; ++w) best = cand[w] > best ? cand[w] : best;
+        if (tid == 0) {
+            tkv[r] = __uint_as_float((unsigned)(best >> 32));
+            tki[r] = (int)(0xFFFFFFFFu - (unsigned)best);
+            *psum += tkv[r];
         }
+        if (mine == best) mine = 0ull;
+        __syncthreads();
     }
-    __syncthreads();
     return lmax;
 }
 

@@ -43,9 +43,9 @@ class MoEStack:
     def n_layers(self) -> int:
         return len(self.layers)
 
-    TRACE_POINTS = ("B start", "top-k done", "copies issued", "x converted", "shared gate|up done",
-                    "routed gate|up done", "h written", "after barrier H", "h converted", "down resident",
-                    "down done", "combined", "router partial done", "-", "-", "-")
+    TRACE_POINTS = ("B start", "top-k done", "gate|up copies issued", "down copies issued (warp 1)",
+                    "copies done", "gate|up rows done", "h written", "after barrier H", "h converted",
+                    "down resident", "down done", "router partial done", "-", "-", "-", "-")
 
     def phase_trace(self, m: int = 1):
         """Raw SM cycle-counter stamps of the last single-launch step,
