@@ -39,9 +39,14 @@ WsLayout ws_layout(const qmoe_dims& d, int max_tokens);
 // the abort word (1152 B), then two accumulators of E + 1 router logits, each
 // in kStackLogitReplicas replicas (CTA c adds into replica c % replicas), four
 // logits per 128-byte line so that the CTAs' atomic adds spread over lines.
+// After them, two buffers of per-32-value block maxima of h (|h| bits, for
+// atomicMax), one per layer parity, one word per 128-byte line.
 constexpr int kStackLogitReplicas = 1;
+constexpr int kStackHmaxBlocks = (kMaxTopK + 1) * 16;     // (k + 1) slots x 512 / 32 blocks
+constexpr int kStackHmaxWords = kStackHmaxBlocks * 32;    // a line per block
 inline size_t stack_logit_groups(int E) { return (size_t)(E + 1 + 3) / 4; }
-inline size_t stack_sync_bytes(int E) { return 1152 + 2 * (size_t)kStackLogitReplicas * stack_logit_groups(E) * 128; }
+inline size_t stack_logit_bytes(int E) { return 2 * (size_t)kStackLogitReplicas * stack_logit_groups(E) * 128; }
+inline size_t stack_sync_bytes(int E) { return 1152 + stack_logit_bytes(E) + 2 * kStackHmaxWords * 4; }
 
 // Launch arguments of the routing kernel.
 struct RouteArgs {

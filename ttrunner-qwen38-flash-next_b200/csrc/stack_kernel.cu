@@ -62,7 +62,8 @@ constexpr int kSKMaxLayers = 64;
 struct SKArgs {
     const __nv_bfloat16* x;  // [D] layer-0 input
     float* out;              // [D] last layer's output
-    float* act;              // [D] layer activation (workspace)
+    __nv_bfloat16* act;      // [D] layer activation, bf16 (workspace)
+    unsigned* hmax;          // two buffers of per-block max |h| bits (workspace)
     float* logits;           // two accumulators of G lines x 32 floats (logits 4g..4g+3 at a line's front)
     float* h;                // [(K + 1) * I] (workspace)
     unsigned* sync;          // 8 counters, 128 B apart, then the abort word
@@ -166,10 +167,10 @@ __device__ __forceinline__ void trace_mark(const SKArgs& a, int L, int k, int re
 }
 
 // trace_mark taken only once `dep` has been computed (the clock read consumes it).
-__device__ __forceinline__ void trace_mark_after(const SKArgs& a, int L, int k, unsigned dep) {
+__device__ __forceinline__ void trace_mark_after(const SKArgs& a, int L, int k, unsigned long long dep) {
     if (a.trace && threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1)) {
         unsigned long long t;
-        asm volatile("mov.u64 %0, %%clock64;" : "=l"(t) : "r"(dep));
+        asm volatile("mov.u64 %0, %%clock64;" : "=l"(t) : "l"(dep));
         a.trace[(blockIdx.x == 0 ? L : 64 + L) * 16 + k] = t;
     }
 }
@@ -239,6 +240,27 @@ __device__ __forceinline__ float row_dot(const uint8_t* row, const int (&xr)[SBL
         acc = fmaf(dl * xs[i], (float)S, acc);
     }
     return warp_sum(acc);
+}
+
+// Block floating point of a 32-value block given its largest |v| as float
+// bits (the same step and rounding as warp_block_fp): the pair word of
+// values j and j + 16 (v0, v1) and, in *step, the block's step.
+__device__ __forceinline__ int block_fp_pair(float v0, float v1, unsigned mb, float* step) {
+    const int E = (int)(mb >> 23);
+    int q0 = 0, q1 = 0;
+    float st = 0.0f;
+    if (E >= 255) {
+        st = __uint_as_float(0x7fc00000u);
+    } else if (E >= 1) {
+        const int k = 140 - E, k1 = k >> 1, k2 = k - k1;
+        const float s1 = __uint_as_float((unsigned)(127 + k1) << 23);
+        const float s2 = __uint_as_float((unsigned)(127 + k2) << 23);
+        q0 = __float2int_rn((v0 * s1) * s2);
+        q1 = __float2int_rn((v1 * s1) * s2);
+        st = E >= 14 ? __uint_as_float((unsigned)(E - 13) << 23) : __uint_as_float(1u << (E + 9));
+    }
+    *step = st;
+    return (q0 & 0xFFFF) | (q1 << 16);
 }
 
 // One 32-value block to block floating point, lane j holding value j.
@@ -478,7 +500,6 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     int* s_ok = reinterpret_cast<int*>(sm + S.misc);
     int* s_cnt = reinterpret_cast<int*>(sm + S.misc) + 8;
     float* s_glogit = reinterpret_cast<float*>(sm + S.misc) + 12;
-    float* s_psum = reinterpret_cast<float*>(sm + S.misc) + 13;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S.bars);
     uint64_t* bar_sgu = bars;
     uint64_t* bar_sdn = bars + 1;
@@ -533,18 +554,20 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             xv[i] = 0.0f;
             if (b < NXB)
                 xv[i] = L == 0 ? __bfloat162float(a.x[b * 32 + lane])
-                               : __bfloat162float(__float2bfloat16_rn(__ldcg(a.act + b * 32 + lane)));
+                               : __bfloat162float(__ushort_as_bfloat16(
+                                     __ldcg(reinterpret_cast<const unsigned short*>(a.act) + b * 32 + lane)));
         }
         if (tid == 0) *s_glogit = __ldcg(lg + (E >> 2) * 32 + (E & 3));
         const float lmax = block_topk_threshold(
             [&](int i) { return __ldcg(lg + (i >> 2) * 32 + (i & 3)); }, E, K, cand, wmax, red, s_cnt, tkv, tki,
-            s_psum, [&]() {
+            [&]() {
 #pragma unroll
                 for (int i = 0; i < XPW; ++i) {
                     const int b = warp + i * kSKWarps;
                     if (b < NXB) convert_block(xv[i], xq + b * 16, xs + b, lane);
                 }
-            });
+            },
+            [&](int pt, unsigned long long d) { trace_mark_after(a, L, 12 + pt, d); });
         trace_mark(a, L, 1);
         // Warps 0 and 1 issue the routed copies; the others stay off the
         // shared-memory pipe meanwhile (traffic there slows the issue).
@@ -604,8 +627,34 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             break;
         }
         trace_mark(a, L, 5);
-        for (int u = tid; u < np; u += kSKThreads) a.h[p.p_lo + u] = silu(gv[u]) * uv[u];
-        if (tid < nsq) a.h[(size_t)K * I + p.sq_lo + tid] = silu(sgv[tid]) * suv[tid];
+        {
+            // h slice and its blocks' running max |h| (bits of non-negative
+            // floats order like unsigned integers; NaN above infinity)
+            // Each warp reduces first: one atomic per block a warp's 32 h
+            // values touch (at most three).
+            unsigned* hm = a.hmax + (L & 1) * kStackHmaxWords;
+            const int n_h = np + nsq;  // routed slice, then the shared slice
+            for (int i0 = warp * 32; i0 < n_h; i0 += kSKThreads) {
+                const int i = i0 + lane;
+                int hidx = -1;
+                float v = 0.0f;
+                if (i < np) {
+                    v = silu(gv[i]) * uv[i];
+                    hidx = p.p_lo + i;
+                } else if (i < n_h) {
+                    v = silu(sgv[i - np]) * suv[i - np];
+                    hidx = K * I + p.sq_lo + (i - np);
+                }
+                if (hidx >= 0) a.h[hidx] = v;
+                const unsigned bits = hidx >= 0 ? __float_as_uint(fabsf(v)) : 0u;
+                const int b = hidx >= 0 ? hidx >> 5 : -1;
+                // lanes grouped by block (up to three groups where the routed
+                // slice meets the shared one); one atomic per group
+                const unsigned grp = __match_any_sync(0xffffffffu, b);
+                const unsigned m = __reduce_max_sync(grp, bits);
+                if (b >= 0 && lane == __ffs(grp) - 1) atomicMax(hm + b * 32, m);
+            }
+        }
         trace_mark(a, L, 6);
         if (!grid_sync(a.sync, ++gen, a.status, s_ok)) {
             ok = false;
@@ -623,28 +672,41 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             ++iss_pre;
         }
         {
-            const int nbh = (K + 1) * p.NSBH;
-            constexpr int NB = 12;
-            for (int b0 = warp; b0 < nbh; b0 += NB * kSKWarps) {
-                float hv[NB];
+            // h -> block floating point with the producers' block maxima: lanes
+            // 0-15 / 16-31 take one block each, element l and l + 16 per lane.
+            const unsigned* hm = a.hmax + (L & 1) * kStackHmaxWords;
+            constexpr int NBH = (K + 1) * (I / 32), NIT = (NBH + 2 * kSKWarps - 1) / (2 * kSKWarps);
+            const int half = lane >> 4, hl = lane & 15;
+            float v0[NIT], v1[NIT];
+            unsigned mb[NIT];
 #pragma unroll
-                for (int i = 0; i < NB; ++i) {
-                    const int b = b0 + i * kSKWarps;
-                    hv[i] = b < nbh ? __ldcg(a.h + (size_t)b * 32 + lane) : 0.0f;
-                }
-#pragma unroll
-                for (int i = 0; i < NB; ++i) {
-                    const int b = b0 + i * kSKWarps;
-                    if (b < nbh) {
-                        float st;
-                        const int pw = warp_block_fp(hv[i], &st);
-                        const int slot = b / p.NSBH, t = b - slot * p.NSBH;
-                        // word w = 4*quad + (w & 3) of block t of the slot
-                        if (lane < 16) hq[slot * p.NSBH * 16 + ((lane >> 2) * p.NSBH + t) * 4 + (lane & 3)] = pw;
-                        if (lane == 0) hs[b] = st;
-                    }
+            for (int i = 0; i < NIT; ++i) {
+                const int b = warp + kSKWarps * (2 * i + half);
+                v0[i] = v1[i] = 0.0f;
+                mb[i] = 0u;
+                if (b < NBH) {
+                    v0[i] = __ldcg(a.h + (size_t)b * 32 + hl);
+                    v1[i] = __ldcg(a.h + (size_t)b * 32 + 16 + hl);
+                    mb[i] = __ldcg(hm + b * 32);
                 }
             }
+#pragma unroll
+            for (int i = 0; i < NIT; ++i) {
+                const int b = warp + kSKWarps * (2 * i + half);
+                if (b < NBH) {
+                    float st;
+                    const int pw = block_fp_pair(v0[i], v1[i], mb[i], &st);
+                    const int slot = b / (I / 32), t = b - slot * (I / 32);
+                    // word w = 4*quad + (w & 3) of block t of the slot
+                    hq[slot * p.NSBH * 16 + ((hl >> 2) * p.NSBH + t) * 4 + (hl & 3)] = pw;
+                    if (hl == 0) hs[b] = st;
+                }
+            }
+            // CTA 0 clears the other block-maximum buffer for the next layer
+            // (read last in the previous layer's phase C).
+            if (blockIdx.x == 0 && !last)
+                for (int i = tid; i < kStackHmaxBlocks; i += kSKThreads)
+                    a.hmax[((L + 1) & 1) * kStackHmaxWords + i * 32] = 0u;
         }
         __syncthreads();
         trace_mark(a, L, 8);
@@ -663,7 +725,9 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
         // Down + combine: a warp per output row j; its lanes walk the row's
         // (slot, sub-block) pairs of all k + 1 slots with the slot weight folded
         // in, so one reduction per row.  Slot K is the shared expert.
-        const float inv_psum = 1.0f / *s_psum, gate = sigmoid(*s_glogit);
+        float psum = 0.0f;
+        for (int s2 = 0; s2 < K; ++s2) psum += tkv[s2];
+        const float inv_psum = 1.0f / psum, gate = sigmoid(*s_glogit);
         for (int j = warp; j < nj; j += kSKWarps) {
             float acc = 0.0f;
             constexpr int NT = (K + 1) * (I / 32);
@@ -675,8 +739,10 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             }
             acc = warp_sum(acc);
             if (lane == 0) {
-                (last ? a.out : a.act)[p.j_lo + j] = acc;
-                xo[j] = __bfloat162float(__float2bfloat16_rn(acc));
+                const __nv_bfloat16 xb = __float2bfloat16_rn(acc);
+                if (last) a.out[p.j_lo + j] = acc;
+                else a.act[p.j_lo + j] = xb;
+                xo[j] = __bfloat162float(xb);
             }
         }
         // the next layer's router columns
@@ -793,8 +859,9 @@ cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* lo
     a.trace = trace;
     a.x = reinterpret_cast<const __nv_bfloat16*>(x);
     a.out = out;
-    a.act = act;
+    a.act = reinterpret_cast<__nv_bfloat16*>(act);
     a.logits = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(sync) + 1152);
+    a.hmax = reinterpret_cast<unsigned*>(reinterpret_cast<unsigned char*>(sync) + 1152 + stack_logit_bytes(d.n_experts));
     a.h = h;
     a.sync = sync;
     a.status = status;
@@ -822,8 +889,8 @@ cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* lo
     }
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    // Barrier counters, the abort word and both logit accumulators start at
-    // zero for every launch.
+    // Barrier counters, the abort word, both logit accumulators and both
+    // block-maximum buffers start at zero for every launch.
     err = cudaMemsetAsync(sync, 0, stack_sync_bytes(d.n_experts), stream);
     if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg{};

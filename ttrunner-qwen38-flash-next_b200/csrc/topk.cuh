@@ -138,6 +138,10 @@ static __device__ __noinline__ float warp_topk(const float* __restrict__ logits,
 
 namespace qmoe {
 
+struct NoStamp {
+    __device__ void operator()(int, unsigned long long = 0) const {}
+};
+
 // Order-preserving map of a float to an unsigned integer (for redux.sync max).
 __device__ __forceinline__ unsigned topk_ord(float f) {
     const unsigned b = __float_as_uint(f);
@@ -159,25 +163,23 @@ __device__ __forceinline__ unsigned topk_ord(float f) {
 //      rounds of block arg-max.
 // `logit(i)` loads logit i (from L2: it is read once); `between()` runs while
 // the loads are in flight.  Shared scratch: cand[256] u64, wmax[nw + 1] u64,
-// red[nw] u32, cnt (int).  Writes tkv (p values, not normalised), tki (ids),
-// descending, and *psum = their sum; returns l_max.  Every thread of the CTA
-// must call it.
-template <class LogitAt, class Between>
+// red[nw] u32, cnt (int).  Writes tkv (p values, not normalised) and tki
+// (ids), descending; returns l_max.  Every thread of the CTA must call it.
+template <class LogitAt, class Between, class Stamp = NoStamp>
 __device__ __forceinline__ float block_topk_threshold(LogitAt logit, int E, int k, unsigned long long* cand,
                                                       unsigned long long* wmax, unsigned* red, int* cnt, float* tkv,
-                                                      int* tki, float* psum, Between between) {
+                                                      int* tki, Between between, Stamp stamp = Stamp()) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int e = lane * nw + warp;
     float l = -INFINITY;
     if (e < E) l = logit(e);
+    stamp(0, (unsigned long long)__float_as_uint(l));
     between();  // caller's work that overlaps the logit loads
+    stamp(1, 0ull);
     if (l != l) l = -INFINITY;  // NaN ranks last
     const unsigned m = __reduce_max_sync(0xffffffffu, topk_ord(l));
     if (lane == 0) red[warp] = m;
-    if (tid == 0) {
-        *cnt = 0;
-        *psum = 0.0f;
-    }
+    if (tid == 0) *cnt = 0;
     __syncthreads();
     unsigned mm = 0;
     for (int w = 0; w < nw; ++w) mm = max(mm, red[w]);
@@ -197,6 +199,7 @@ __device__ __forceinline__ float block_topk_threshold(LogitAt logit, int E, int 
     }
     __syncthreads();
     const unsigned long long T0 = wmax[nw];
+    stamp(2, T0);
     const bool is_c = e < E && key >= T0;
     const unsigned bal = __ballot_sync(0xffffffffu, is_c);
     int base = 0;
@@ -212,13 +215,12 @@ __device__ __forceinline__ float block_topk_threshold(LogitAt logit, int E, int 
             int r = 0;
             for (int j = 0; j < C; ++j) r += cand[j] > ci ? 1 : 0;
             if (r < k) {
-                const float pv = __uint_as_float((unsigned)(ci >> 32));
-                tkv[r] = pv;
+                tkv[r] = __uint_as_float((unsigned)(ci >> 32));
                 tki[r] = (int)(0xFFFFFFFFu - (unsigned)ci);
-                atomicAdd(psum, pv);
             }
         }
         __syncthreads();
+        stamp(3, 0ull);
         return lmax;
     }
     // Adversarial ties: k rounds of block arg-max over the keys.
@@ -234,7 +236,6 @@ __device__ __forceinline__ float block_topk_threshold(LogitAt logit, int E, int 
         if (tid == 0) {
             tkv[r] = __uint_as_float((unsigned)(best >> 32));
             tki[r] = (int)(0xFFFFFFFFu - (unsigned)best);
-            *psum += tkv[r];
         }
         if (mine == best) mine = 0ull;
         __syncthreads();

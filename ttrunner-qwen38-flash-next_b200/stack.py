@@ -45,7 +45,8 @@ class MoEStack:
 
     TRACE_POINTS = ("B start", "top-k done", "gate|up copies issued", "down copies issued (warp 1)",
                     "copies done", "gate|up rows done", "h written", "after barrier H", "h converted",
-                    "down resident", "down done", "router partial done", "-", "-", "-", "-")
+                    "down resident", "down done", "router partial done", "top-k: logits loaded", "top-k: x converted",
+                    "top-k: threshold found", "top-k: ranked")
 
     def phase_trace(self, m: int = 1):
         """Raw SM cycle-counter stamps of the last single-launch step,
