@@ -22,6 +22,7 @@
 
 #include "common.cuh"
 #include "ptx.cuh"
+#include "tma_host.cuh"
 #include "topk.cuh"
 
 namespace qmoe {
@@ -72,6 +73,16 @@ struct GemmArgs {
     const int* meta;         // meta[0]: number of n-tiles
     float* out;              // [T][D]
     int* status;
+    // This mode's weights as 2-D uint16 tensors [rows][row bytes / 2]: the
+    // routed experts' (rows of all experts stacked) and the shared expert's.
+    // A stage is boxes of 136 elements (272 bytes: two super-blocks) x 64
+    // rows (gate|up: a gate box and an up box) or x 128 rows (down).
+    CUtensorMap wmap;
+    CUtensorMap shmap;
+    // B operand rows as a bf16 tensor [slot rows][K] (the expert-sorted copy of x
+    // for gate|up, h for down), boxes of 64 columns x 128 rows in the 128-byte
+    // swizzle layout the MMA descriptors read.
+    CUtensorMap bmap;
 };
 
 struct PfSmem {
@@ -220,7 +231,6 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
     const int K = a.mode == 0 ? a.D : a.I;
     const int nslots = K / kGSlotK;
     const int n_tiles = __ldg(a.meta) * MT;
-    const int RB = (K / 256) * QMOE_SB_BYTES;  // bytes of one weight row
 
     if (warp == kWLoad) {
         // ---- IQ4_XS stage producer: 128 rows x 272 bytes per stage --------
@@ -235,14 +245,23 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                     ok = false;
                     break;
                 }
-                if (lane == 0) ptx::mbar_expect_tx(S.iq_full(st), kGStageBytes);
-                __syncwarp();
-                uint8_t* dst = S.stage(st);
-                for (int m = lane; m < kGM; m += 32) {
-                    const int wrow = a.mode == 0 ? ((m & 1) ? a.I : 0) + ti.mt * 64 + (m >> 1) : ti.mt * kGM + m;
-                    ptx::bulk_g2s(dst + m * kGStageRowB, ti.w + (size_t)wrow * RB + kst * kGStageRowB, kGStageRowB,
-                                  S.iq_full(st));
+                if (lane == 0) {
+                    // gate|up: gate rows mt*64.. -> stage rows 0-63, up rows -> 64-127;
+                    // down: rows mt*128.. -> stage rows 0-127
+                    const CUtensorMap* map = ti.g < a.E ? &a.wmap : &a.shmap;
+                    const int rows_per_e = a.mode == 0 ? 2 * a.I : a.D;
+                    const int y0 = (ti.g < a.E ? ti.g * rows_per_e : 0) + ti.mt * (a.mode == 0 ? 64 : kGM);
+                    const int x = kst * (kGStageRowB / 2);
+                    ptx::mbar_expect_tx(S.iq_full(st), kGStageBytes);
+                    uint8_t* dst = S.stage(st);
+                    if (a.mode == 0) {
+                        ptx::tma_load_2d(dst, map, x, y0, S.iq_full(st));
+                        ptx::tma_load_2d(dst + 64 * kGStageRowB, map, x, y0 + a.I, S.iq_full(st));
+                    } else {
+                        ptx::tma_load_2d(dst, map, x, y0, S.iq_full(st));
+                    }
                 }
+                __syncwarp();
                 last_issue[st] = st_it;
                 ++st_it;
             }
@@ -254,47 +273,29 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                     (void)pf_wait(S.iq_full(s), (last_issue[s] / kGStages) & 1, abort_flag, a.status, false);
         }
     } else if (warp == kWGather) {
-        // ---- B operand gather: N token rows x 128 bytes per slot ----------
-        int it = 0, prev = -1;
-        bool ok = true;
-        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-            const TileInfo ti = tile_info(a, t, MT);
-            const int c = lane & 7;
-            for (int ks = 0; ks < nslots; ++ks) {
-                const int slot = it % kGSlots;
-                if (!pf_wait_warp(S.s_empty(slot), ((it / kGSlots) & 1) ^ 1, abort_flag, a.status)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* dst = S.b_slot(slot);
-                for (int n = lane >> 3; n < ti.cnt; n += 4) {
-                    const __nv_bfloat16* src;
-                    if (a.mode == 0) {
-                        const int tok = __ldg(a.slot_tok + ti.row0 + n);
-                        if ((unsigned)tok >= (unsigned)a.T) continue;  // never: slot rows hold valid tokens
-                        src = a.x + (size_t)tok * a.D + ks * kGSlotK + c * 8;
-                    } else {
-                        src = a.h + (size_t)(ti.row0 + n) * a.I + ks * kGSlotK + c * 8;
+        // ---- B operand: one 2-D tensor copy per slot (64 K x 128 rows) -----
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const TileInfo ti = tile_info(a, t, MT);
+                for (int ks = 0; ks < nslots; ++ks) {
+                    const int slot = it % kGSlots;
+                    if (!pf_wait(S.s_empty(slot), ((it / kGSlots) & 1) ^ 1, abort_flag, a.status)) {
+                        ok = false;
+                        break;
                     }
-                    ptx::cp_async16(dst + sw128_off(n, c), src);
+                    ptx::mbar_expect_tx(S.s_full(slot), kGSlotBytes);
+                    ptx::tma_load_2d(S.b_slot(slot), &a.bmap, ks * kGSlotK, ti.row0, S.s_full(slot));
+                    ++it;
                 }
-                ptx::cp_async_commit();
-                if (prev >= 0) {
-                    ptx::cp_async_wait<1>();
-                    ptx::fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive(S.s_full(prev));
-                }
-                prev = slot;
-                ++it;
             }
+            // the last slots' copies land before the CTA leaves (bounded)
+            if (!ok)
+                for (int j = 1; j <= kGSlots && it - j >= 0; ++j)
+                    (void)pf_wait(S.s_full((it - j) % kGSlots), ((it - j) / kGSlots) & 1, abort_flag, a.status, false);
         }
-        ptx::cp_async_wait<0>();
-        if (prev >= 0 && ok) {
-            ptx::fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(S.s_full(prev));
-        }
+        __syncwarp();
     } else if (warp == kWMma) {
         // ---- MMA issue: one thread --------------------------------------
         if (lane == 0) {
@@ -357,7 +358,9 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                     break;
                 }
                 const int sbk = (ks & 7) * 2 + sub;  // sub-block of the row within the stage (0..15)
-                const uint8_t* blk = S.stage(st) + m * kGStageRowB + (sbk >> 3) * QMOE_SB_BYTES;
+                // stage row of M row m: gate|up stages hold the gate box then the up box
+                const int srow = a.mode == 0 ? ((m & 1) ? 64 + (m >> 1) : (m >> 1)) : m;
+                const uint8_t* blk = S.stage(st) + srow * kGStageRowB + (sbk >> 3) * QMOE_SB_BYTES;
                 const int ib = sbk & 7;
                 const uint2 hd = *reinterpret_cast<const uint2*>(blk);
                 const uint2 qa = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
@@ -429,6 +432,21 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
 }
 
 // ---- router, top-k, grouping -------------------------------------------------
+
+// xg[r] = x[slot_tok[r]] for every slot row r < meta[1] (bf16 rows of D): the
+// gate|up B operand in expert-sorted order, so each tile's token rows are one
+// contiguous box.
+__global__ void __launch_bounds__(256) pf_gather_kernel(const __nv_bfloat16* __restrict__ x, int D,
+                                                        const int* __restrict__ slot_tok, const int* __restrict__ meta,
+                                                        int T, __nv_bfloat16* __restrict__ xg) {
+    const int r = blockIdx.x;
+    if (r >= __ldg(meta + 1)) return;
+    const int tok = __ldg(slot_tok + r);
+    if ((unsigned)tok >= (unsigned)T) return;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok * D);
+    uint4* dst = reinterpret_cast<uint4*>(xg + (size_t)r * D);
+    for (int i = threadIdx.x; i < D / 8; i += blockDim.x) dst[i] = __ldg(src + i);
+}
 
 // bf16 copy of the activations (fp32 input is rounded to bf16, the activation
 // dtype between layers).
@@ -645,7 +663,7 @@ __global__ void __launch_bounds__(kPlaceWarps * 32) pf_place_kernel(const int32_
 // ---- workspace and launches ---------------------------------------------------
 
 struct PfLayout {
-    size_t status, meta, xb, logits, ids, weights, slog, counts, offsets, ntiles, slot_tok, slot_w, h, total;
+    size_t status, meta, xb, logits, ids, weights, slog, counts, offsets, ntiles, slot_tok, slot_w, h, xg, total;
     int max_ntiles, rows;
 };
 
@@ -682,6 +700,8 @@ PfLayout pf_layout(const qmoe_dims& d, int T) {
     o = pf_align(o + (size_t)L.rows * 4);
     L.h = o;
     o = pf_align(o + (size_t)L.rows * d.inter * 2);
+    L.xg = o;
+    o = pf_align(o + (size_t)L.rows * d.hidden * 2);
     L.total = o;
     return L;
 }
@@ -785,11 +805,34 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     err = cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemBytes);
     if (err != cudaSuccess) return err;
     const int n_sm = device_sm_count();
+    const unsigned long long rb = (unsigned long long)(d.hidden / 256) * QMOE_SB_BYTES;
+    const unsigned long long drb = (unsigned long long)(d.inter / 256) * QMOE_SB_BYTES;
+    __nv_bfloat16* xg = reinterpret_cast<__nv_bfloat16*>(ws + L.xg);
+    pf_gather_kernel<<<(unsigned)L.rows, 256, 0, s>>>(xb, d.hidden, slot_tok, meta, T, xg);
     a.mode = 0;
+    err = encode_2d(&a.bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xg, (unsigned long long)d.hidden,
+                    (unsigned long long)L.rows, (unsigned long long)d.hidden * 2, kGSlotK, kGNMax,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+    if (err != cudaSuccess) return err;
+    err = encode_2d(&a.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.gate_up, rb / 2, (unsigned long long)E * 2 * d.inter, rb,
+                    kGStageRowB / 2, 64);
+    if (err == cudaSuccess && has_shared)
+        err = encode_2d(&a.shmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.sh_gate_up, rb / 2, 2ull * d.inter, rb,
+                        kGStageRowB / 2, 64);
+    if (err != cudaSuccess) return err;
     grouped_gemm_kernel<<<(unsigned)n_sm, kGThreads, kGSmemBytes, s>>>(a);
     err = cudaMemsetAsync(out, 0, (size_t)T * d.hidden * 4, s);
     if (err != cudaSuccess) return err;
     a.mode = 1;
+    err = encode_2d(&a.bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, h, (unsigned long long)d.inter, (unsigned long long)L.rows,
+                    (unsigned long long)d.inter * 2, kGSlotK, kGNMax, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (err != cudaSuccess) return err;
+    err = encode_2d(&a.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.down, drb / 2, (unsigned long long)E * d.hidden, drb,
+                    kGStageRowB / 2, kGM);
+    if (err == cudaSuccess && has_shared)
+        err = encode_2d(&a.shmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.sh_down, drb / 2, (unsigned long long)d.hidden,
+                        drb, kGStageRowB / 2, kGM);
+    if (err != cudaSuccess) return err;
     grouped_gemm_kernel<<<(unsigned)n_sm, kGThreads, kGSmemBytes, s>>>(a);
     return cudaGetLastError();
 }

@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "ptx.cuh"
+#include "tma_host.cuh"
 #include "topk.cuh"
 
 namespace qmoe {
@@ -807,38 +808,12 @@ void (*pick_kernel(const qmoe_dims& d, int n_sm, unsigned* smem))(SKArgs) {
 
 }  // namespace
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
-// against the driver library).
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_tiled() {
-    static EncodeTiledFn fn = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (EncodeTiledFn) nullptr;
-        return reinterpret_cast<EncodeTiledFn>(p);
-    }();
-    return fn;
-}
-
 // fp32 [rows][cols] row-major (cols * 4 bytes a multiple of 16, base 16-byte
 // aligned) as a 2-D tensor with boxes of kRColW columns x min(rows, kRBoxRows)
 // rows; reads past the last column return zeros.
 static cudaError_t encode_rows_map(CUtensorMap* m, const float* base, int cols, int rows) {
-    EncodeTiledFn fn = encode_tiled();
-    if (!fn) return cudaErrorNotSupported;
-    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
-    const cuuint32_t box[2] = {(cuuint32_t)kRColW, (cuuint32_t)(rows < kRBoxRows ? rows : kRBoxRows)};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+    return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, (unsigned long long)cols, (unsigned long long)rows,
+                     (unsigned long long)cols * 4, kRColW, (unsigned)(rows < kRBoxRows ? rows : kRBoxRows));
 }
 
 bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers) {
