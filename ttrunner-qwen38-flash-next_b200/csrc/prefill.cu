@@ -29,30 +29,37 @@ namespace qmoe {
 namespace {
 
 constexpr int kPfMaxTokens = 8192;
+constexpr int kPfTraceSlots = 64;
+constexpr size_t kPfTraceBytes = kPfTraceSlots * 8 * 8;
 constexpr unsigned long long kPfTimeoutNs = 1000ull * 1000 * 1000;
 
 // ---- grouped GEMM geometry --------------------------------------------------
 constexpr int kGM = 128;            // MMA M: weight rows per tile
-constexpr int kGNMax = 128;         // tokens per n-tile (MMA N, padded to 16)
+constexpr int kGNMax = 64;          // tokens per n-tile (MMA N, padded to 16)
 constexpr int kGSlotK = 64;         // K per operand slot: one 128-byte swizzle row of bf16
-constexpr int kGSlots = 4;          // operand ring depth
+constexpr int kGSlots = 4;          // A (expanded weights) ring depth
+constexpr int kGBSlots = 8;         // B (token rows) ring depth: its copies run further ahead
 constexpr int kGStageK = 512;       // K per IQ4_XS stage: two super-blocks of every row
 constexpr int kGStageRowB = 2 * QMOE_SB_BYTES;  // 272 bytes of one row per stage
 constexpr int kGStages = 2;
-constexpr int kGSlotBytes = kGM * kGSlotK * 2;  // 16 KB (A and B slots alike: N <= 128)
+constexpr int kGSlotBytes = kGM * kGSlotK * 2;      // 16 KB A slot
+constexpr int kGBSlotBytes = kGNMax * kGSlotK * 2;  // 8 KB B slot
 constexpr int kGStageBytes = kGM * kGStageRowB;  // 34,816
-constexpr int kGTmemCols = 256;     // two accumulator buffers of 128 columns
+constexpr int kGTmemCols = 2 * kGNMax;  // two accumulator buffers
 // warp roles
-constexpr int kWLoad = 0, kWGather = 1, kWMma = 2, kWDq0 = 3, kNDq = 8, kWEp0 = 11, kNEp = 4;
-constexpr int kGWarps = kWEp0 + kNEp;  // 15
+// Dequant: two groups of kNDqG warps; group g expands the slots whose running
+// index is g mod 2, so two slots are expanded at once.
+constexpr int kNDqG = 8, kNDqGroups = 2;
+constexpr int kWLoad = 0, kWGather = 1, kWMma = 2, kWDq0 = 3, kNDq = kNDqG * kNDqGroups, kWEp0 = kWDq0 + kNDq, kNEp = 4;
+constexpr int kGWarps = kWEp0 + kNEp;  // 23
 constexpr int kGThreads = kGWarps * 32;
 
 // shared-memory carve-up from a 1024-aligned base
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kGSlots * kGSlotBytes;
-constexpr int kOffStage = kOffB + kGSlots * kGSlotBytes;
+constexpr int kOffStage = kOffB + kGBSlots * kGBSlotBytes;
 constexpr int kOffBars = kOffStage + kGStages * kGStageBytes;
-constexpr int kNBars = 2 * kGStages + 2 * kGSlots + 2 * 2 + 1;
+constexpr int kNBars = 2 * kGStages + 2 * kGSlots + 2 * kGBSlots + 2 * 2 + 1;
 constexpr int kOffMisc = kOffBars + kNBars * 8;
 constexpr int kGSmemBytes = kOffMisc + 64 + 1024;  // + slack to align the base
 static_assert(kOffStage % 1024 == 0 && kOffB % 1024 == 0, "operand tiles must be 1024-aligned");
@@ -73,6 +80,7 @@ struct GemmArgs {
     const int* meta;         // meta[0]: number of n-tiles
     float* out;              // [T][D]
     int* status;
+    unsigned long long* trace;  // CTA 0's per-slot clock stamps [64 slots][8] (workspace)
     // This mode's weights as 2-D uint16 tensors [rows][row bytes / 2]: the
     // routed experts' (rows of all experts stacked) and the shared expert's.
     // A stage is boxes of 136 elements (272 bytes: two super-blocks) x 64
@@ -89,15 +97,17 @@ struct PfSmem {
     unsigned char* base;
     uint64_t* bars;
     __device__ uint8_t* a_slot(int s) const { return base + kOffA + s * kGSlotBytes; }
-    __device__ uint8_t* b_slot(int s) const { return base + kOffB + s * kGSlotBytes; }
+    __device__ uint8_t* b_slot(int s) const { return base + kOffB + s * kGBSlotBytes; }
     __device__ uint8_t* stage(int s) const { return base + kOffStage + s * kGStageBytes; }
     __device__ uint64_t* iq_full(int s) const { return bars + s; }
     __device__ uint64_t* iq_empty(int s) const { return bars + kGStages + s; }
     __device__ uint64_t* s_full(int s) const { return bars + 2 * kGStages + s; }
     __device__ uint64_t* s_empty(int s) const { return bars + 2 * kGStages + kGSlots + s; }
-    __device__ uint64_t* acc_full(int b) const { return bars + 2 * kGStages + 2 * kGSlots + b; }
-    __device__ uint64_t* acc_empty(int b) const { return bars + 2 * kGStages + 2 * kGSlots + 2 + b; }
-    __device__ uint64_t* fin() const { return bars + 2 * kGStages + 2 * kGSlots + 4; }
+    __device__ uint64_t* b_full(int s) const { return bars + 2 * kGStages + 2 * kGSlots + s; }
+    __device__ uint64_t* b_empty(int s) const { return bars + 2 * kGStages + 2 * kGSlots + kGBSlots + s; }
+    __device__ uint64_t* acc_full(int b) const { return bars + 2 * kGStages + 2 * kGSlots + 2 * kGBSlots + b; }
+    __device__ uint64_t* acc_empty(int b) const { return bars + 2 * kGStages + 2 * kGSlots + 2 * kGBSlots + 2 + b; }
+    __device__ uint64_t* fin() const { return bars + 2 * kGStages + 2 * kGSlots + 2 * kGBSlots + 4; }
     __device__ uint32_t* tmem_holder() const { return reinterpret_cast<uint32_t*>(base + kOffMisc); }
     __device__ volatile int* abort_flag() const { return reinterpret_cast<volatile int*>(base + kOffMisc + 16); }
 };
@@ -110,8 +120,8 @@ __device__ bool pf_wait(uint64_t* bar, uint32_t par, volatile int* abort_flag, i
     if (ptx::mbar_test(bar, par)) return true;
     const unsigned long long t0 = ptx::now_ns();
     for (unsigned it = 0;; ++it) {
-        if (ptx::mbar_test(bar, par)) return true;
-        if ((it & 63u) == 63u) {
+        if (ptx::mbar_test_sleep(bar, par, 20000u)) return true;
+        if ((it & 3u) == 3u) {
             if (honour_abort && *abort_flag) return false;
             if (ptx::now_ns() - t0 > kPfTimeoutNs) {
                 *abort_flag = 1;
@@ -125,6 +135,12 @@ __device__ bool pf_wait(uint64_t* bar, uint32_t par, volatile int* abort_flag, i
 __device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, uint32_t par, volatile int* abort_flag, int* status) {
     const bool ok = pf_wait(bar, par, abort_flag, status);
     return __all_sync(0xffffffffu, ok);
+}
+
+// CTA 0 stamps its SM clock for slot `it` (< kPfTraceSlots), event k.
+__device__ __forceinline__ void pf_stamp(const GemmArgs& a, int it, int k) {
+    if (a.trace && blockIdx.x == 0 && it < kPfTraceSlots)
+        a.trace[it * 8 + k] = (unsigned long long)clock64();
 }
 
 struct TileInfo {
@@ -207,8 +223,12 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
             ptx::mbar_init(S.iq_empty(s), kNDq);
         }
         for (int s = 0; s < kGSlots; ++s) {
-            ptx::mbar_init(S.s_full(s), kNDq + 1);
+            ptx::mbar_init(S.s_full(s), kNDqG);
             ptx::mbar_init(S.s_empty(s), 1);
+        }
+        for (int s = 0; s < kGBSlots; ++s) {
+            ptx::mbar_init(S.b_full(s), 1);
+            ptx::mbar_init(S.b_empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
             ptx::mbar_init(S.acc_full(b), 1);
@@ -262,6 +282,7 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                     }
                 }
                 __syncwarp();
+                if (lane == 0) pf_stamp(a, st_it * (kGStageK / kGSlotK), 6);
                 last_issue[st] = st_it;
                 ++st_it;
             }
@@ -273,27 +294,30 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                     (void)pf_wait(S.iq_full(s), (last_issue[s] / kGStages) & 1, abort_flag, a.status, false);
         }
     } else if (warp == kWGather) {
-        // ---- B operand: one 2-D tensor copy per slot (64 K x 128 rows) -----
+        // ---- B operand: one 2-D tensor copy per slot (64 K x 64 rows), on its
+        // own ring of kGBSlots so the copies run ahead of the A ring ---------
         if (lane == 0) {
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
                 const TileInfo ti = tile_info(a, t, MT);
                 for (int ks = 0; ks < nslots; ++ks) {
-                    const int slot = it % kGSlots;
-                    if (!pf_wait(S.s_empty(slot), ((it / kGSlots) & 1) ^ 1, abort_flag, a.status)) {
+                    const int slot = it % kGBSlots;
+                    if (!pf_wait(S.b_empty(slot), ((it / kGBSlots) & 1) ^ 1, abort_flag, a.status)) {
                         ok = false;
                         break;
                     }
-                    ptx::mbar_expect_tx(S.s_full(slot), kGSlotBytes);
-                    ptx::tma_load_2d(S.b_slot(slot), &a.bmap, ks * kGSlotK, ti.row0, S.s_full(slot));
+                    ptx::mbar_expect_tx(S.b_full(slot), kGBSlotBytes);
+                    ptx::tma_load_2d(S.b_slot(slot), &a.bmap, ks * kGSlotK, ti.row0, S.b_full(slot));
+                    pf_stamp(a, it, 0);
                     ++it;
                 }
             }
-            // the last slots' copies land before the CTA leaves (bounded)
+            // the last copies land before the CTA leaves (bounded)
             if (!ok)
-                for (int j = 1; j <= kGSlots && it - j >= 0; ++j)
-                    (void)pf_wait(S.s_full((it - j) % kGSlots), ((it - j) / kGSlots) & 1, abort_flag, a.status, false);
+                for (int j = 1; j <= kGBSlots && it - j >= 0; ++j)
+                    (void)pf_wait(S.b_full((it - j) % kGBSlots), ((it - j) / kGBSlots) & 1, abort_flag, a.status,
+                                  false);
         }
         __syncwarp();
     } else if (warp == kWMma) {
@@ -312,18 +336,26 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * kGNMax);
                 for (int ks = 0; ks < nslots; ++ks) {
-                    const int slot = it % kGSlots;
+                    const int slot = it % kGSlots, bslot = it % kGBSlots;
                     if (!pf_wait(S.s_full(slot), (it / kGSlots) & 1, abort_flag, a.status)) {
                         ok = false;
                         break;
                     }
+                    pf_stamp(a, it, 1);
+                    if (!pf_wait(S.b_full(bslot), (it / kGBSlots) & 1, abort_flag, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    pf_stamp(a, it, 2);
                     ptx::tc_fence_after();
-                    const uint32_t a0 = ptx::smem_addr(S.a_slot(slot)), b0 = ptx::smem_addr(S.b_slot(slot));
+                    const uint32_t a0 = ptx::smem_addr(S.a_slot(slot)), b0 = ptx::smem_addr(S.b_slot(bslot));
 #pragma unroll
                     for (int k = 0; k < kGSlotK / 16; ++k)
                         ptx::mma_bf16(d_tmem, ptx::desc_sw128(a0 + k * 32), ptx::desc_sw128(b0 + k * 32), idesc,
                                       (ks | k) != 0 ? 1u : 0u);
                     ptx::mma_commit(S.s_empty(slot));
+                    ptx::mma_commit(S.b_empty(bslot));
+                    pf_stamp(a, it, 3);
                     issued = true;
                     ++it;
                 }
@@ -340,41 +372,49 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
         __syncwarp();
     } else if (warp < kWEp0) {
         // ---- dequant: IQ4_XS stage -> bf16 A slot -----------------------
-        const int d = (warp - kWDq0) * 32 + lane;  // 0..255
+        const int dq = warp - kWDq0, grp = dq / kNDqG;
+        const int d = (dq % kNDqG) * 32 + lane;  // 0..255 within the group
         const int m = d & (kGM - 1), sub = d >> 7;
         int it = 0, st_it = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
             for (int ks = 0; ks < nslots; ++ks) {
                 const int st = st_it % kGStages;
-                if ((ks & 7) == 0 &&
-                    !pf_wait_warp(S.iq_full(st), (st_it / kGStages) & 1, abort_flag, a.status)) {
-                    ok = false;
-                    break;
+                if ((ks & 7) == 0) {
+                    if (!pf_wait_warp(S.iq_full(st), (st_it / kGStages) & 1, abort_flag, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    if (dq == 0 && lane == 0) pf_stamp(a, it, 7);
                 }
                 const int slot = it % kGSlots;
-                if (!pf_wait_warp(S.s_empty(slot), ((it / kGSlots) & 1) ^ 1, abort_flag, a.status)) {
-                    ok = false;
-                    break;
-                }
-                const int sbk = (ks & 7) * 2 + sub;  // sub-block of the row within the stage (0..15)
-                // stage row of M row m: gate|up stages hold the gate box then the up box
-                const int srow = a.mode == 0 ? ((m & 1) ? 64 + (m >> 1) : (m >> 1)) : m;
-                const uint8_t* blk = S.stage(st) + srow * kGStageRowB + (sbk >> 3) * QMOE_SB_BYTES;
-                const int ib = sbk & 7;
-                const uint2 hd = *reinterpret_cast<const uint2*>(blk);
-                const uint2 qa = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
-                const uint2 qb = *reinterpret_cast<const uint2*>(blk + 16 + 16 * ib);
-                uint4 cv[4];
-                dequant_subblock_bf16(hd.x, hd.y, ib, qa.x, qa.y, qb.x, qb.y, cv);
-                uint8_t* dst = S.a_slot(slot);
+                if ((it & 1) == grp) {
+                    if (!pf_wait_warp(S.s_empty(slot), ((it / kGSlots) & 1) ^ 1, abort_flag, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    if (dq % kNDqG == 0 && lane == 0) pf_stamp(a, it, 4);
+                    const int sbk = (ks & 7) * 2 + sub;  // sub-block of the row within the stage (0..15)
+                    // stage row of M row m: gate|up stages hold the gate box then the up box
+                    const int srow = a.mode == 0 ? ((m & 1) ? 64 + (m >> 1) : (m >> 1)) : m;
+                    const uint8_t* blk = S.stage(st) + srow * kGStageRowB + (sbk >> 3) * QMOE_SB_BYTES;
+                    const int ib = sbk & 7;
+                    const uint2 hd = *reinterpret_cast<const uint2*>(blk);
+                    const uint2 qa = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
+                    const uint2 qb = *reinterpret_cast<const uint2*>(blk + 16 + 16 * ib);
+                    uint4 cv[4];
+                    dequant_subblock_bf16(hd.x, hd.y, ib, qa.x, qa.y, qb.x, qb.y, cv);
+                    uint8_t* dst = S.a_slot(slot);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + sw128_off(m, sub * 4 + j)) = cv[j];
-                ptx::fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(S.s_full(slot));
+                    for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + sw128_off(m, sub * 4 + j)) = cv[j];
+                    ptx::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(S.s_full(slot));
+                    if (dq % kNDqG == 0 && lane == 0) pf_stamp(a, it, 5);
+                }
                 ++it;
                 if ((ks & 7) == 7 || ks == nslots - 1) {
+                    __syncwarp();
                     if (lane == 0) ptx::mbar_arrive(S.iq_empty(st));
                     ++st_it;
                 }
@@ -663,7 +703,7 @@ __global__ void __launch_bounds__(kPlaceWarps * 32) pf_place_kernel(const int32_
 // ---- workspace and launches ---------------------------------------------------
 
 struct PfLayout {
-    size_t status, meta, xb, logits, ids, weights, slog, counts, offsets, ntiles, slot_tok, slot_w, h, xg, total;
+    size_t status, meta, trace, xb, logits, ids, weights, slog, counts, offsets, ntiles, slot_tok, slot_w, h, xg, total;
     int max_ntiles, rows;
 };
 
@@ -677,7 +717,8 @@ PfLayout pf_layout(const qmoe_dims& d, int T) {
     size_t o = 0;
     L.status = 0;
     L.meta = 64;
-    o = 256;
+    L.trace = 256;  // [64 slots][8] u64 clock stamps of CTA 0's pipeline (per launch)
+    o = 256 + kPfTraceBytes;
     L.xb = o;
     o = pf_align(o + (size_t)T * d.hidden * 2);
     L.logits = o;
@@ -802,6 +843,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     a.meta = meta;
     a.out = out;
     a.status = status;
+    a.trace = reinterpret_cast<unsigned long long*>(ws + L.trace);
     err = cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemBytes);
     if (err != cudaSuccess) return err;
     const int n_sm = device_sm_count();

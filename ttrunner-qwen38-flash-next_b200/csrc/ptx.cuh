@@ -35,6 +35,19 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// The same test, letting the hardware suspend the thread until the phase
+// completes or about `hint_ns` pass, so a waiting warp issues no instructions
+// (a spinning one takes issue slots from the warps doing the work).
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // ---- copies ------------------------------------------------------------------
 // Global -> this CTA's shared memory bulk copy completing on `bar`;
 // dst and src 16-byte aligned, bytes a multiple of 16.

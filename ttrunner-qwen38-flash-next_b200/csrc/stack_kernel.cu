@@ -150,7 +150,7 @@ using ptx::now_ns;
 __device__ bool mbar_wait(uint64_t* bar, uint32_t par) {
     if (mbar_test(bar, par)) return true;
     const unsigned long long t0 = now_ns();
-    while (!mbar_test(bar, par)) {
+    while (!ptx::mbar_test_sleep(bar, par, 20000u)) {
         if (now_ns() - t0 > kTimeoutNs) return false;
     }
     return true;
