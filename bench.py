@@ -172,6 +172,8 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=1, help="tokens per step (1 = decode; 4/8 = verify)")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--variant", default="B", choices=["A", "B"])
+    ap.add_argument("--exchange", default="auto", choices=["auto", "kernel", "nccl"],
+                    help="N>1: partial sums exchanged inside the stack kernel over NVLink, or NCCL per layer")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill timings")
@@ -205,8 +207,11 @@ def main() -> None:
     if world > 1:
         from importlib import import_module
 
-        ShardedMoEStack = import_module(pkg.__name__ + ".dist").ShardedMoEStack
-        stack = ShardedMoEStack(layers, max_tokens=max(M, 1))
+        dist_mod = import_module(pkg.__name__ + ".dist")
+        exchange = args.exchange
+        if exchange == "auto":
+            exchange = "kernel" if M == 1 and dist_mod.kernel_exchange_supported(layers) else "nccl"
+        stack = dist_mod.ShardedMoEStack(layers, max_tokens=max(M, 1), exchange=exchange)
         out_buf = stack.act
     else:
         stack = pkg.MoEStack(layers, max_tokens=max(M, 1))
@@ -283,11 +288,11 @@ def main() -> None:
         ms_step = ms / args.steps
         us_tok = ms_step * 1000.0 / M
         bytes_tok = cfg.n_layers * cfg.layer_expert_bytes() / max(world, 1) if M == 1 else None
-        single = world == 1 and stack.single_launch(M)
+        single = stack.single_launch(M) if world == 1 else stack.exchange == "kernel"
         if single:
-            # one persistent launch per step: its bytes are the whole stack's
+            # one persistent launch per step: its bytes are the whole stack's (this rank's slice on N > 1)
             rl_kernel, rl_bytes, rl_us = "stack_kernel", bytes_tok, ms_step * 1000.0
-            rl_traffic = STACK_TRAFFIC_PER_LAYER_B * cfg.n_layers
+            rl_traffic = STACK_TRAFFIC_PER_LAYER_B * cfg.n_layers if world == 1 else None
         else:
             rl_kernel = "gateup_swiglu"
             rl_bytes = (cfg.top_k + (1 if shard.has_shared() else 0)) * 2 * shard.dims(cfg).inter_local \
@@ -306,7 +311,9 @@ def main() -> None:
                             f"{M} token(s)/step, hidden {cfg.hidden}, inter {cfg.inter}, {cfg.n_experts} experts, "
                             f"top-{cfg.top_k} + shared",
                 "tokens_per_step": M, "layers": cfg.n_layers,
-                "parallelism": f"variant {args.variant} x{world}" if world > 1 else "1 GPU",
+                "parallelism": (f"variant {args.variant} x{world}, " + (
+                    "partial rows exchanged inside the stack kernel over NVLink" if single else
+                    "NCCL all-reduce per layer")) if world > 1 else "1 GPU",
                 "l2": "inputs larger than L2: ~1.08 GB of weights read per token vs 126 MB L2",
             },
             "e2e": {"value": round(ms_e2e / args.steps * 1000.0 / M, 3), "unit": "us/token",

@@ -151,22 +151,24 @@ int qmoe_moe_block(const void* x, int x_dtype, int n_tokens, const qmoe_layer_we
                    void* stream);
 
 /* 1 when qmoe_stack_decode runs these shapes as one persistent launch (one
- * token, hidden 1024 or 2048, inter 512 with a 512-row shared expert,
- * unsharded, <= 64 layers, operands 16-byte aligned), else 0 (three launches
- * per layer).  The whole-stack analogue of the traced step
- * (tt/traced.py:261-277), which replays all 48 layers' MoE ops at once. */
+ * token, hidden 1024 or 2048, inter 512 with a 512-row shared expert, the
+ * whole expert range and the shared expert sliced like the routed ones,
+ * <= 64 layers, operands 16-byte aligned), else 0 (three launches per
+ * layer).  The whole-stack analogue of the traced step (tt/traced.py:261-277),
+ * which replays all 48 layers' MoE ops at once. */
 int qmoe_stack_single_launch(const qmoe_dims* dims, int n_tokens, int n_layers);
 
-/* Tracing: the single-launch stack kernel stamps its SM's cycle counter at 16
- * points of every layer in CTA 0 into the workspace: phase A start, x
- * loaded, x converted, router/shared rows resident, A computed, A done (0-5);
- * after barrier 1, top-k done, routed copies issued, routed gate|up done, B
- * done (6-10); after barrier 2, h converted, down rows resident, down done,
- * C done (11-15); the last CTA stamps the same points.  Copies the
- * n_layers x 16 stamps of CTA 0 and then those of the last CTA (2 x n_layers
- * x 16 values) of the last launch made with this workspace and n_tokens to
- * host_out (synchronises `stream`).  The
- * reference's analogue is its section profiler (tt/bench.py:33-78). */
+/* Tracing: the single-launch stack kernel stamps its SM's cycle counter at 24
+ * points of every layer in CTA 0 into the workspace (unused points stay 0):
+ * B start, top-k done, gate|up copies issued, down copies issued, copies
+ * done, gate|up rows done, h written, after barrier H, h converted, down
+ * resident, down done, router partial done (0-11); inside the top-k: logits
+ * loaded, x converted, threshold found, ranked (12-15); with an exchange
+ * between ranks: partial rows sent, peers' rows summed (16-17).  The last
+ * CTA stamps the same points.  Copies the n_layers x 24 stamps of CTA 0 and
+ * then those of the last CTA (2 x n_layers x 24 values) of the last launch
+ * made with this workspace and n_tokens to host_out (synchronises `stream`).
+ * The reference's analogue is its section profiler (tt/bench.py:33-78). */
 int qmoe_read_stack_trace(void* workspace, const qmoe_dims* dims, int n_tokens, int n_layers,
                           uint64_t* host_out, void* stream);
 
@@ -187,6 +189,55 @@ int qmoe_shared_expert(const void* x, int x_dtype, int n_tokens, const qmoe_laye
 int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* layers,
                       int n_layers, const qmoe_dims* dims, float* out, void* workspace,
                       size_t workspace_bytes, void* stream);
+
+/* ---- the stack sharded over the GPUs of one node ---------------------------
+ * One process per GPU, rank r of n_ranks (2, 4 or 8) holding the slice
+ * [r * inter / n, (r + 1) * inter / n) of every expert's intermediate rows
+ * (gate/up rows and the matching down columns; the shared expert sliced the
+ * same way): the reference's shipped shard plan (tt/plan.py:70-103).  Where
+ * the reference all-reduces each layer's partial output over its fabric
+ * (TTModel._moe_block, tt/model.py:2041-2052; tt/ops.py:97-111), here the
+ * single-launch stack kernel of every rank stores its partial rows straight
+ * into the peers' exchange buffers over NVLink and sums the n partials of
+ * its rows in rank order, so every rank ends each layer with bitwise the same
+ * activation and routes identically.
+ *
+ * Each rank allocates its exchange buffer with qmoe_xchg_alloc (zeroed; the
+ * 64-byte CUDA IPC handle goes to the peers through the caller's own
+ * channel, e.g. an all-gather), maps every peer's with qmoe_xchg_open, and
+ * passes all of them in a qmoe_xchg.  The buffers carry a launch counter:
+ * every rank must make the same sequence of qmoe_stack_decode_xchg calls with
+ * the same n_layers, and after a call that reports an error (a peer that
+ * never arrived: QMOE_ERR_TIMEOUT after a bounded wait) the buffers must be
+ * freed and allocated anew on every rank.  Unmap peers (qmoe_xchg_close) and
+ * free (qmoe_xchg_free) only when no rank has a launch in flight. */
+typedef struct qmoe_xchg {
+    int rank;
+    int n_ranks;
+    void* buf[8]; /* every rank's exchange buffer as mapped in this process; buf[rank] is this rank's own */
+} qmoe_xchg;
+
+#define QMOE_XCHG_HANDLE_BYTES 64
+
+size_t qmoe_xchg_bytes(int n_ranks, int hidden);
+/* cudaMalloc + zero (synchronous) on the current device; ipc_handle receives
+ * QMOE_XCHG_HANDLE_BYTES bytes for the peers. */
+int qmoe_xchg_alloc(int n_ranks, int hidden, void** buf, void* ipc_handle);
+/* Maps a peer's exchange buffer into this process (peer access enabled). */
+int qmoe_xchg_open(const void* ipc_handle, void** peer_buf);
+int qmoe_xchg_close(void* peer_buf);
+int qmoe_xchg_free(void* buf);
+/* 1 when qmoe_stack_decode_xchg runs these dims (this rank's slice) on
+ * n_ranks ranks: the shapes of qmoe_stack_single_launch with
+ * inter_local * n_ranks == inter. */
+int qmoe_stack_xchg_supported(const qmoe_dims* dims, int n_ranks, int n_tokens, int n_layers);
+/* qmoe_stack_decode on this rank's slice with the per-layer sum over ranks
+ * inside the launch: out [1, hidden] fp32 is the full (summed) last layer's
+ * output, the same bits on every rank.  Stream-ordered, capturable into a
+ * CUDA graph (one launch per call). */
+int qmoe_stack_decode_xchg(const void* x, int n_tokens, const qmoe_layer_weights* layers, int n_layers,
+                           const qmoe_dims* dims, const qmoe_xchg* xc, float* out, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* The MoE block for callers that cannot allocate device memory: the same
  * computation as qmoe_moe_block, with no workspace argument.  No counterpart

@@ -164,3 +164,68 @@ def _lonely_rank(port: int) -> None:
     except Exception:  # noqa: BLE001 -- any error is the expected outcome
         os._exit(3)
     os._exit(0)
+
+
+def test_exchange_host_logic(pkg):
+    """In-kernel exchange: buffer sizes, and which dims it runs (host-side checks, no GPU)."""
+    import ctypes
+
+    lib = pkg._lib.lib
+    assert lib.qmoe_xchg_bytes(2, 2048) == 128 + 2 * 2 * 2048 * 8
+    assert lib.qmoe_xchg_bytes(8, 2048) == 128 + 2 * 8 * 2048 * 8
+    assert lib.qmoe_xchg_bytes(9, 2048) == 0 and lib.qmoe_xchg_bytes(0, 2048) == 0
+    cfg = pkg.C2
+    for world in (2, 4, 8):
+        for rank in (0, world - 1):
+            d = pkg.Shard("B", rank, world).dims(cfg)
+            assert lib.qmoe_stack_xchg_supported(ctypes.byref(d), world, 1, 48) == 1
+            assert lib.qmoe_stack_xchg_supported(ctypes.byref(d), world, 2, 48) == 0  # one token only
+            assert lib.qmoe_stack_xchg_supported(ctypes.byref(d), world, 1, 65) == 0
+            other = 2 if world != 2 else 4
+            assert lib.qmoe_stack_xchg_supported(ctypes.byref(d), other, 1, 48) == 0  # slice width != inter / R
+    da = pkg.Shard("A", 0, 2).dims(cfg)
+    assert lib.qmoe_stack_xchg_supported(ctypes.byref(da), 2, 1, 48) == 0
+    dn = pkg.Shard().dims(cfg)
+    assert lib.qmoe_stack_xchg_supported(ctypes.byref(dn), 1, 1, 48) == 0
+    x = pkg._lib.Xchg(rank=0, n_ranks=2)
+    dims = pkg.Shard("B", 0, 2).dims(cfg)
+    # argument checks come before any device work
+    assert lib.qmoe_stack_decode_xchg(None, 1, None, 1, ctypes.byref(dims), ctypes.byref(x), None, None, 0,
+                                      None) == pkg._lib.QMOE_ERR_INVALID_ARG
+
+
+def _gather_main(rank: int, world: int, port: int, q) -> None:
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(root))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        import __graft_entry__
+        from importlib import import_module
+
+        pkg = __graft_entry__.load_package()
+        gather = import_module(pkg.__name__ + ".dist").gather_handles
+        got = gather(bytes([rank]) * 64)
+        q.put((rank, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_handles_gathered_in_rank_order(pkg):
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    want = [bytes([r]) * 64 for r in range(world)]
+    assert all(res[r] == want for r in range(world))

@@ -64,6 +64,19 @@ class Dims(ctypes.Structure):
     ]
 
 
+class Xchg(ctypes.Structure):
+    """qmoe_xchg: this rank, the rank count and every rank's exchange buffer as mapped here."""
+
+    _fields_ = [
+        ("rank", c_int),
+        ("n_ranks", c_int),
+        ("buf", c_void_p * 8),
+    ]
+
+
+XCHG_HANDLE_BYTES = 64
+
+
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
@@ -102,6 +115,14 @@ _SIGS = {
                                   c_size_t, _P]),
     "qmoe_read_stack_trace": (c_int, [_P, POINTER(Dims), c_int, c_int, _P, _P]),
     "qmoe_stack_single_launch": (c_int, [POINTER(Dims), c_int, c_int]),
+    "qmoe_xchg_bytes": (c_size_t, [c_int, c_int]),
+    "qmoe_xchg_alloc": (c_int, [c_int, c_int, POINTER(c_void_p), _P]),
+    "qmoe_xchg_open": (c_int, [_P, POINTER(c_void_p)]),
+    "qmoe_xchg_close": (c_int, [_P]),
+    "qmoe_xchg_free": (c_int, [_P]),
+    "qmoe_stack_xchg_supported": (c_int, [POINTER(Dims), c_int, c_int, c_int]),
+    "qmoe_stack_decode_xchg": (c_int, [_P, c_int, POINTER(LayerWeights), c_int, POINTER(Dims), POINTER(Xchg), _P,
+                                       _P, c_size_t, _P]),
     "qmoe_moe_block_noalloc": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P]),
     "qmoe_prefill_max_tokens": (c_int, []),
     "qmoe_prefill_workspace_bytes": (c_size_t, [POINTER(Dims), c_int]),

@@ -1,5 +1,6 @@
 // extern "C" entry points: argument checks, workspace layout, launches.
 #include <stdio.h>
+#include <string.h>
 
 #include "common.cuh"
 
@@ -201,7 +202,7 @@ WsLayout ws_layout(const qmoe_dims& d, int max_tokens) {
     L.sync = off;
     off = align_up(off + stack_sync_bytes(d.n_experts), 256);
     L.trace = off;
-    off = align_up(off + 2 * 64 * 16 * 8, 256);
+    off = align_up(off + 2 * 64 * kTraceSlots * 8, 256);
     L.total = off;
     return L;
 }
@@ -407,18 +408,18 @@ int qmoe_read_stack_trace(void* workspace, const qmoe_dims* dims, int n_tokens, 
     if (!workspace || !host_out || n_layers < 1 || n_layers > 64) return QMOE_ERR_INVALID_ARG;
     const WsLayout L = ws_layout(*dims, n_tokens);
     cudaStream_t s = (cudaStream_t)stream;
-    const size_t rows = (size_t)n_layers * 16 * sizeof(uint64_t);
+    const size_t rows = (size_t)n_layers * kTraceSlots * sizeof(uint64_t);
     QMOE_TRY(cuda_status(cudaMemcpyAsync(host_out, (unsigned char*)workspace + L.trace, rows,
                                          cudaMemcpyDeviceToHost, s)));
-    QMOE_TRY(cuda_status(cudaMemcpyAsync(host_out + (size_t)n_layers * 16,
-                                         (unsigned char*)workspace + L.trace + 64 * 16 * sizeof(uint64_t), rows,
-                                         cudaMemcpyDeviceToHost, s)));
+    QMOE_TRY(cuda_status(cudaMemcpyAsync(host_out + (size_t)n_layers * kTraceSlots,
+                                         (unsigned char*)workspace + L.trace + 64 * kTraceSlots * sizeof(uint64_t),
+                                         rows, cudaMemcpyDeviceToHost, s)));
     return cuda_status(cudaStreamSynchronize(s));
 }
 
 int qmoe_stack_single_launch(const qmoe_dims* dims, int n_tokens, int n_layers) {
     if (check_dims(dims) != QMOE_OK) return 0;
-    return stack_kernel_supported(*dims, n_tokens, n_layers) ? 1 : 0;
+    return stack_kernel_supported(*dims, n_tokens, n_layers, 1) ? 1 : 0;
 }
 
 int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* layers, int n_layers,
@@ -448,9 +449,9 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
                     aligned(w.gate_up, 16) && aligned(w.down, 16) && aligned(w.sh_gate_up, 16) &&
                     aligned(w.sh_down, 16);
     }
-    if (aligned16 && stack_kernel_supported(*dims, n_tokens, n_layers))
-        return cuda_status(launch_stack_kernel(x, out, ws.act(), ws.logits(), ws.h(), ws.sync(), ws.trace(), ws.status(), layers,
-                                               n_layers, *dims, s));
+    if (aligned16 && stack_kernel_supported(*dims, n_tokens, n_layers, 1))
+        return cuda_status(launch_stack_kernel(x, out, ws.act(), ws.h(), ws.sync(), ws.trace(), ws.status(), layers,
+                                               n_layers, *dims, nullptr, s));
     // Otherwise three launches per layer. Layer L+1 reads `out` (layer L's result) in its router and gate|up
     // launches; its down launch overwrites `out` only after both, in stream
     // order, so one buffer carries the activation through the stack.
@@ -460,6 +461,96 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
         QMOE_TRY(run_block(in, dt, n_tokens, &layers[l], dims, out, ws, s));
     }
     return QMOE_OK;
+}
+
+// ---- the stack sharded over ranks, exchange inside the kernel ----------------
+
+static int check_stack_operands(const void* x, int n_tokens, const qmoe_layer_weights* layers, int n_layers,
+                                const qmoe_dims* dims, const float* out) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_act(x, QMOE_ACT_BF16));
+    if (!layers || n_layers < 1 || !out) return QMOE_ERR_INVALID_ARG;
+    for (int l = 0; l < n_layers; ++l) {
+        QMOE_TRY(check_weights_route(&layers[l]));
+        QMOE_TRY(check_weights_experts(&layers[l], dims));
+    }
+    return QMOE_OK;
+}
+
+size_t qmoe_xchg_bytes(int n_ranks, int hidden) {
+    if (n_ranks < 1 || n_ranks > kMaxXchgRanks || hidden < 1 || hidden > kMaxHidden) return 0;
+    return xchg_bytes(n_ranks, hidden);
+}
+
+int qmoe_xchg_alloc(int n_ranks, int hidden, void** buf, void* ipc_handle) {
+    if (!buf || !ipc_handle) return QMOE_ERR_INVALID_ARG;
+    const size_t bytes = qmoe_xchg_bytes(n_ranks, hidden);
+    if (!bytes) return QMOE_ERR_UNSUPPORTED;
+    void* p = nullptr;
+    QMOE_TRY(cuda_status(cudaMalloc(&p, bytes)));
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(e);
+    }
+    static_assert(sizeof(h) == QMOE_XCHG_HANDLE_BYTES, "CUDA IPC handle size");
+    memcpy(ipc_handle, &h, sizeof(h));
+    *buf = p;
+    return QMOE_OK;
+}
+
+int qmoe_xchg_open(const void* ipc_handle, void** peer_buf) {
+    if (!ipc_handle || !peer_buf) return QMOE_ERR_INVALID_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    return cuda_status(cudaIpcOpenMemHandle(peer_buf, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int qmoe_xchg_close(void* peer_buf) {
+    if (!peer_buf) return QMOE_ERR_INVALID_ARG;
+    return cuda_status(cudaIpcCloseMemHandle(peer_buf));
+}
+
+int qmoe_xchg_free(void* buf) {
+    if (!buf) return QMOE_ERR_INVALID_ARG;
+    return cuda_status(cudaFree(buf));
+}
+
+int qmoe_stack_xchg_supported(const qmoe_dims* dims, int n_ranks, int n_tokens, int n_layers) {
+    if (check_dims(dims) != QMOE_OK || n_ranks < 2 || n_ranks > kMaxXchgRanks) return 0;
+    return stack_kernel_supported(*dims, n_tokens, n_layers, n_ranks) ? 1 : 0;
+}
+
+int qmoe_stack_decode_xchg(const void* x, int n_tokens, const qmoe_layer_weights* layers, int n_layers,
+                           const qmoe_dims* dims, const qmoe_xchg* xc, float* out, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+    QMOE_TRY(check_stack_operands(x, n_tokens, layers, n_layers, dims, out));
+    if (!xc || xc->n_ranks < 2 || xc->n_ranks > kMaxXchgRanks || xc->rank < 0 || xc->rank >= xc->n_ranks)
+        return QMOE_ERR_INVALID_ARG;
+    XchgDesc desc{};
+    desc.R = xc->n_ranks;
+    desc.rank = xc->rank;
+    for (int q = 0; q < xc->n_ranks; ++q) {
+        if (!xc->buf[q]) return QMOE_ERR_INVALID_ARG;
+        if (!aligned(xc->buf[q], 256)) return QMOE_ERR_ALIGNMENT;
+        desc.buf[q] = (unsigned char*)xc->buf[q];
+    }
+    if (!aligned(x, 16) || !aligned(out, 16)) return QMOE_ERR_ALIGNMENT;
+    for (int l = 0; l < n_layers; ++l) {
+        const qmoe_layer_weights& w = layers[l];
+        if (!w.gate_vec || !w.sh_gate_up || !w.sh_down) return QMOE_ERR_INVALID_ARG;
+        if (!aligned(w.router, 16) || !aligned(w.gate_vec, 16) || !aligned(w.gate_up, 16) || !aligned(w.down, 16) ||
+            !aligned(w.sh_gate_up, 16) || !aligned(w.sh_down, 16))
+            return QMOE_ERR_ALIGNMENT;
+    }
+    if (!stack_kernel_supported(*dims, n_tokens, n_layers, xc->n_ranks)) return QMOE_ERR_UNSUPPORTED;
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    return cuda_status(launch_stack_kernel(x, out, ws.act(), ws.h(), ws.sync(), ws.trace(), ws.status(), layers,
+                                           n_layers, *dims, &desc, (cudaStream_t)stream));
 }
 
 // ---- prefill / large verify chunks ------------------------------------------

@@ -48,6 +48,22 @@ inline size_t stack_logit_groups(int E) { return (size_t)(E + 1 + 3) / 4; }
 inline size_t stack_logit_bytes(int E) { return 2 * (size_t)kStackLogitReplicas * stack_logit_groups(E) * 128; }
 inline size_t stack_sync_bytes(int E) { return 1152 + stack_logit_bytes(E) + 2 * kStackHmaxWords * 4; }
 
+// Phase stamps per layer in the stack kernel's trace ([2][64 layers][slots]).
+constexpr int kTraceSlots = 24;
+
+// In-kernel exchange between ranks: a rank's exchange buffer holds its
+// launch counter (first 128 bytes), then the receive words
+// u64 [2 parities][R][hidden] that the peers store into.
+constexpr int kMaxXchgRanks = 8;
+constexpr size_t kXchgHeader = 128;
+inline size_t xchg_bytes(int R, int hidden) { return kXchgHeader + (size_t)2 * R * hidden * 8; }
+
+// Where the stack kernel exchanges partial rows with its peers.
+struct XchgDesc {
+    int R, rank;
+    unsigned char* buf[kMaxXchgRanks];  // every rank's exchange buffer as mapped here
+};
+
 // Launch arguments of the routing kernel.
 struct RouteArgs {
     const void* x;
@@ -102,11 +118,13 @@ cudaError_t launch_synth_f32(uint64_t seed, uint64_t sid, int64_t n, float std_d
 
 int device_sm_count();
 
-// The single-launch decode stack kernel (stack_kernel.cu).
-bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers);
-cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* logits, float* h, unsigned* sync,
+// The single-launch decode stack kernel (stack_kernel.cu).  R ranks exchange
+// their partial rows inside the kernel when R > 1.
+// xc: null for one rank.
+bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers, int R);
+cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* h, unsigned* sync,
                                 unsigned long long* trace, int* status, const qmoe_layer_weights* layers, int n_layers,
-                                const qmoe_dims& d, cudaStream_t stream);
+                                const qmoe_dims& d, const XchgDesc* xc, cudaStream_t stream);
 
 // Prefill / large verify chunks (prefill.cu).
 int prefill_max_tokens();

@@ -4,31 +4,45 @@
 // over the layers.  Every layer is the reference's `_moe` (reference/model.py
 // :387-417) in two phases separated by grid barriers:
 //
-//   B  warp 0 ranks the E router logits (warp top-k, lower id on ties) and
-//      starts bulk copies (cp.async.bulk, mbarrier completion) of only this
-//      CTA's slice of the selected experts' gate|up rows and down rows; warps
-//      1-15 meanwhile convert x to block floating point and compute the CTA's
-//      rows of the shared expert's gate|up (prefetched); then all warps decode
-//      routed gate|up rows as their 4-pair chunks land -> h slice.
+//   B  every CTA ranks the E router logits (block top-k, lower id on ties);
+//      warps 0 and 1 start bulk copies (cp.async.bulk, mbarrier completion)
+//      of only this CTA's slice of the selected experts' gate|up rows and
+//      down rows while x converts to block floating point; all warps decode
+//      the shared expert's rows of the slice (prefetched), then the routed
+//      gate|up rows as their chunks land -> h slice.
 //   C  while the next layer's shared rows and router columns stream in (HBM
 //      is otherwise idle here): the full h (k + 1 slots) -> block floating
 //      point; this CTA's output rows of every selected expert's down (resident
 //      since phase B) and of the shared expert, a warp per row ->
 //      out[j] = sum_s w_s D_s[j].h_s + sigmoid(g.x) D_sh[j].h_sh; then the NEXT
 //      layer's router logits restricted to these rows, sum_j R[e][j] x[j] over
-//      this CTA's j, added into a logit accumulator with vector fp32 atomics.
+//      this CTA's j, added into a logit accumulator with atomics.
 //
 // The barrier after C therefore publishes both the next layer's input and
-// its complete router logits: two grid barriers per layer.  The router
-// logits are sums of per-CTA partials in arrival order (fp32 atomics), so
-// their last bits may vary between runs; selection reads them only after
-// the barrier.  A prologue computes layer 0's logits the same way.
+// its complete router logits: two grid barriers per layer.  A prologue
+// computes layer 0's logits the same way.
+//
+// Sharded over R ranks (one process and one GPU each; the reference's
+// split of every expert's intermediate rows, tt/plan.py:70-103), each rank
+// runs this kernel on its slice of every expert (I / R gate|up row pairs and
+// the matching down columns) and its phase-C rows are partial sums.  The
+// reduction over ranks happens inside the kernel: CTA c sends its partial
+// rows to CTA c of every peer as 8-byte words (value bits, flag) stored
+// straight into the peer's memory over NVLink, each word its own completion
+// signal, and sums the R partials of its rows in rank order once the peers'
+// words are in.  Every rank then holds bitwise the same next-layer input, and
+// computes the router partials from it as on one GPU; on R > 1 ranks the
+// logits accumulate in fp64, where a sum of fp32 partials is exact unless
+// their magnitudes span more than 2^21, so every rank ranks the same logits
+// and selects the same experts.  On one rank the accumulation is fp32 and
+// its last bits depend on arrival order (selection reads it only after the
+// barrier).
 //
 // Activations between layers are fp32 rounded to bf16 where they are read
 // (bf16 activations, fp32 accumulation).  All waits are bounded in time
-// (%globaltimer): a grid barrier or copy that does not complete sets
-// QMOE_ERR_TIMEOUT and an abort word; every CTA waits (bounded) for its own
-// copies in flight and returns.  No trap, no unbounded spin.
+// (%globaltimer): a grid barrier, copy or exchange that does not complete
+// sets QMOE_ERR_TIMEOUT and an abort word; every CTA waits (bounded) for its
+// own copies in flight and returns.  No trap, no unbounded spin.
 #include <cuda.h>  // CUtensorMap
 
 #include "common.cuh"
@@ -42,6 +56,8 @@ namespace {
 constexpr int kSKWarps = 16;
 constexpr int kSKThreads = kSKWarps * 32;
 constexpr unsigned long long kTimeoutNs = 200ull * 1000 * 1000;
+// A peer rank's rows may arrive late by as much as the ranks' launch skew.
+constexpr unsigned long long kXchgTimeoutNs = 4000ull * 1000 * 1000;
 constexpr int kSKChunk = 8;      // routed row pairs per gate|up bulk-copy chunk
 constexpr int kSKMaxChunks = 6;  // chunks of a CTA's pairs (<= 40 pairs per CTA)
 constexpr int kRColW = 20;      // router columns per tensor-copy box (80 B): covers 16 from a 16-byte-aligned start
@@ -61,6 +77,14 @@ struct SKLayer {
 constexpr int kSKMaxLayers = 64;
 
 struct SKArgs {
+    // In-kernel exchange over R ranks (R == 1: none).  xr[q]: rank q's receive
+    // words [2 parities][R][D] as mapped in this process (xr[rank] local);
+    // epoch: this rank's count of completed launches, which makes every
+    // exchange's flag value new.
+    int R, rank;
+    int ib0;                              // first sub-block of a down row's slice inside its super-block
+    unsigned long long* xr[kMaxXchgRanks];
+    unsigned* epoch;
     const __nv_bfloat16* x;  // [D] layer-0 input
     float* out;              // [D] last layer's output
     __nv_bfloat16* act;      // [D] layer activation, bf16 (workspace)
@@ -68,7 +92,7 @@ struct SKArgs {
     float* logits;           // two accumulators of G lines x 32 floats (logits 4g..4g+3 at a line's front)
     float* h;                // [(K + 1) * I] (workspace)
     unsigned* sync;          // 8 counters, 128 B apart, then the abort word
-    unsigned long long* trace;  // [2][64][16] phase stamps of CTA 0 and the last CTA, or null
+    unsigned long long* trace;  // [2][64][kTraceSlots] phase stamps of CTA 0 and the last CTA, or null
     int* status;
     int n_layers, D, I, E, K;
     SKLayer L[kSKMaxLayers];
@@ -80,7 +104,7 @@ struct SKArgs {
 
 // Shared-memory carve-up (byte offsets), a function of the shape and grid.
 struct SKLayout {
-    int NSQ, NP, NJ, RJ;
+    int NSQ, NP, NJ, NJR, RJ;
     unsigned xq, xs, rcol, xo, sgu, sdn, gbuf, ubuf, dbuf, hq, hs, gv, uv, sgv, suv, cand, wmax, red, tkv, tki, misc, bars,
         total;
 };
@@ -91,13 +115,22 @@ __host__ __device__ constexpr unsigned sk_take(unsigned& o, unsigned bytes) {
     return r;
 }
 
+// Bytes of a down row of I values: whole super-blocks, or (a rank's slice of
+// fewer than 256 columns) the super-block's 8-byte header then the slice's
+// I / 32 16-byte code groups.
+__host__ __device__ constexpr int sk_down_row_bytes(int I) { return I >= 256 ? (I / 256) * 136 : 8 + 16 * (I / 32); }
+
 __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int n) {
     SKLayout s{};
-    const unsigned RB = (unsigned)(D / 256) * 136, DRB = (unsigned)(I / 256) * 136;
+    const unsigned RB = (unsigned)(D / 256) * 136, DRB = (unsigned)sk_down_row_bytes(I);
     const unsigned NSB = D / 32, NSBH = I / 32;
     s.NSQ = (I + n - 1) / n;
     s.NP = (K * I + n - 1) / n;
     s.NJ = (D + n - 1) / n;
+    // Down rows whose size is not a multiple of 16 bytes are copied in pairs
+    // from an even row, so that every bulk copy starts 16-byte aligned: up
+    // to two extra rows per slot, and an even row count keeps slots aligned.
+    s.NJR = DRB % 16 ? (s.NJ + 3) & ~1 : s.NJ;
     s.RJ = kRColW;  // the tensor-copy box's row pitch
     unsigned o = 0;
     s.xq = sk_take(o, NSB * 64);
@@ -105,10 +138,10 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     s.rcol = sk_take(o, (unsigned)(((E + kRBoxRows - 1) / kRBoxRows) * kRBoxRows + 1) * kRColW * 4);
     s.xo = sk_take(o, (unsigned)s.NJ * 4);
     s.sgu = sk_take(o, 2u * s.NSQ * RB);
-    s.sdn = sk_take(o, (unsigned)s.NJ * DRB);
+    s.sdn = sk_take(o, (unsigned)s.NJR * DRB);
     s.gbuf = sk_take(o, (unsigned)s.NP * RB);
     s.ubuf = sk_take(o, (unsigned)s.NP * RB);
-    s.dbuf = sk_take(o, (unsigned)K * s.NJ * DRB);
+    s.dbuf = sk_take(o, (unsigned)K * s.NJR * DRB);
     s.hq = sk_take(o, (unsigned)(K + 1) * NSBH * 64);
     s.hs = sk_take(o, (unsigned)(K + 1) * NSBH * 4);
     s.gv = sk_take(o, s.NP * 4);
@@ -128,15 +161,21 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
 
 // The shapes the single launch is built for: everything that sizes or
 // places data is a compile-time constant, so the layer loop keeps only its
-// data in registers.  Inter is 512 (the BASELINE family).
-template <int D_, int E_, int K_, int NSM_>
+// data in registers.  I is the intermediate width this rank holds: 512 (the
+// BASELINE family) unsharded, 512 / R on each of R ranks.
+template <int D_, int E_, int K_, int NSM_, int I_ = 512>
 struct SKShape {
-    static constexpr int D = D_, E = E_, K = K_, NSM = NSM_, I = 512;
-    static constexpr SKLayout S = sk_layout(D_, 512, E_, K_, NSM_);
+    static constexpr int D = D_, E = E_, K = K_, NSM = NSM_, I = I_;
+    static constexpr int DRB = sk_down_row_bytes(I_);
+    static constexpr bool kPairRows = DRB % 16 != 0;
+    static constexpr SKLayout S = sk_layout(D_, I_, E_, K_, NSM_);
     static_assert(E_ <= kSKThreads && E_ % 32 == 0, "one router row per thread");
-    static_assert(K_ * 512 / NSM_ + 1 <= 512, "a CTA's routed rows span at most two experts");
-    static_assert((K_ * 512 + NSM_ - 1) / NSM_ <= kSKChunk * (kSKMaxChunks - 1), "chunks of a CTA's pairs");
+    static_assert(I_ % 32 == 0 && I_ <= 512 && (I_ >= 256 ? I_ % 256 == 0 : 256 % I_ == 0), "intermediate slice");
+    static_assert((K_ + 1) * (I_ / 32) <= kStackHmaxBlocks, "block maxima of h");
+    static_assert(K_ * I_ / NSM_ + 1 <= I_, "a CTA's routed rows span at most two experts");
+    static_assert((K_ * I_ + NSM_ - 1) / NSM_ <= kSKChunk * (kSKMaxChunks - 1), "chunks of a CTA's pairs");
     static_assert((D_ + NSM_ - 1) / NSM_ + 3 <= kRColW, "router column slice: one box per CTA");
+    static_assert(D_ % 2 == 0, "down rows copied in pairs");
 };
 
 namespace {
@@ -162,8 +201,8 @@ __device__ __forceinline__ unsigned* abort_word(unsigned* sync) { return sync + 
 // stamp their SM's cycle counter (clock64) at each phase boundary.
 __device__ __forceinline__ void trace_mark(const SKArgs& a, int L, int k, int rec = 0) {
     if (a.trace && (int)threadIdx.x == rec) {
-        if (blockIdx.x == 0) a.trace[L * 16 + k] = (unsigned long long)clock64();
-        else if (blockIdx.x == gridDim.x - 1) a.trace[(64 + L) * 16 + k] = (unsigned long long)clock64();
+        if (blockIdx.x == 0) a.trace[L * kTraceSlots + k] = (unsigned long long)clock64();
+        else if (blockIdx.x == gridDim.x - 1) a.trace[(64 + L) * kTraceSlots + k] = (unsigned long long)clock64();
     }
 }
 
@@ -172,7 +211,7 @@ __device__ __forceinline__ void trace_mark_after(const SKArgs& a, int L, int k, 
     if (a.trace && threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1)) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%clock64;" : "=l"(t) : "l"(dep));
-        a.trace[(blockIdx.x == 0 ? L : 64 + L) * 16 + k] = t;
+        a.trace[(blockIdx.x == 0 ? L : 64 + L) * kTraceSlots + k] = t;
     }
 }
 
@@ -294,8 +333,12 @@ __device__ __forceinline__ void load_xr(const int* xq, const float* xs, int lane
 }
 
 // Sub-block t of one down row dotted with its slot's activation block (hq in
-// the [quad][sub-block][4 words] layout), scaled: d*(ls-32) * step * S.
-__device__ __forceinline__ float down_unit_one(const uint8_t* row, const int* hq, const float* hs, int nsbh, int t) {
+// the [quad][sub-block][4 words] layout), scaled: d*(ls-32) * step * S.  A
+// row of whole super-blocks has ib0 = 0; a rank's slice of fewer than 8
+// sub-blocks stores them after the super-block's header and takes its scales
+// from sub-block ib0 on.
+__device__ __forceinline__ float down_unit_one(const uint8_t* row, const int* hq, const float* hs, int nsbh, int t,
+                                               int ib0) {
     const uint8_t* blk = row + (t >> 3) * QMOE_SB_BYTES;
     const int ib = t & 7;
     const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
@@ -312,7 +355,7 @@ __device__ __forceinline__ float down_unit_one(const uint8_t* row, const int* hq
     }
     const int Sd = qmoe_subblock_dot(q0.x, q0.y, q1.x, q1.y, xp, 0);
     const float dl = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu))) *
-                     (float)(qmoe_iq4xs_ls(hdr.x, hdr.y, ib) - 32);
+                     (float)(qmoe_iq4xs_ls(hdr.x, hdr.y, ib0 + ib) - 32);
     return dl * hs[t] * (float)Sd;
 }
 
@@ -321,6 +364,7 @@ struct SKPart {
     int D, I, E, K, RB, DRB, NSBH;
     size_t GUE, DNE;
     int sq_lo, sq_hi, p_lo, p_hi, j_lo, j_hi;
+    int jc_lo, jc_hi;  // down rows copied: [j_lo, j_hi), widened to even bounds for rows of 8 mod 16 bytes
 };
 
 template <class SH>
@@ -333,7 +377,7 @@ __device__ __forceinline__ SKPart sk_part() {
     p.E = SH::E;
     p.K = SH::K;
     p.RB = (SH::D >> 8) * QMOE_SB_BYTES;
-    p.DRB = (SH::I >> 8) * QMOE_SB_BYTES;
+    p.DRB = SH::DRB;
     p.NSBH = SH::I >> 5;
     p.GUE = (size_t)2 * SH::I * p.RB;
     p.DNE = (size_t)SH::D * p.DRB;
@@ -344,6 +388,8 @@ __device__ __forceinline__ SKPart sk_part() {
     p.p_hi = (c + 1) * P / n;
     p.j_lo = c * SH::D / n;
     p.j_hi = (c + 1) * SH::D / n;
+    p.jc_lo = SH::kPairRows ? p.j_lo & ~1 : p.j_lo;
+    p.jc_hi = SH::kPairRows ? (p.j_hi + 1) & ~1 : p.j_hi;
     return p;
 }
 
@@ -363,9 +409,9 @@ __device__ __forceinline__ void issue_sgu(const SKLayer& W, const SKPart& p, con
 // Shared-expert down rows of this CTA's output slice (thread 0 only).
 __device__ __forceinline__ void issue_sdn(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
                                           uint64_t* bar) {
-    const int nj = p.j_hi - p.j_lo;
-    mbar_expect_tx(bar, (uint32_t)(nj * p.DRB));
-    if (nj > 0) ptx::bulk_g2s(sm + S.sdn, W.sh_down + (size_t)p.j_lo * p.DRB, (uint32_t)(nj * p.DRB), bar);
+    const int nc = p.jc_hi - p.jc_lo;
+    mbar_expect_tx(bar, (uint32_t)(nc * p.DRB));
+    if (nc > 0) ptx::bulk_g2s(sm + S.sdn, W.sh_down + (size_t)p.jc_lo * p.DRB, (uint32_t)(nc * p.DRB), bar);
 }
 
 // Router columns of this CTA's output rows, for every router row and the gate
@@ -383,10 +429,11 @@ __device__ __forceinline__ void issue_rcol(const CUtensorMap* rmap, const CUtens
 }
 
 // This CTA's share of the router logits: thread e (and thread 0 for the gate
-// row E) sums rcol[e][j] * x[j_lo + j] over its j; four consecutive experts
-// combine into one vector atomic add on their accumulator line.
+// row E) sums rcol[e][j] * x[j_lo + j] over its j.  fp32 accumulators: four
+// consecutive experts combine into one vector atomic add on their line; fp64
+// (f64): one atomic add per logit, four per line.
 __device__ __forceinline__ void router_partial(const SKPart& p, const SKLayout& S, const unsigned char* sm,
-                                               float* acc_buf) {
+                                               float* acc_buf, bool f64) {
     const float* xo = reinterpret_cast<const float*>(sm + S.xo);
     const float* rcol = reinterpret_cast<const float*>(sm + S.rcol) + (p.j_lo & 3);  // column j_lo of row 0
     const int nj = p.j_hi - p.j_lo, e = threadIdx.x, lane = threadIdx.x & 31;
@@ -394,6 +441,19 @@ __device__ __forceinline__ void router_partial(const SKPart& p, const SKLayout& 
     float v = 0.0f;
     if (e < p.E)
         for (int j = 0; j < nj; ++j) v = fmaf(rcol[e * S.RJ + j], xo[j], v);
+    if (f64) {
+        double* acc64 = reinterpret_cast<double*>(acc_buf);
+        if (e < p.E)
+            asm volatile("red.global.add.f64 [%0], %1;" ::"l"(acc64 + (e >> 2) * 16 + (e & 3)), "d"((double)v)
+                         : "memory");
+        if (e == 0) {
+            float g = 0.0f;
+            for (int j = 0; j < nj; ++j) g = fmaf(rcol[gate_row * S.RJ + j], xo[j], g);
+            asm volatile("red.global.add.f64 [%0], %1;" ::"l"(acc64 + (p.E >> 2) * 16 + (p.E & 3)), "d"((double)g)
+                         : "memory");
+        }
+        return;
+    }
     const float v1 = __shfl_down_sync(0xffffffffu, v, 1), v2 = __shfl_down_sync(0xffffffffu, v, 2),
                 v3 = __shfl_down_sync(0xffffffffu, v, 3);
     if (e < p.E && (lane & 3) == 0)
@@ -460,12 +520,12 @@ __device__ __forceinline__ void issue_gate_up(const SKLayer& W, const SKPart& p,
 // in phase C).
 __device__ __forceinline__ void issue_down(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
                                            const int* ids, uint64_t* bar_dn, int lane) {
-    const int nj = p.j_hi - p.j_lo;
-    if (lane == 0) mbar_expect_tx(bar_dn, (uint32_t)(p.K * nj * p.DRB));
+    const int nc = p.jc_hi - p.jc_lo;
+    if (lane == 0) mbar_expect_tx(bar_dn, (uint32_t)(p.K * nc * p.DRB));
     __syncwarp();
-    if (lane < p.K && nj > 0)
-        ptx::bulk_g2s(sm + S.dbuf + (size_t)lane * S.NJ * p.DRB,
-                      W.down + (size_t)ids[lane] * p.DNE + (size_t)p.j_lo * p.DRB, (uint32_t)(nj * p.DRB), bar_dn);
+    if (lane < p.K && nc > 0)
+        ptx::bulk_g2s(sm + S.dbuf + (size_t)lane * S.NJR * p.DRB,
+                      W.down + (size_t)ids[lane] * p.DNE + (size_t)p.jc_lo * p.DRB, (uint32_t)(nc * p.DRB), bar_dn);
 }
 
 template <class SH>
@@ -501,6 +561,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     int* s_ok = reinterpret_cast<int*>(sm + S.misc);
     int* s_cnt = reinterpret_cast<int*>(sm + S.misc) + 8;
     float* s_glogit = reinterpret_cast<float*>(sm + S.misc) + 12;
+    unsigned* s_epoch = reinterpret_cast<unsigned*>(sm + S.misc) + 2;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S.bars);
     uint64_t* bar_sgu = bars;
     uint64_t* bar_sdn = bars + 1;
@@ -512,8 +573,11 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     if (tid == 0) {
         for (int i = 0; i < nbars; ++i) mbar_init(bars + i, 1);
         ptx::fence_mbar_init();
+        *s_epoch = a.R > 1 ? __ldcg(a.epoch) : 0u;
     }
     __syncthreads();
+    const bool xchg = a.R > 1;
+    const unsigned epoch = *s_epoch;
     // Phases issued (kept by thread 0 in registers), for the bounded drain:
     // the prefetch barriers (shared rows, shared down rows, router columns) and
     // the per-layer routed copies (chunks and down rows, issued together).
@@ -528,7 +592,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     // ---------------- prologue: layer 0's router logits --------------------
     if (tid < nj) xo[tid] = __bfloat162float(a.x[p.j_lo + tid]);
     bool ok = !__syncthreads_or(!mbar_wait(bar_rc, 0));
-    if (ok) router_partial(p, S, sm, a.logits + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32);
+    if (ok) router_partial(p, S, sm, a.logits + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32, xchg);
     else if (tid == 0) {
         record_status(a.status, QMOE_ERR_TIMEOUT);
         atomicExch(abort_word(a.sync), 1u);
@@ -558,9 +622,14 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                                : __bfloat162float(__ushort_as_bfloat16(
                                      __ldcg(reinterpret_cast<const unsigned short*>(a.act) + b * 32 + lane)));
         }
-        if (tid == 0) *s_glogit = __ldcg(lg + (E >> 2) * 32 + (E & 3));
+        // logit i: fp32 at float (i / 4) * 32 + i % 4, or fp64 at double (i / 4) * 16 + i % 4
+        const double* lg64 = reinterpret_cast<const double*>(lg);
+        auto logit_at = [&](int i) {
+            return xchg ? (float)__ldcg(lg64 + (i >> 2) * 16 + (i & 3)) : __ldcg(lg + (i >> 2) * 32 + (i & 3));
+        };
+        if (tid == 0) *s_glogit = logit_at(E);
         const float lmax = block_topk_threshold(
-            [&](int i) { return __ldcg(lg + (i >> 2) * 32 + (i & 3)); }, E, K, cand, wmax, red, s_cnt, tkv, tki,
+            logit_at, E, K, cand, wmax, red, s_cnt, tkv, tki,
             [&]() {
 #pragma unroll
                 for (int i = 0; i < XPW; ++i) {
@@ -588,8 +657,10 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             // CTA 0 clears the other logit accumulator for the next layer's sums
             // (read last in the previous layer's phase B; first added to after
             // this layer's second barrier).
-            for (int g = tid - 64; g < kStackLogitReplicas * G; g += kSKThreads - 64)
+            for (int g = tid - 64; g < kStackLogitReplicas * G; g += kSKThreads - 64) {
                 *reinterpret_cast<float4*>(lg_next + g * 32) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4*>(lg_next + g * 32 + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
         __syncthreads();
         trace_mark(a, L, 4);
@@ -729,22 +800,82 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
         float psum = 0.0f;
         for (int s2 = 0; s2 < K; ++s2) psum += tkv[s2];
         const float inv_psum = 1.0f / psum, gate = sigmoid(*s_glogit);
+        const int jo = p.j_lo - p.jc_lo;  // row j_lo's place in the copied rows
+        // exchange: this layer's flag value and receive parity (both change
+        // with every exchange, across launches too)
+        const unsigned fval = epoch * 64u + (unsigned)L + 1u;
+        const int xpar = (int)((epoch * (unsigned)a.n_layers + (unsigned)L) & 1u);
         for (int j = warp; j < nj; j += kSKWarps) {
             float acc = 0.0f;
             constexpr int NT = (K + 1) * (I / 32);
             for (int t = lane; t < NT; t += 32) {
                 const int s = t / (I / 32), b = t - s * (I / 32);
-                const uint8_t* row = s < K ? dbuf + ((size_t)s * S.NJ + j) * p.DRB : sdn + (size_t)j * p.DRB;
+                const uint8_t* row = s < K ? dbuf + ((size_t)s * S.NJR + jo + j) * p.DRB : sdn + (size_t)(jo + j) * p.DRB;
                 const float wgt = s < K ? tkv[s] * inv_psum : gate;
-                acc += wgt * down_unit_one(row, hq + s * p.NSBH * 16, hs + s * p.NSBH, p.NSBH, b);
+                acc += wgt * down_unit_one(row, hq + s * p.NSBH * 16, hs + s * p.NSBH, p.NSBH, b, a.ib0);
             }
             acc = warp_sum(acc);
-            if (lane == 0) {
-                const __nv_bfloat16 xb = __float2bfloat16_rn(acc);
-                if (last) a.out[p.j_lo + j] = acc;
-                else a.act[p.j_lo + j] = xb;
-                xo[j] = __bfloat162float(xb);
+            if (!xchg) {
+                if (lane == 0) {
+                    const __nv_bfloat16 xb = __float2bfloat16_rn(acc);
+                    if (last) a.out[p.j_lo + j] = acc;
+                    else a.act[p.j_lo + j] = xb;
+                    xo[j] = __bfloat162float(xb);
+                }
+            } else {
+                // this rank's partial of row j: kept, and stored into every
+                // peer as one word (value bits, flag)
+                if (lane == 0) xo[j] = acc;
+                if (lane < a.R && lane != a.rank)
+                    ptx::st_relaxed_sys_u64(
+                        a.xr[lane] + ((size_t)(xpar * a.R + a.rank) * D + p.j_lo + j),
+                        ((unsigned long long)fval << 32) | __float_as_uint(acc));
             }
+        }
+        if (xchg) {
+            trace_mark(a, L, 16);
+            __syncthreads();
+            // Row j_lo + tid: the R partials summed in rank order (the same
+            // order, so the same bits, on every rank) once the peers' words
+            // carry this exchange's flag.
+            bool x_ok = true;
+            if (tid < nj) {
+                const unsigned long long* rx = a.xr[a.rank] + (size_t)xpar * a.R * D + p.j_lo + tid;
+                float v = 0.0f;
+                for (int q = 0; q < a.R && x_ok; ++q) {
+                    float pv;
+                    if (q == a.rank) {
+                        pv = xo[tid];
+                    } else {
+                        unsigned long long w = ptx::ld_relaxed_sys_u64(rx + (size_t)q * D);
+                        if ((unsigned)(w >> 32) != fval) {
+                            const unsigned long long t0 = now_ns();
+                            do {
+                                if (now_ns() - t0 > kXchgTimeoutNs) {
+                                    x_ok = false;
+                                    break;
+                                }
+                                w = ptx::ld_relaxed_sys_u64(rx + (size_t)q * D);
+                            } while ((unsigned)(w >> 32) != fval);
+                        }
+                        pv = __uint_as_float((unsigned)w);
+                    }
+                    v = q == 0 ? pv : v + pv;
+                }
+                const __nv_bfloat16 xb = __float2bfloat16_rn(v);
+                if (last) a.out[p.j_lo + tid] = v;
+                else a.act[p.j_lo + tid] = xb;
+                xo[tid] = __bfloat162float(xb);
+            }
+            if (__syncthreads_or(!x_ok)) {
+                if (tid == 0) {
+                    record_status(a.status, QMOE_ERR_TIMEOUT);
+                    atomicExch(abort_word(a.sync), 1u);
+                }
+                ok = false;
+                break;
+            }
+            trace_mark(a, L, 17);
         }
         // the next layer's router columns
         if (__syncthreads_or(!last && !mbar_wait(bar_rc, (uint32_t)((L + 1) & 1)))) {
@@ -762,7 +893,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             ++iss_sdn;
         }
         if (!last) {
-            router_partial(p, S, sm, lg_next + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32);
+            router_partial(p, S, sm, lg_next + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32, xchg);
             trace_mark(a, L, 11);
             if (!grid_sync(a.sync, ++gen, a.status, s_ok)) {
                 ok = false;
@@ -770,6 +901,10 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             }
         }
     }
+
+    // This rank's launch count, read by every CTA at its start (all read it
+    // before the prologue's barrier, which CTA 0 has passed).
+    if (xchg && blockIdx.x == 0 && tid == 0) *a.epoch = epoch + 1u;
 
     // Stopped early: let this CTA's copies in flight land (bounded) before exit.
     if (!ok && tid == 0) {
@@ -790,20 +925,40 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
 
 namespace {
 
-using SKShapeC2 = SKShape<2048, 512, 10, 148>;    // BASELINE configs 1-2 on a 148-SM B200
-using SKShapeTest = SKShape<1024, 64, 10, 148>;   // a small member of the family (tests)
+// BASELINE configs 1-2 on a 148-SM B200: the whole layer (I = 512), or one
+// rank's slice of every expert's intermediate rows on 2, 4 or 8 ranks.
+using SKShapeC2 = SKShape<2048, 512, 10, 148>;
+using SKShapeC2R2 = SKShape<2048, 512, 10, 148, 256>;
+using SKShapeC2R4 = SKShape<2048, 512, 10, 148, 128>;
+using SKShapeC2R8 = SKShape<2048, 512, 10, 148, 64>;
+using SKShapeTest = SKShape<1024, 64, 10, 148>;  // a small member of the family (tests)
+
+template <class SH>
+void (*entry(unsigned* smem))(SKArgs) {
+    *smem = SH::S.total;
+    return stack_kernel<SH>;
+}
 
 // The compiled instantiation for these shapes on this device, or null.
 void (*pick_kernel(const qmoe_dims& d, int n_sm, unsigned* smem))(SKArgs) {
-    if (n_sm == 148 && d.hidden == 2048 && d.n_experts == 512 && d.top_k == 10) {
-        *smem = SKShapeC2::S.total;
-        return stack_kernel<SKShapeC2>;
+    if (n_sm != 148 || d.top_k != 10 || d.inter != 512) return nullptr;
+    if (d.hidden == 2048 && d.n_experts == 512) {
+        switch (d.inter_local) {
+            case 512: return entry<SKShapeC2>(smem);
+            case 256: return entry<SKShapeC2R2>(smem);
+            case 128: return entry<SKShapeC2R4>(smem);
+            case 64: return entry<SKShapeC2R8>(smem);
+            default: return nullptr;
+        }
     }
-    if (n_sm == 148 && d.hidden == 1024 && d.n_experts == 64 && d.top_k == 10) {
-        *smem = SKShapeTest::S.total;
-        return stack_kernel<SKShapeTest>;
-    }
+    if (d.hidden == 1024 && d.n_experts == 64 && d.inter_local == 512) return entry<SKShapeTest>(smem);
     return nullptr;
+}
+
+// The down rows in the format the kernel reads for I local columns: whole
+// super-blocks, or one segment (header + I / 32 code groups) of one.
+bool down_format_ok(int I, int nseg, int nsub) {
+    return I >= 256 ? (nseg == I / 256 && nsub == 8) : (nseg == 1 && nsub == I / 32);
 }
 
 }  // namespace
@@ -816,25 +971,37 @@ static cudaError_t encode_rows_map(CUtensorMap* m, const float* base, int cols, 
                      (unsigned long long)cols * 4, kRColW, (unsigned)(rows < kRBoxRows ? rows : kRBoxRows));
 }
 
-bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers) {
-    if (M != 1 || n_layers < 1 || n_layers > kSKMaxLayers) return false;
-    if (d.inter != 512 || d.inter_local != 512 || d.down_nseg != 2 || d.down_nsub != 8 || d.down_ib0 != 0)
-        return false;
-    if (d.sh_inter_local != 512 || d.sh_down_nseg != 2 || d.sh_down_nsub != 8 || d.sh_down_ib0 != 0) return false;
+bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers, int R) {
+    if (M != 1 || n_layers < 1 || n_layers > kSKMaxLayers || R < 1 || R > kMaxXchgRanks) return false;
     if (d.expert_lo != 0 || d.expert_hi != d.n_experts) return false;
+    const int I = d.inter_local;
+    if (!down_format_ok(I, d.down_nseg, d.down_nsub) || (I >= 256 && d.down_ib0 != 0)) return false;
+    // the shared expert sliced like the routed ones (variant B of the family: equal widths)
+    if (d.sh_inter_local != I || d.sh_down_nseg != d.down_nseg || d.sh_down_nsub != d.down_nsub ||
+        d.sh_down_ib0 != d.down_ib0)
+        return false;
+    if (R > 1 && I * R != d.inter) return false;
     unsigned smem = 0;
     return pick_kernel(d, device_sm_count(), &smem) != nullptr && smem <= 227u * 1024u;
 }
 
-cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* logits, float* h, unsigned* sync,
+cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* h, unsigned* sync,
                                 unsigned long long* trace, int* status, const qmoe_layer_weights* layers, int n_layers,
-                                const qmoe_dims& d, cudaStream_t stream) {
-    (void)logits;  // the single launch keeps its logits in the accumulators behind the barrier words
+                                const qmoe_dims& d, const XchgDesc* xc, cudaStream_t stream) {
     SKArgs a{};
+    a.R = xc ? xc->R : 1;
+    a.rank = xc ? xc->rank : 0;
+    a.ib0 = d.down_ib0;
+    if (xc) {
+        for (int q = 0; q < xc->R; ++q)
+            a.xr[q] = reinterpret_cast<unsigned long long*>(xc->buf[q] + kXchgHeader);
+        a.epoch = reinterpret_cast<unsigned*>(xc->buf[xc->rank]);
+    }
     a.trace = trace;
     a.x = reinterpret_cast<const __nv_bfloat16*>(x);
     a.out = out;
     a.act = reinterpret_cast<__nv_bfloat16*>(act);
+    // the single launch keeps its logits in the accumulators behind the barrier words
     a.logits = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(sync) + 1152);
     a.hmax = reinterpret_cast<unsigned*>(reinterpret_cast<unsigned char*>(sync) + 1152 + stack_logit_bytes(d.n_experts));
     a.h = h;

@@ -22,6 +22,15 @@ from .moe import Workspace, _stream
 from .weights import DeviceLayer
 
 
+# The single-launch kernel's phase stamps per layer (qmoe_read_stack_trace).
+TRACE_SLOTS = 24
+TRACE_POINTS = ("B start", "top-k done", "gate|up copies issued", "down copies issued (warp 1)",
+                "copies done", "gate|up rows done", "h written", "after barrier H", "h converted",
+                "down resident", "down done", "router partial done", "top-k: logits loaded", "top-k: x converted",
+                "top-k: threshold found", "top-k: ranked", "exchange: partial rows sent",
+                "exchange: peers' rows summed")
+
+
 class MoEStack:
     def __init__(self, layers: list[DeviceLayer], max_tokens: int = 16, use_graph: bool = True):
         if not layers:
@@ -43,18 +52,15 @@ class MoEStack:
     def n_layers(self) -> int:
         return len(self.layers)
 
-    TRACE_POINTS = ("B start", "top-k done", "gate|up copies issued", "down copies issued (warp 1)",
-                    "copies done", "gate|up rows done", "h written", "after barrier H", "h converted",
-                    "down resident", "down done", "router partial done", "top-k: logits loaded", "top-k: x converted",
-                    "top-k: threshold found", "top-k: ranked")
+    TRACE_POINTS = TRACE_POINTS
 
     def phase_trace(self, m: int = 1):
         """Raw SM cycle-counter stamps of the last single-launch step,
-        [2, n_layers, 16]: CTA 0 then the last CTA, in the order of
-        TRACE_POINTS."""
+        [2, n_layers, TRACE_SLOTS]: CTA 0 then the last CTA, in the order of
+        TRACE_POINTS (later slots unused)."""
         import numpy as np
 
-        buf = np.zeros((2, self.n_layers, 16), dtype=np.uint64)
+        buf = np.zeros((2, self.n_layers, TRACE_SLOTS), dtype=np.uint64)
         check(lib.qmoe_read_stack_trace(self.ws.ptr, ctypes.byref(self.dims), m, self.n_layers,
                                         buf.ctypes.data, _stream()), "qmoe_read_stack_trace")
         return buf
