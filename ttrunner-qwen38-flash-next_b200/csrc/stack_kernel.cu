@@ -724,7 +724,8 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 // slice meets the shared one); one atomic per group
                 const unsigned grp = __match_any_sync(0xffffffffu, b);
                 const unsigned m = __reduce_max_sync(grp, bits);
-                if (b >= 0 && lane == __ffs(grp) - 1) atomicMax(hm + b * 32, m);
+                if (b >= 0 && lane == __ffs(grp) - 1)  // no return value: nothing waits for the L2 round trip
+                    asm volatile("red.global.max.u32 [%0], %1;" ::"l"(hm + b * 32), "r"(m) : "memory");
             }
         }
         trace_mark(a, L, 6);
