@@ -528,7 +528,9 @@ __device__ __forceinline__ void issue_down(const SKLayer& W, const SKPart& p, co
                       W.down + (size_t)ids[lane] * p.DNE + (size_t)p.jc_lo * p.DRB, (uint32_t)(nc * p.DRB), bar_dn);
 }
 
-template <class SH>
+// XC: this launch exchanges partial rows with peer ranks (a.R > 1); one rank
+// compiles without any of it.
+template <class SH, bool XC>
 __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_constant__ SKArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -573,10 +575,11 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     if (tid == 0) {
         for (int i = 0; i < nbars; ++i) mbar_init(bars + i, 1);
         ptx::fence_mbar_init();
-        *s_epoch = a.R > 1 ? __ldcg(a.epoch) : 0u;
+        *s_epoch = XC ? __ldcg(a.epoch) : 0u;
     }
     __syncthreads();
-    const bool xchg = a.R > 1;
+    constexpr bool xchg = XC;
+    const int ib0 = SH::I >= 256 ? 0 : a.ib0;  // whole super-blocks start at sub-block 0
     const unsigned epoch = *s_epoch;
     // Phases issued (kept by thread 0 in registers), for the bounded drain:
     // the prefetch barriers (shared rows, shared down rows, router columns) and
@@ -659,7 +662,8 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             // this layer's second barrier).
             for (int g = tid - 64; g < kStackLogitReplicas * G; g += kSKThreads - 64) {
                 *reinterpret_cast<float4*>(lg_next + g * 32) = make_float4(0.f, 0.f, 0.f, 0.f);
-                *reinterpret_cast<float4*>(lg_next + g * 32 + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+                if constexpr (XC)  // four fp64 logits per line
+                    *reinterpret_cast<float4*>(lg_next + g * 32 + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
         __syncthreads();
@@ -813,10 +817,10 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 const int s = t / (I / 32), b = t - s * (I / 32);
                 const uint8_t* row = s < K ? dbuf + ((size_t)s * S.NJR + jo + j) * p.DRB : sdn + (size_t)(jo + j) * p.DRB;
                 const float wgt = s < K ? tkv[s] * inv_psum : gate;
-                acc += wgt * down_unit_one(row, hq + s * p.NSBH * 16, hs + s * p.NSBH, p.NSBH, b, a.ib0);
+                acc += wgt * down_unit_one(row, hq + s * p.NSBH * 16, hs + s * p.NSBH, p.NSBH, b, ib0);
             }
             acc = warp_sum(acc);
-            if (!xchg) {
+            if constexpr (!xchg) {
                 if (lane == 0) {
                     const __nv_bfloat16 xb = __float2bfloat16_rn(acc);
                     if (last) a.out[p.j_lo + j] = acc;
@@ -833,7 +837,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                         ((unsigned long long)fval << 32) | __float_as_uint(acc));
             }
         }
-        if (xchg) {
+        if constexpr (xchg) {
             trace_mark(a, L, 16);
             __syncthreads();
             // Row j_lo + tid: the R partials summed in rank order (the same
@@ -935,24 +939,28 @@ using SKShapeC2R8 = SKShape<2048, 512, 10, 148, 64>;
 using SKShapeTest = SKShape<1024, 64, 10, 148>;  // a small member of the family (tests)
 
 template <class SH>
-void (*entry(unsigned* smem))(SKArgs) {
+void (*entry(unsigned* smem, bool xc))(SKArgs) {
     *smem = SH::S.total;
-    return stack_kernel<SH>;
+    if constexpr (SH::I < 512) {
+        if (xc) return stack_kernel<SH, true>;
+    }
+    return xc ? nullptr : stack_kernel<SH, false>;
 }
 
-// The compiled instantiation for these shapes on this device, or null.
-void (*pick_kernel(const qmoe_dims& d, int n_sm, unsigned* smem))(SKArgs) {
+// The compiled instantiation for these shapes on this device (xc: with the
+// exchange between ranks), or null.
+void (*pick_kernel(const qmoe_dims& d, int n_sm, unsigned* smem, bool xc))(SKArgs) {
     if (n_sm != 148 || d.top_k != 10 || d.inter != 512) return nullptr;
     if (d.hidden == 2048 && d.n_experts == 512) {
         switch (d.inter_local) {
-            case 512: return entry<SKShapeC2>(smem);
-            case 256: return entry<SKShapeC2R2>(smem);
-            case 128: return entry<SKShapeC2R4>(smem);
-            case 64: return entry<SKShapeC2R8>(smem);
+            case 512: return entry<SKShapeC2>(smem, xc);
+            case 256: return entry<SKShapeC2R2>(smem, xc);
+            case 128: return entry<SKShapeC2R4>(smem, xc);
+            case 64: return entry<SKShapeC2R8>(smem, xc);
             default: return nullptr;
         }
     }
-    if (d.hidden == 1024 && d.n_experts == 64 && d.inter_local == 512) return entry<SKShapeTest>(smem);
+    if (d.hidden == 1024 && d.n_experts == 64 && d.inter_local == 512) return entry<SKShapeTest>(smem, xc);
     return nullptr;
 }
 
@@ -983,7 +991,7 @@ bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers, int R) {
         return false;
     if (R > 1 && I * R != d.inter) return false;
     unsigned smem = 0;
-    return pick_kernel(d, device_sm_count(), &smem) != nullptr && smem <= 227u * 1024u;
+    return pick_kernel(d, device_sm_count(), &smem, R > 1) != nullptr && smem <= 227u * 1024u;
 }
 
 cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* h, unsigned* sync,
@@ -1023,7 +1031,7 @@ cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* h,
     }
     const int n = device_sm_count();
     unsigned smem = 0;
-    void (*kern)(SKArgs) = pick_kernel(d, n, &smem);
+    void (*kern)(SKArgs) = pick_kernel(d, n, &smem, xc != nullptr);
     if (!kern) return cudaErrorInvalidValue;
     for (int l = 0; l < n_layers; ++l) {
         cudaError_t e = encode_rows_map(&a.rmap[l], layers[l].router, d.hidden, d.n_experts);
