@@ -164,7 +164,8 @@ int qmoe_stack_single_launch(const qmoe_dims* dims, int n_tokens, int n_layers);
  * done, gate|up rows done, h written, after barrier H, h converted, down
  * resident, down done, router partial done (0-11); inside the top-k: logits
  * loaded, x converted, threshold found, ranked (12-15); with an exchange
- * between ranks: partial rows sent, peers' rows summed (16-17).  The last
+ * between ranks: partial rows sent, peers' rows summed (16-17); gate|up
+ * chunks 0-5 landed, as seen by the warp of the chunk's first pair (18-23).  The last
  * CTA stamps the same points.  Copies the n_layers x 24 stamps of CTA 0 and
  * then those of the last CTA (2 x n_layers x 24 values) of the last launch
  * made with this workspace and n_tokens to host_out (synchronises `stream`).

@@ -259,27 +259,43 @@ __device__ bool grid_sync(unsigned* sync, unsigned gen, int* status, int* s_ok) 
     return *s_ok != 0;
 }
 
-// One IQ4_XS row of D = 1024 * SBL2 values dotted with the activation in
-// block floating point held in registers; lane l owns sub-blocks
-// l*SBL2 .. l*SBL2+SBL2-1, all in one super-block, so one header load.
+// Two IQ4_XS rows of D = 1024 * SBL2 values (a pair's gate and up rows)
+// dotted with the activation in block floating point held in registers,
+// decoded side by side so that their loads, decodes and reductions overlap;
+// lane l owns sub-blocks l*SBL2 .. l*SBL2+SBL2-1, all in one super-block, so
+// one header load per row.
 template <int SBL2>
-__device__ __forceinline__ float row_dot(const uint8_t* row, const int (&xr)[SBL2][16], const float (&xs)[SBL2],
-                                      int lane) {
+__device__ __forceinline__ void row_dot2(const uint8_t* row_a, const uint8_t* row_b, const int (&xr)[SBL2][16],
+                                         const float (&xs)[SBL2], int lane, float& out_a, float& out_b) {
     const int b0 = lane * SBL2;
-    const uint8_t* blk = row + (b0 >> 3) * QMOE_SB_BYTES;
-    const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
-    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
-    float acc = 0.0f;
+    const uint8_t* blk_a = row_a + (b0 >> 3) * QMOE_SB_BYTES;
+    const uint8_t* blk_b = row_b + (b0 >> 3) * QMOE_SB_BYTES;
+    const uint2 ha = *reinterpret_cast<const uint2*>(blk_a);
+    const uint2 hb = *reinterpret_cast<const uint2*>(blk_b);
+    const float da = __half2float(__ushort_as_half((unsigned short)(ha.x & 0xFFFFu)));
+    const float db = __half2float(__ushort_as_half((unsigned short)(hb.x & 0xFFFFu)));
+    float acc_a = 0.0f, acc_b = 0.0f;
 #pragma unroll
     for (int i = 0; i < SBL2; ++i) {
         const int ib = (b0 + i) & 7;
-        const uint2 q0 = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
-        const uint2 q1 = *reinterpret_cast<const uint2*>(blk + 16 + 16 * ib);
-        const int S = qmoe_subblock_dot(q0.x, q0.y, q1.x, q1.y, xr[i], 0);
-        const float dl = d * (float)(qmoe_iq4xs_ls(hdr.x, hdr.y, ib) - 32);
-        acc = fmaf(dl * xs[i], (float)S, acc);
+        const uint2 a0 = *reinterpret_cast<const uint2*>(blk_a + 8 + 16 * ib);
+        const uint2 a1 = *reinterpret_cast<const uint2*>(blk_a + 16 + 16 * ib);
+        const uint2 c0 = *reinterpret_cast<const uint2*>(blk_b + 8 + 16 * ib);
+        const uint2 c1 = *reinterpret_cast<const uint2*>(blk_b + 16 + 16 * ib);
+        const int Sa = qmoe_subblock_dot(a0.x, a0.y, a1.x, a1.y, xr[i], 0);
+        const int Sb = qmoe_subblock_dot(c0.x, c0.y, c1.x, c1.y, xr[i], 0);
+        const float dla = da * (float)(qmoe_iq4xs_ls(ha.x, ha.y, ib) - 32);
+        const float dlb = db * (float)(qmoe_iq4xs_ls(hb.x, hb.y, ib) - 32);
+        acc_a = fmaf(dla * xs[i], (float)Sa, acc_a);
+        acc_b = fmaf(dlb * xs[i], (float)Sb, acc_b);
     }
-    return warp_sum(acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        acc_a += __shfl_xor_sync(0xffffffffu, acc_a, o);
+        acc_b += __shfl_xor_sync(0xffffffffu, acc_b, o);
+    }
+    out_a = acc_a;
+    out_b = acc_b;
 }
 
 // Block floating point of a 32-value block given its largest |v| as float
@@ -311,7 +327,7 @@ __device__ __forceinline__ void convert_block(float v, int* q16, float* step, in
     if (lane == 0) *step = st;
 }
 
-// The activation's block-floating-point words and steps for row_dot: lane l
+// The activation's block-floating-point words and steps for row_dot2: lane l
 // takes sub-blocks l*SBL2 .. l*SBL2+SBL2-1.
 template <int SBL2>
 __device__ __forceinline__ void load_xr(const int* xq, const float* xs, int lane, int (&xr)[SBL2][16],
@@ -675,21 +691,34 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             // Row tasks: the shared expert's 2 * nsq rows (prefetched), then the
             // routed pairs' gate and up rows as their chunks land.
             const bool w_ok = mbar_wait(bar_sgu, par);
-            const int ns = 2 * nsq;
-            for (int t = warp; t < ns + 2 * np && ok && w_ok; t += kSKWarps) {
-                if (t < ns) {
-                    const uint8_t* row = sgu + (size_t)((t & 1) ? (S.NSQ + (t >> 1)) : (t >> 1)) * p.RB;
-                    const float r = row_dot<SBL2>(row, xr, xsr, lane);
-                    if (lane == 0) ((t & 1) ? suv : sgv)[t >> 1] = r;
+            // Pair tasks: the shared expert's nsq pairs (prefetched), then the
+            // routed pairs as their chunks land; a warp decodes a pair's gate
+            // and up rows side by side.
+            for (int t = warp; t < nsq + np && ok && w_ok; t += kSKWarps) {
+                const uint8_t *rg, *ru;
+                float *dg, *du;
+                if (t < nsq) {
+                    rg = sgu + (size_t)t * p.RB;
+                    ru = sgu + (size_t)(S.NSQ + t) * p.RB;
+                    dg = sgv + t;
+                    du = suv + t;
                 } else {
-                    const int tt = t - ns, u = tt >> 1;
+                    const int u = t - nsq;
                     if (!mbar_wait(bar_ch + u / kSKChunk, par)) {
                         ok = false;
                         break;
                     }
-                    const uint8_t* row = ((tt & 1) ? ubuf : gbuf) + (size_t)u * p.RB;
-                    const float r = row_dot<SBL2>(row, xr, xsr, lane);
-                    if (lane == 0) ((tt & 1) ? uv : gv)[u] = r;
+                    if (u % kSKChunk == 0) trace_mark(a, L, 18 + u / kSKChunk, 32 * warp);  // chunk landed
+                    rg = gbuf + (size_t)u * p.RB;
+                    ru = ubuf + (size_t)u * p.RB;
+                    dg = gv + u;
+                    du = uv + u;
+                }
+                float g, up;
+                row_dot2<SBL2>(rg, ru, xr, xsr, lane, g, up);
+                if (lane == 0) {
+                    *dg = g;
+                    *du = up;
                 }
             }
             if (!w_ok) ok = false;

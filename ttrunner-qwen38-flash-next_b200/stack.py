@@ -28,7 +28,8 @@ TRACE_POINTS = ("B start", "top-k done", "gate|up copies issued", "down copies i
                 "copies done", "gate|up rows done", "h written", "after barrier H", "h converted",
                 "down resident", "down done", "router partial done", "top-k: logits loaded", "top-k: x converted",
                 "top-k: threshold found", "top-k: ranked", "exchange: partial rows sent",
-                "exchange: peers' rows summed")
+                "exchange: peers' rows summed", "gate|up chunk 0 landed", "chunk 1 landed", "chunk 2 landed",
+                "chunk 3 landed", "chunk 4 landed", "chunk 5 landed")
 
 
 class MoEStack:
