@@ -136,7 +136,7 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     s.xq = sk_take(o, NSB * 64);
     s.xs = sk_take(o, NSB * 4);
     s.rcol = sk_take(o, (unsigned)(((E + kRBoxRows - 1) / kRBoxRows) * kRBoxRows + 1) * kRColW * 4);
-    s.xo = sk_take(o, (unsigned)s.NJ * 4);
+    s.xo = sk_take(o, (unsigned)(s.NJ > kRColW ? s.NJ : kRColW) * 4);  // the router-column window's x
     s.sgu = sk_take(o, 2u * s.NSQ * RB);
     s.sdn = sk_take(o, (unsigned)s.NJR * DRB);
     s.gbuf = sk_take(o, (unsigned)s.NP * RB);
@@ -444,27 +444,45 @@ __device__ __forceinline__ void issue_rcol(const CUtensorMap* rmap, const CUtens
     ptx::tma_load_2d(rcol + nbox * kRBoxRows * kRColW, gmap, x, 0, bar);
 }
 
+// Row r of the router-column window (kRColW floats from column j_lo & ~3)
+// dotted with x over the same window: 16-byte loads (the 8 rows a quarter
+// warp reads, 80 bytes apart, fall in 8 distinct bank groups).  The window's
+// columns outside this CTA's rows hold x = 0 and add exact zeros, so the sum
+// runs over the CTA's columns in order, as a plain loop over them would
+// (router weights are finite).
+__device__ __forceinline__ float rcol_dot(const float* row, const float4* x4) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    float v = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kRColW / 4; ++q) {
+        const float4 r = r4[q], x = x4[q];
+        v = fmaf(r.x, x.x, v);
+        v = fmaf(r.y, x.y, v);
+        v = fmaf(r.z, x.z, v);
+        v = fmaf(r.w, x.w, v);
+    }
+    return v;
+}
+
 // This CTA's share of the router logits: thread e (and thread 0 for the gate
-// row E) sums rcol[e][j] * x[j_lo + j] over its j.  fp32 accumulators: four
+// row E) sums rcol[e][j] * x[j] over its columns j.  fp32 accumulators: four
 // consecutive experts combine into one vector atomic add on their line; fp64
 // (f64): one atomic add per logit, four per line.
 __device__ __forceinline__ void router_partial(const SKPart& p, const SKLayout& S, const unsigned char* sm,
                                                float* acc_buf, bool f64) {
-    const float* xo = reinterpret_cast<const float*>(sm + S.xo);
-    const float* rcol = reinterpret_cast<const float*>(sm + S.rcol) + (p.j_lo & 3);  // column j_lo of row 0
-    const int nj = p.j_hi - p.j_lo, e = threadIdx.x, lane = threadIdx.x & 31;
+    const float4* x4 = reinterpret_cast<const float4*>(sm + S.xo);
+    const float* rcol = reinterpret_cast<const float*>(sm + S.rcol);
+    const int e = threadIdx.x, lane = threadIdx.x & 31;
     const int gate_row = ((p.E + kRBoxRows - 1) / kRBoxRows) * kRBoxRows;
     float v = 0.0f;
-    if (e < p.E)
-        for (int j = 0; j < nj; ++j) v = fmaf(rcol[e * S.RJ + j], xo[j], v);
+    if (e < p.E) v = rcol_dot(rcol + e * kRColW, x4);
     if (f64) {
         double* acc64 = reinterpret_cast<double*>(acc_buf);
         if (e < p.E)
             asm volatile("red.global.add.f64 [%0], %1;" ::"l"(acc64 + (e >> 2) * 16 + (e & 3)), "d"((double)v)
                          : "memory");
         if (e == 0) {
-            float g = 0.0f;
-            for (int j = 0; j < nj; ++j) g = fmaf(rcol[gate_row * S.RJ + j], xo[j], g);
+            const float g = rcol_dot(rcol + gate_row * kRColW, x4);
             asm volatile("red.global.add.f64 [%0], %1;" ::"l"(acc64 + (p.E >> 2) * 16 + (p.E & 3)), "d"((double)g)
                          : "memory");
         }
@@ -476,11 +494,7 @@ __device__ __forceinline__ void router_partial(const SKPart& p, const SKLayout& 
         asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(acc_buf + (e >> 2) * 32), "f"(v), "f"(v1),
                      "f"(v2), "f"(v3)
                      : "memory");
-    if (e == 0) {
-        float g = 0.0f;
-        for (int j = 0; j < nj; ++j) g = fmaf(rcol[gate_row * S.RJ + j], xo[j], g);
-        atomicAdd(acc_buf + (p.E >> 2) * 32 + (p.E & 3), g);
-    }
+    if (e == 0) atomicAdd(acc_buf + (p.E >> 2) * 32 + (p.E & 3), rcol_dot(rcol + gate_row * kRColW, x4));
 }
 
 // This CTA's routed pairs [p_lo, p_hi) fall in at most two expert slots: the
@@ -559,7 +573,10 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
 
     int* xq = reinterpret_cast<int*>(sm + S.xq);
     float* xs = reinterpret_cast<float*>(sm + S.xs);
+    // xo: x over the router-column window [j_lo & ~3, +kRColW); row j of this
+    // CTA's slice at xo[xw + j], the rest zero
     float* xo = reinterpret_cast<float*>(sm + S.xo);
+    const int xw = p.j_lo & 3;
     const uint8_t* sgu = sm + S.sgu;
     const uint8_t* sdn = sm + S.sdn;
     const uint8_t* gbuf = sm + S.gbuf;
@@ -609,7 +626,10 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     }
 
     // ---------------- prologue: layer 0's router logits --------------------
-    if (tid < nj) xo[tid] = __bfloat162float(a.x[p.j_lo + tid]);
+    if (tid < kRColW) {
+        const int j = tid - xw;
+        xo[tid] = j >= 0 && j < nj ? __bfloat162float(a.x[p.j_lo + j]) : 0.0f;
+    }
     bool ok = !__syncthreads_or(!mbar_wait(bar_rc, 0));
     if (ok) router_partial(p, S, sm, a.logits + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32, xchg);
     else if (tid == 0) {
@@ -854,12 +874,12 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                     const __nv_bfloat16 xb = __float2bfloat16_rn(acc);
                     if (last) a.out[p.j_lo + j] = acc;
                     else a.act[p.j_lo + j] = xb;
-                    xo[j] = __bfloat162float(xb);
+                    xo[xw + j] = __bfloat162float(xb);
                 }
             } else {
                 // this rank's partial of row j: kept, and stored into every
                 // peer as one word (value bits, flag)
-                if (lane == 0) xo[j] = acc;
+                if (lane == 0) xo[xw + j] = acc;
                 if (lane < a.R && lane != a.rank)
                     ptx::st_relaxed_sys_u64(
                         a.xr[lane] + ((size_t)(xpar * a.R + a.rank) * D + p.j_lo + j),
@@ -879,7 +899,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 for (int q = 0; q < a.R && x_ok; ++q) {
                     float pv;
                     if (q == a.rank) {
-                        pv = xo[tid];
+                        pv = xo[xw + tid];
                     } else {
                         unsigned long long w = ptx::ld_relaxed_sys_u64(rx + (size_t)q * D);
                         if ((unsigned)(w >> 32) != fval) {
@@ -899,7 +919,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 const __nv_bfloat16 xb = __float2bfloat16_rn(v);
                 if (last) a.out[p.j_lo + tid] = v;
                 else a.act[p.j_lo + tid] = xb;
-                xo[tid] = __bfloat162float(xb);
+                xo[xw + tid] = __bfloat162float(xb);
             }
             if (__syncthreads_or(!x_ok)) {
                 if (tid == 0) {
@@ -921,11 +941,12 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             break;
         }
         trace_mark(a, L, 10);
-        if (tid == 0 && !last) {
+        // warp 1 issues the next layer's shared down rows (thread 0 also adds the gate row below)
+        if (tid == 32 && !last) {
             ptx::fence_proxy_async();
             issue_sdn(a.L[L + 1], p, S, sm, bar_sdn);
-            ++iss_sdn;
         }
+        if (tid == 0 && !last) ++iss_sdn;
         if (!last) {
             router_partial(p, S, sm, lg_next + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32, xchg);
             trace_mark(a, L, 11);
