@@ -497,38 +497,73 @@ __global__ void pf_convert_kernel(const void* x, int x_f32, size_t n, __nv_bfloa
 
 // logits[t][e] = x_t . R_e in fp32 for e < E and the gate vector at e = E.
 // Tile: 64 tokens x 64 router rows, K step 32, 4 x 4 outputs per thread.
+// Router logits of a chunk, fp32: logits[t][e] = x_t . R_e, row E the gate
+// vector (zero without one).  64 x 64 tiles of (tokens, router rows), 256
+// threads each holding a 4 x 4 block; K in steps of 32, each step's operands
+// loaded with 16-byte loads one step ahead of the arithmetic.  When the tiles
+// alone would leave SMs idle (small chunks), grid.z splits K into equal
+// chunks whose partials go to part[z] and are summed in chunk order by
+// pf_logit_reduce_kernel: the same bits on every run.
+constexpr int kRtK = 32;
+
 __global__ void __launch_bounds__(256) pf_router_kernel(const __nv_bfloat16* __restrict__ xb, int T, int D,
                                                         const float* __restrict__ router,
-                                                        const float* __restrict__ gate_vec, int E,
-                                                        float* __restrict__ logits) {
-    __shared__ float xs[32][64 + 4];
-    __shared__ float rs[32][64 + 4];
+                                                        const float* __restrict__ gate_vec, int E, int k_chunk,
+                                                        float* __restrict__ out) {
+    __shared__ __align__(16) float xs[kRtK][64 + 4];
+    __shared__ __align__(16) float rs[kRtK][64 + 4];
     const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64, tid = threadIdx.x;
+    const int kb = blockIdx.z * k_chunk, nsteps = k_chunk / kRtK;
     const int tr = tid >> 4, tcol = tid & 15;
+    // loader: row lr of the tile, 8 consecutive k at lk
+    const int lr = tid >> 2, lk = (tid & 3) * 8;
+    const int t = t0 + lr, e = e0 + lr;
+    const __nv_bfloat16* xrow = t < T ? xb + (size_t)t * D + kb + lk : nullptr;
+    const float* rrow = e < E ? router + (size_t)e * D + kb + lk : (e == E && gate_vec ? gate_vec + kb + lk : nullptr);
+    uint4 xv4 = make_uint4(0u, 0u, 0u, 0u);
+    float4 r0 = make_float4(0.f, 0.f, 0.f, 0.f), r1 = r0;
+    if (xrow) xv4 = __ldg(reinterpret_cast<const uint4*>(xrow));
+    if (rrow) {
+        r0 = __ldg(reinterpret_cast<const float4*>(rrow));
+        r1 = __ldg(reinterpret_cast<const float4*>(rrow) + 1);
+    }
     float acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-    for (int k0 = 0; k0 < D; k0 += 32) {
-        for (int i = tid; i < 64 * 32; i += 256) {
-            const int r = i >> 5, kk = i & 31;
-            const int t = t0 + r, e = e0 + r;
-            xs[kk][r] = t < T ? __bfloat162float(xb[(size_t)t * D + k0 + kk]) : 0.0f;
-            float w = 0.0f;
-            if (e < E) w = __ldg(router + (size_t)e * D + k0 + kk);
-            else if (e == E && gate_vec) w = __ldg(gate_vec + k0 + kk);
-            rs[kk][r] = w;
+    for (int st = 0; st < nsteps; ++st) {
+        {
+            const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv4);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 f = __bfloat1622float2(xp[q]);
+                xs[lk + 2 * q][lr] = f.x;
+                xs[lk + 2 * q + 1][lr] = f.y;
+            }
+            rs[lk + 0][lr] = r0.x;
+            rs[lk + 1][lr] = r0.y;
+            rs[lk + 2][lr] = r0.z;
+            rs[lk + 3][lr] = r0.w;
+            rs[lk + 4][lr] = r1.x;
+            rs[lk + 5][lr] = r1.y;
+            rs[lk + 6][lr] = r1.z;
+            rs[lk + 7][lr] = r1.w;
         }
         __syncthreads();
-#pragma unroll 8
-        for (int kk = 0; kk < 32; ++kk) {
-            float xv[4], rv[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                xv[i] = xs[kk][tr * 4 + i];
-                rv[i] = rs[kk][tcol * 4 + i];
+        if (st + 1 < nsteps) {  // the next step's operands, in flight during this step's arithmetic
+            const int off = (st + 1) * kRtK;
+            if (xrow) xv4 = __ldg(reinterpret_cast<const uint4*>(xrow + off));
+            if (rrow) {
+                r0 = __ldg(reinterpret_cast<const float4*>(rrow + off));
+                r1 = __ldg(reinterpret_cast<const float4*>(rrow + off) + 1);
             }
+        }
+#pragma unroll 8
+        for (int kk = 0; kk < kRtK; ++kk) {
+            const float4 xq = *reinterpret_cast<const float4*>(&xs[kk][tr * 4]);
+            const float4 rq = *reinterpret_cast<const float4*>(&rs[kk][tcol * 4]);
+            const float xv[4] = {xq.x, xq.y, xq.z, xq.w}, rv[4] = {rq.x, rq.y, rq.z, rq.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -536,16 +571,36 @@ __global__ void __launch_bounds__(256) pf_router_kernel(const __nv_bfloat16* __r
         }
         __syncthreads();
     }
+    float* o = out + (size_t)blockIdx.z * T * (E + 1);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const int t = t0 + tr * 4 + i;
-        if (t >= T) continue;
+        const int tt = t0 + tr * 4 + i;
+        if (tt >= T) continue;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int e = e0 + tcol * 4 + j;
-            if (e <= E) logits[(size_t)t * (E + 1) + e] = acc[i][j];
+            const int ee = e0 + tcol * 4 + j;
+            if (ee <= E) o[(size_t)tt * (E + 1) + ee] = acc[i][j];
         }
     }
+}
+
+// logits[i] = part[0][i] + part[1][i] + ... in chunk order.
+__global__ void __launch_bounds__(256) pf_logit_reduce_kernel(const float* __restrict__ part, int S, size_t n,
+                                                              float* __restrict__ logits) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v = part[i];
+        for (int s = 1; s < S; ++s) v += part[(size_t)s * n + i];
+        logits[i] = v;
+    }
+}
+
+// K chunks of the router GEMM for a chunk of T tokens: enough CTAs to cover
+// the SMs, each chunk a multiple of 256 columns.
+int router_splits(int T, int E, int D) {
+    const int tiles = ((T + 63) / 64) * ((E + 1 + 63) / 64);
+    int S = 1;
+    while (S * 2 * tiles <= 2 * 148 && D % (S * 2 * 256) == 0) S *= 2;
+    return S;
 }
 
 constexpr int kTopkWarps = 8;
@@ -703,7 +758,8 @@ __global__ void __launch_bounds__(kPlaceWarps * 32) pf_place_kernel(const int32_
 // ---- workspace and launches ---------------------------------------------------
 
 struct PfLayout {
-    size_t status, meta, trace, xb, logits, ids, weights, slog, counts, offsets, ntiles, slot_tok, slot_w, h, xg, total;
+    size_t status, meta, trace, xb, logits, part, ids, weights, slog, counts, offsets, ntiles, slot_tok, slot_w, h, xg,
+        total;
     int max_ntiles, rows;
 };
 
@@ -723,6 +779,11 @@ PfLayout pf_layout(const qmoe_dims& d, int T) {
     o = pf_align(o + (size_t)T * d.hidden * 2);
     L.logits = o;
     o = pf_align(o + (size_t)T * G * 4);
+    L.part = o;  // the router's K-chunk partials when it splits K
+    {
+        const int S = router_splits(T, E, d.hidden);
+        o = pf_align(o + (S > 1 ? (size_t)S * T * G * 4 : 0));
+    }
     L.ids = o;
     o = pf_align(o + (size_t)T * k * 4);
     L.weights = o;
@@ -789,9 +850,17 @@ cudaError_t launch_prefill_route(const __nv_bfloat16* xb, int T, const qmoe_laye
     const PfLayout L = pf_layout(d, T);
     int* status = reinterpret_cast<int*>(ws + L.status);
     const int E = d.n_experts;
-    dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 1 + 63) / 64));
-    pf_router_kernel<<<grid, 256, 0, s>>>(xb, T, d.hidden, w.router, w.gate_vec, E,
-                                          reinterpret_cast<float*>(ws + L.logits));
+    const int S = router_splits(T, E, d.hidden);
+    float* logits = reinterpret_cast<float*>(ws + L.logits);
+    dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 1 + 63) / 64), (unsigned)S);
+    pf_router_kernel<<<grid, 256, 0, s>>>(xb, T, d.hidden, w.router, w.gate_vec, E, d.hidden / S,
+                                          S > 1 ? reinterpret_cast<float*>(ws + L.part) : logits);
+    if (S > 1) {
+        const size_t n = (size_t)T * (E + 1);
+        const size_t blocks = (n + 255) / 256;
+        pf_logit_reduce_kernel<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, s>>>(
+            reinterpret_cast<const float*>(ws + L.part), S, n, logits);
+    }
     pf_topk_kernel<<<(unsigned)((T + kTopkWarps - 1) / kTopkWarps), kTopkWarps * 32, 0, s>>>(
         reinterpret_cast<const float*>(ws + L.logits), T, E, d.top_k, w.gate_vec ? 1 : 0, ids, weights,
         shared_logit, status);
