@@ -271,6 +271,15 @@ int qmoe_moe_block_noalloc(const void* x, int x_dtype, int n_tokens, const qmoe_
  * outputs are summed with fp32 atomics, so the low bits of `out` may differ
  * between runs. */
 int qmoe_prefill_max_tokens(void);
+/* Experts that see at most this many tokens of a chunk (default 8, at most
+ * 8) skip the bf16 expansion and run as a grouped GEMV: each IQ4_XS row is
+ * decoded once with the decode path's integer core and dotted with every
+ * token of the group; larger groups take the tcgen05 grouped GEMM.  n >= 0
+ * sets it (0: every group on the tensor cores), n < 0 only queries; returns
+ * the previous value.  Process-wide, read when a call is issued.  The
+ * reference has no counterpart (its prefill runs every group through the
+ * same matmul, tt/moe.py:330-368). */
+int qmoe_prefill_small_group_max(int n);
 size_t qmoe_prefill_workspace_bytes(const qmoe_dims* dims, int n_tokens);
 /* ids [T, top_k] int32 and weights [T, top_k] fp32 (renormalised, descending,
  * ties to the lower id); shared_logit [T] (x . gate_vec) or NULL. */

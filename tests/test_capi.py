@@ -129,3 +129,15 @@ def test_host_quantiser_edge_values(pkg, oracle):
 def test_quantiser_rejects_partial_blocks(pkg):
     with pytest.raises(ValueError):
         pkg.weights.quantize_host(np.zeros((3, 100), np.float32))
+
+
+def test_prefill_small_group_threshold(pkg):
+    """The grouped-GEMV threshold: query, set, clamp to 8, restore (host state only)."""
+    lib = pkg._lib.lib
+    prev = lib.qmoe_prefill_small_group_max(-1)
+    assert prev == 8
+    assert lib.qmoe_prefill_small_group_max(3) == 8
+    assert lib.qmoe_prefill_small_group_max(-1) == 3
+    assert lib.qmoe_prefill_small_group_max(100) == 3
+    assert lib.qmoe_prefill_small_group_max(-1) == 8
+    lib.qmoe_prefill_small_group_max(prev)

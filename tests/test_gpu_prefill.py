@@ -1,4 +1,5 @@
-"""Chunked prefill (grouped tcgen05 GEMMs) vs the CPU oracle.
+"""Chunked prefill (grouped tcgen05 GEMMs, and the grouped GEMV for experts
+with at most 8 tokens) vs the CPU oracle.
 
 one layer of the config-1 shape (hidden 2048, inter 512,
 512 experts, top-10 + shared), chunks of T = 128 and 2048 tokens, x ~ N(0,1)
@@ -132,3 +133,26 @@ def test_prefill_matches_decode_path(pkg, c1):
     torch.cuda.synchronize()
     d = (a - b).abs().max().item() / b.abs().max().item()
     assert d <= TOL
+
+
+@pytest.mark.parametrize("T", [5, 128, 300])
+def test_prefill_small_groups_both_paths(pkg, oracle, c1, T):
+    """The same chunk with every group on the tensor cores and with the small
+    groups (<= 8 tokens; at T = 5 the shared group too) on the grouped GEMV:
+    both within the bar of the oracle and of each other."""
+    hl, dl, layer = c1
+    x = _x(T, seed=200 + T)
+    ref = _oracle(oracle, hl, x, hl.cfg.top_k)
+    lib = pkg._lib.lib
+    prev = lib.qmoe_prefill_small_group_max(0)
+    try:
+        tc = layer.prefill(x.cuda()).clone()
+        lib.qmoe_prefill_small_group_max(8)
+        gv = layer.prefill(x.cuda()).clone()
+    finally:
+        lib.qmoe_prefill_small_group_max(prev)
+    torch.cuda.synchronize()
+    pkg.moe.prefill_workspace_for(layer.dims, T, gv.device).raise_if_error("prefill")
+    assert oracle.max_rel_err(tc.cpu().numpy(), ref["out"]) <= TOL
+    assert oracle.max_rel_err(gv.cpu().numpy(), ref["out"]) <= TOL
+    assert oracle.max_rel_err(gv.cpu().numpy(), tc.cpu().numpy()) <= TOL

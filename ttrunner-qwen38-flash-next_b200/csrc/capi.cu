@@ -582,6 +582,7 @@ static int get_prefill_ws(void* workspace, size_t bytes, const qmoe_dims* d, int
 }
 
 int qmoe_prefill_max_tokens(void) { return prefill_max_tokens(); }
+int qmoe_prefill_small_group_max(int n) { return prefill_small_group_max(n); }
 
 size_t qmoe_prefill_workspace_bytes(const qmoe_dims* dims, int n_tokens) {
     if (check_dims(dims) != QMOE_OK || n_tokens < 1 || n_tokens > prefill_max_tokens()) return 0;

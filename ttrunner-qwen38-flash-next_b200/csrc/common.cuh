@@ -128,6 +128,7 @@ cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* h,
 
 // Prefill / large verify chunks (prefill.cu).
 int prefill_max_tokens();
+int prefill_small_group_max(int n);
 bool prefill_supported(const qmoe_dims& d);
 struct PfLayout;
 size_t prefill_workspace_bytes(const qmoe_dims& d, int T);

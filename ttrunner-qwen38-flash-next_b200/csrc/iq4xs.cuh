@@ -286,6 +286,36 @@ __device__ __forceinline__ int qmoe_subblock_dot(uint32_t q0, uint32_t q1, uint3
     return acc + ((a0 + a1) + (a2 + a3));
 }
 
+// qmoe_subblock_dot in two halves, for one sub-block dotted with several
+// activation blocks: the codes' codebook bytes once (w[0..7]: lo, hi of each
+// qs word), then a dp2a pass per activation block.  Same exact int32 sum.
+__device__ __forceinline__ void qmoe_subblock_decode(uint32_t q0, uint32_t q1, uint32_t q2, uint32_t q3,
+                                                     uint32_t (&w)[8]) {
+    qmoe_lut8(q0, w[0], w[1]);
+    qmoe_lut8(q1, w[2], w[3]);
+    qmoe_lut8(q2, w[4], w[5]);
+    qmoe_lut8(q3, w[6], w[7]);
+}
+__device__ __forceinline__ int qmoe_subblock_dot_decoded(const uint32_t (&w)[8], const int* xp) {
+    int a0 = __dp2a_lo(xp[0], (int)w[0], 0);
+    int a1 = __dp2a_lo(xp[4], (int)w[2], 0);
+    int a2 = __dp2a_lo(xp[8], (int)w[4], 0);
+    int a3 = __dp2a_lo(xp[12], (int)w[6], 0);
+    a0 = __dp2a_hi(xp[1], (int)w[0], a0);
+    a1 = __dp2a_hi(xp[5], (int)w[2], a1);
+    a2 = __dp2a_hi(xp[9], (int)w[4], a2);
+    a3 = __dp2a_hi(xp[13], (int)w[6], a3);
+    a0 = __dp2a_lo(xp[2], (int)w[1], a0);
+    a1 = __dp2a_lo(xp[6], (int)w[3], a1);
+    a2 = __dp2a_lo(xp[10], (int)w[5], a2);
+    a3 = __dp2a_lo(xp[14], (int)w[7], a3);
+    a0 = __dp2a_hi(xp[3], (int)w[1], a0);
+    a1 = __dp2a_hi(xp[7], (int)w[3], a1);
+    a2 = __dp2a_hi(xp[11], (int)w[5], a2);
+    a3 = __dp2a_hi(xp[15], (int)w[7], a3);
+    return (a0 + a1) + (a2 + a3);
+}
+
 // Block floating point for an activation sub-block: the power-of-two step
 // 2^(e-14), e the binary exponent of the block's largest magnitude
 // (|x| < 2^e), so every |x / step| < 2^14 fits int16 with a bit to spare.

@@ -13,10 +13,13 @@
 //   1. x -> bf16 copy, when x is fp32 or not 16-byte aligned;
 //   2. router logits [T][E + 1] in fp32 (row E: the shared-expert gate vector);
 //   3. top-k per token (warp per token, the decode path's selection rule);
-//   4. grouping: per-expert counts, offsets, n-tiles of <= 128 tokens, and slot
-//      rows ordered by token (deterministic);
-//   5. gate|up grouped GEMM + SwiGLU epilogue -> h [rows][I] bf16;
-//   6. out = 0, then the down grouped GEMM with a gate-weighted scatter-add.
+//   4. grouping: per-expert counts, offsets, n-tiles of <= 64 tokens, and slot
+//      rows ordered by token (deterministic); groups of at most 8 tokens are
+//      listed apart for the grouped GEMV (no bf16 expansion);
+//   5. gate|up grouped GEMM + SwiGLU epilogue -> h [rows][I] bf16, and the
+//      small groups' gate|up GEMV -> h;
+//   6. out = 0, then the down grouped GEMM and the small groups' down GEMV,
+//      both with a gate-weighted scatter-add.
 // The shared expert is group E: every token, weight sigmoid(x . gate_vec).
 #include <math.h>
 
@@ -642,56 +645,69 @@ __global__ void pf_count_kernel(const int32_t* __restrict__ ids, int n, int E, i
 // One CTA: counts[E] = shared-group size, exclusive scans of counts (slot rows)
 // and of the n-tile counts, and the n-tile table.
 constexpr int kScanThreads = 1024;
-__global__ void __launch_bounds__(kScanThreads) pf_scan_kernel(int* counts, int G, int shared_count, int* offsets,
-                                                               int4* ntiles, int* meta) {
-    __shared__ int s_rows[kScanThreads / 32], s_nt[kScanThreads / 32];
+// Groups of at most gv_max tokens are listed in gv instead (the grouped GEMV
+// path); the others are cut into n-tiles of <= kGNMax tokens for the
+// tensor-core path.  meta: [0] n-tiles, [1] slot rows, [2] small groups.
+__global__ void __launch_bounds__(kScanThreads) pf_scan_kernel(int* counts, int G, int shared_count, int gv_max,
+                                                               int* offsets, int4* ntiles, int4* gv, int* meta) {
+    __shared__ int s_rows[kScanThreads / 32], s_nt[kScanThreads / 32], s_ns[kScanThreads / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // G <= 1025 groups: thread tid owns groups 2*tid and 2*tid + 1.
-    int c[2], nt[2];
+    int c[2], nt[2], sg[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
         const int g = 2 * tid + j;
         c[j] = 0;
         if (g < G) c[j] = g == G - 1 ? shared_count : counts[g];
-        nt[j] = (c[j] + kGNMax - 1) / kGNMax;
+        sg[j] = c[j] > 0 && c[j] <= gv_max ? 1 : 0;
+        nt[j] = sg[j] ? 0 : (c[j] + kGNMax - 1) / kGNMax;
     }
     if (2 * tid + 1 == G - 1 || 2 * tid == G - 1) counts[G - 1] = shared_count;
-    int r = c[0] + c[1], n = nt[0] + nt[1];
-    int ri = r, ni = n;
+    int r = c[0] + c[1], n = nt[0] + nt[1], ns = sg[0] + sg[1];
+    int ri = r, ni = n, nsi = ns;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const int yr = __shfl_up_sync(0xffffffffu, ri, o), yn = __shfl_up_sync(0xffffffffu, ni, o);
+        const int yr = __shfl_up_sync(0xffffffffu, ri, o), yn = __shfl_up_sync(0xffffffffu, ni, o),
+                  ys = __shfl_up_sync(0xffffffffu, nsi, o);
         if (lane >= o) {
             ri += yr;
             ni += yn;
+            nsi += ys;
         }
     }
     if (lane == 31) {
         s_rows[warp] = ri;
         s_nt[warp] = ni;
+        s_ns[warp] = nsi;
     }
     __syncthreads();
     if (warp == 0) {
-        int vr = s_rows[lane], vn = s_nt[lane];
+        int vr = s_rows[lane], vn = s_nt[lane], vs = s_ns[lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int yr = __shfl_up_sync(0xffffffffu, vr, o), yn = __shfl_up_sync(0xffffffffu, vn, o);
+            const int yr = __shfl_up_sync(0xffffffffu, vr, o), yn = __shfl_up_sync(0xffffffffu, vn, o),
+                      ys = __shfl_up_sync(0xffffffffu, vs, o);
             if (lane >= o) {
                 vr += yr;
                 vn += yn;
+                vs += ys;
             }
         }
         s_rows[lane] = vr;
         s_nt[lane] = vn;
+        s_ns[lane] = vs;
     }
     __syncthreads();
-    const int wr = warp > 0 ? s_rows[warp - 1] : 0, wn = warp > 0 ? s_nt[warp - 1] : 0;
-    int row = wr + ri - r, nti = wn + ni - n;  // exclusive prefixes of this thread's first group
+    const int wr = warp > 0 ? s_rows[warp - 1] : 0, wn = warp > 0 ? s_nt[warp - 1] : 0,
+              ws = warp > 0 ? s_ns[warp - 1] : 0;
+    // exclusive prefixes of this thread's first group
+    int row = wr + ri - r, nti = wn + ni - n, nsg = ws + nsi - ns;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
         const int g = 2 * tid + j;
         if (g < G) {
             offsets[g] = row;
+            if (sg[j]) gv[nsg] = make_int4(g, row, c[j], 0);
             for (int q = 0; q < nt[j]; ++q) {
                 const int n0 = q * kGNMax;
                 ntiles[nti + q] = make_int4(g, n0, min(kGNMax, c[j] - n0), row + n0);
@@ -699,11 +715,230 @@ __global__ void __launch_bounds__(kScanThreads) pf_scan_kernel(int* counts, int 
         }
         row += c[j];
         nti += nt[j];
+        nsg += sg[j];
     }
     if (tid == kScanThreads - 1) {
-        meta[0] = nti;  // total n-tiles
+        meta[0] = nti;  // tensor-core n-tiles
         meta[1] = row;  // total slot rows
+        meta[2] = nsg;  // small groups
         offsets[G] = row;
+    }
+}
+
+// ---- small groups: grouped GEMV ---------------------------------------------
+// A group of at most kGvMax tokens (most experts of a short chunk: ~2.7
+// tokens each at T = 128) is not worth expanding to bf16 for the tensor
+// cores: a warp decodes each weight row once with the decode path's integer
+// core (4-bit codes through the codebook, dp2a against the activations in
+// block floating point) and dots it with every token of the group.  Items are
+// (group, block of rows); the CTAs walk them persistently.
+constexpr int kGvMax = 8;     // largest group the GEMV path takes (the default threshold)
+constexpr int kGvWarps = 8;
+constexpr int kGvPairs = 64;  // gate|up row pairs per item
+constexpr int kGvRows = 256;  // down rows per item
+
+struct GvArgs {
+    int D, I, E;
+    const uint8_t* gate_up;
+    const uint8_t* down;
+    const uint8_t* sh_gate_up;
+    const uint8_t* sh_down;
+    size_t gu_expert_bytes, dn_expert_bytes;
+    const int4* gv;     // small groups {group, first slot row, tokens, 0}
+    const int* meta;    // meta[2]: number of small groups
+    const int* slot_tok;
+    const float* slot_w;
+    const int* xq;      // [T][4 quads][D/32 blocks][4 words]: x in block floating point
+    const float* xs;    // [T][D/32] steps
+    __nv_bfloat16* h;   // [rows][I]
+    float* out;         // [T][D]
+};
+
+// x -> block floating point in the [quad][block][4 words] order: lanes on
+// consecutive blocks read consecutive 16-byte chunks of shared memory.
+__global__ void __launch_bounds__(256) pf_xq_kernel(const __nv_bfloat16* __restrict__ xb, int T, int D,
+                                                    const int* __restrict__ meta, int* __restrict__ xq,
+                                                    float* __restrict__ xs) {
+    if (__ldg(meta + 2) == 0) return;  // no small groups in this chunk
+    const int lane = threadIdx.x & 31, nb = D >> 5;
+    const size_t n = (size_t)T * nb;
+    for (size_t w = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < n;
+         w += ((size_t)gridDim.x * blockDim.x) >> 5) {
+        const int t = (int)(w / nb), b = (int)(w % nb);
+        const float v = __bfloat162float(xb[(size_t)t * D + b * 32 + lane]);
+        float st;
+        const int pw = warp_block_fp(v, &st);
+        if (lane < 16) xq[(((size_t)t * 4 + (lane >> 2)) * nb + b) * 4 + (lane & 3)] = pw;
+        if (lane == 0) xs[(size_t)t * nb + b] = st;
+    }
+}
+
+// gate|up + SwiGLU of the small groups -> h (bf16, the tensor-core path's rows).
+// SBL: 32-value blocks of a row per lane (blocks lane, lane + 32, ...).
+template <int SBL>
+__global__ void __launch_bounds__(kGvWarps * 32) pf_gv_gateup_kernel(const __grid_constant__ GvArgs a) {
+    extern __shared__ __align__(16) unsigned char gsm[];
+    __shared__ int s_tok[kGvMax];
+    const int D = a.D, nb = D >> 5, words = nb * 16;
+    int* sxq = reinterpret_cast<int*>(gsm);                         // [kGvMax][4][nb][4]
+    float* sxs = reinterpret_cast<float*>(sxq + (size_t)kGvMax * words);  // [kGvMax][nb]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ipg = a.I / kGvPairs;
+    const int n_items = __ldg(a.meta + 2) * ipg;
+    const int row_bytes = (D >> 8) * QMOE_SB_BYTES;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        const int4 grp = __ldg(a.gv + it / ipg);
+        const int g = grp.x, row0 = grp.y, cnt = min(grp.z, kGvMax), r0 = (it % ipg) * kGvPairs;
+        __syncthreads();  // the previous item's activations are no longer read
+        if (tid < cnt) s_tok[tid] = __ldg(a.slot_tok + row0 + tid);
+        __syncthreads();
+        for (int m = 0; m < cnt; ++m) {
+            const int4* src = reinterpret_cast<const int4*>(a.xq + (size_t)s_tok[m] * words);
+            int4* dst = reinterpret_cast<int4*>(sxq + (size_t)m * words);
+            for (int i = tid; i < words / 4; i += blockDim.x) dst[i] = __ldg(src + i);
+            for (int i = tid; i < nb; i += blockDim.x) sxs[m * nb + i] = __ldg(a.xs + (size_t)s_tok[m] * nb + i);
+        }
+        __syncthreads();
+        const uint8_t* base = g < a.E ? a.gate_up + (size_t)g * a.gu_expert_bytes : a.sh_gate_up;
+        for (int pi = warp; pi < kGvPairs; pi += kGvWarps) {
+            const int r = r0 + pi;
+            const uint8_t* grow = base + (size_t)r * row_bytes;
+            const uint8_t* urow = base + (size_t)(a.I + r) * row_bytes;
+            uint2 hg[SBL], hu[SBL], qg[SBL][2], qu[SBL][2];
+#pragma unroll
+            for (int i = 0; i < SBL; ++i) {
+                const int b = lane + 32 * i;
+                if (b < nb) {
+                    const int off = (b >> 3) * QMOE_SB_BYTES, q = off + 8 + 16 * (b & 7);
+                    hg[i] = __ldg(reinterpret_cast<const uint2*>(grow + off));
+                    hu[i] = __ldg(reinterpret_cast<const uint2*>(urow + off));
+                    qg[i][0] = __ldg(reinterpret_cast<const uint2*>(grow + q));
+                    qg[i][1] = __ldg(reinterpret_cast<const uint2*>(grow + q + 8));
+                    qu[i][0] = __ldg(reinterpret_cast<const uint2*>(urow + q));
+                    qu[i][1] = __ldg(reinterpret_cast<const uint2*>(urow + q + 8));
+                }
+            }
+            float accg[kGvMax], accu[kGvMax];
+#pragma unroll
+            for (int m = 0; m < kGvMax; ++m) accg[m] = accu[m] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < SBL; ++i) {
+                const int b = lane + 32 * i;
+                if (b >= nb) continue;
+                const int ib = b & 7;
+                const float dg = __half2float(__ushort_as_half((unsigned short)(hg[i].x & 0xFFFFu))) *
+                                 (float)(qmoe_iq4xs_ls(hg[i].x, hg[i].y, ib) - 32);
+                const float du = __half2float(__ushort_as_half((unsigned short)(hu[i].x & 0xFFFFu))) *
+                                 (float)(qmoe_iq4xs_ls(hu[i].x, hu[i].y, ib) - 32);
+                uint32_t wg[8], wu[8];  // the codes' codebook bytes, decoded once for every token
+                qmoe_subblock_decode(qg[i][0].x, qg[i][0].y, qg[i][1].x, qg[i][1].y, wg);
+                qmoe_subblock_decode(qu[i][0].x, qu[i][0].y, qu[i][1].x, qu[i][1].y, wu);
+#pragma unroll
+                for (int m = 0; m < kGvMax; ++m) {
+                    if (m < cnt) {
+                        int xp[16];
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            const int4 w4 = *reinterpret_cast<const int4*>(sxq + (((size_t)m * 4 + v) * nb + b) * 4);
+                            xp[4 * v] = w4.x;
+                            xp[4 * v + 1] = w4.y;
+                            xp[4 * v + 2] = w4.z;
+                            xp[4 * v + 3] = w4.w;
+                        }
+                        const float st = sxs[m * nb + b];
+                        const int sgv = qmoe_subblock_dot_decoded(wg, xp);
+                        const int suv = qmoe_subblock_dot_decoded(wu, xp);
+                        accg[m] = fmaf(dg * st, (float)sgv, accg[m]);
+                        accu[m] = fmaf(du * st, (float)suv, accu[m]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < kGvMax; ++m) {
+                if (m < cnt) {
+                    const float gs = warp_sum(accg[m]), us = warp_sum(accu[m]);
+                    if (lane == 0) a.h[(size_t)(row0 + m) * a.I + r] = __float2bfloat16_rn(silu(gs) * us);
+                }
+            }
+        }
+    }
+}
+
+// down of the small groups, weighted and scatter-added into out: a half
+// warp per output row (two rows at a time), its lanes on the row's blocks.
+__global__ void __launch_bounds__(kGvWarps * 32) pf_gv_down_kernel(const __grid_constant__ GvArgs a) {
+    extern __shared__ __align__(16) unsigned char dsm[];
+    __shared__ int s_tok[kGvMax];
+    __shared__ float s_w[kGvMax];
+    const int D = a.D, I = a.I, nbh = I >> 5;
+    int* shq = reinterpret_cast<int*>(dsm);                               // [kGvMax][4][nbh][4]
+    float* shs = reinterpret_cast<float*>(shq + (size_t)kGvMax * nbh * 16);  // [kGvMax][nbh]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, half = lane >> 4, hl = lane & 15;
+    const int ipg = D / kGvRows;
+    const int n_items = __ldg(a.meta + 2) * ipg;
+    const int drb = (I >> 8) * QMOE_SB_BYTES;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        const int4 grp = __ldg(a.gv + it / ipg);
+        const int g = grp.x, row0 = grp.y, cnt = min(grp.z, kGvMax), j0 = (it % ipg) * kGvRows;
+        __syncthreads();
+        if (tid < cnt) {
+            s_tok[tid] = __ldg(a.slot_tok + row0 + tid);
+            s_w[tid] = __ldg(a.slot_w + row0 + tid);
+        }
+        // the group's h rows -> block floating point, a warp per 32-value block
+        for (int blk = warp; blk < cnt * nbh; blk += kGvWarps) {
+            const int m = blk / nbh, b = blk - m * nbh;
+            const float v = __bfloat162float(a.h[(size_t)(row0 + m) * I + b * 32 + lane]);
+            float st;
+            const int pw = warp_block_fp(v, &st);
+            if (lane < 16) shq[(((size_t)m * 4 + (lane >> 2)) * nbh + b) * 4 + (lane & 3)] = pw;
+            if (lane == 0) shs[m * nbh + b] = st;
+        }
+        __syncthreads();
+        const uint8_t* base = g < a.E ? a.down + (size_t)g * a.dn_expert_bytes : a.sh_down;
+        for (int jj = 2 * warp + half; jj < kGvRows; jj += 2 * kGvWarps) {
+            const int j = j0 + jj;
+            const uint8_t* row = base + (size_t)j * drb;
+            float acc[kGvMax];
+#pragma unroll
+            for (int m = 0; m < kGvMax; ++m) acc[m] = 0.0f;
+            for (int t = hl; t < nbh; t += 16) {
+                const uint8_t* blk = row + (t >> 3) * QMOE_SB_BYTES;
+                const int ib = t & 7;
+                const uint2 hd = __ldg(reinterpret_cast<const uint2*>(blk));
+                const uint2 q0 = __ldg(reinterpret_cast<const uint2*>(blk + 8 + 16 * ib));
+                const uint2 q1 = __ldg(reinterpret_cast<const uint2*>(blk + 16 + 16 * ib));
+                const float dl = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu))) *
+                                 (float)(qmoe_iq4xs_ls(hd.x, hd.y, ib) - 32);
+                uint32_t wd[8];
+                qmoe_subblock_decode(q0.x, q0.y, q1.x, q1.y, wd);
+#pragma unroll
+                for (int m = 0; m < kGvMax; ++m) {
+                    if (m < cnt) {
+                        int xp[16];
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            const int4 w4 = *reinterpret_cast<const int4*>(shq + (((size_t)m * 4 + v) * nbh + t) * 4);
+                            xp[4 * v] = w4.x;
+                            xp[4 * v + 1] = w4.y;
+                            xp[4 * v + 2] = w4.z;
+                            xp[4 * v + 3] = w4.w;
+                        }
+                        const int S = qmoe_subblock_dot_decoded(wd, xp);
+                        acc[m] = fmaf(dl * shs[m * nbh + t], (float)S, acc[m]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < kGvMax; ++m) {
+                if (m < cnt) {
+                    float v = acc[m];
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (hl == 0) atomicAdd(a.out + (size_t)s_tok[m] * D + j, s_w[m] * v);
+                }
+            }
+        }
     }
 }
 
@@ -758,8 +993,8 @@ __global__ void __launch_bounds__(kPlaceWarps * 32) pf_place_kernel(const int32_
 // ---- workspace and launches ---------------------------------------------------
 
 struct PfLayout {
-    size_t status, meta, trace, xb, logits, part, ids, weights, slog, counts, offsets, ntiles, slot_tok, slot_w, h, xg,
-        total;
+    size_t status, meta, trace, xb, logits, part, ids, weights, slog, counts, offsets, ntiles, gv, slot_tok, slot_w, h,
+        xg, xq, xs, total;
     int max_ntiles, rows;
 };
 
@@ -796,6 +1031,8 @@ PfLayout pf_layout(const qmoe_dims& d, int T) {
     o = pf_align(o + (size_t)(G + 1) * 4);
     L.ntiles = o;
     o = pf_align(o + (size_t)L.max_ntiles * 16);
+    L.gv = o;  // small groups
+    o = pf_align(o + (size_t)G * 16);
     L.slot_tok = o;
     o = pf_align(o + (size_t)L.rows * 4);
     L.slot_w = o;
@@ -804,11 +1041,24 @@ PfLayout pf_layout(const qmoe_dims& d, int T) {
     o = pf_align(o + (size_t)L.rows * d.inter * 2);
     L.xg = o;
     o = pf_align(o + (size_t)L.rows * d.hidden * 2);
+    L.xq = o;  // x in block floating point, for the small groups
+    o = pf_align(o + (size_t)T * (d.hidden / 32) * 64);
+    L.xs = o;
+    o = pf_align(o + (size_t)T * (d.hidden / 32) * 4);
     L.total = o;
     return L;
 }
 
 int prefill_max_tokens() { return kPfMaxTokens; }
+
+// Largest expert group the grouped GEMV takes (0: every group goes to the
+// tensor-core path).
+static int g_small_group_max = kGvMax;
+int prefill_small_group_max(int n) {
+    const int prev = g_small_group_max;
+    if (n >= 0) g_small_group_max = n < kGvMax ? n : kGvMax;
+    return prev;
+}
 
 size_t prefill_workspace_bytes(const qmoe_dims& d, int T) { return pf_layout(d, T).total; }
 
@@ -886,7 +1136,9 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     if (err != cudaSuccess) return err;
     const int n = T * k;
     pf_count_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ids, n, E, counts, status);
-    pf_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, G, has_shared ? T : 0, offsets, ntiles, meta);
+    int4* gv = reinterpret_cast<int4*>(ws + L.gv);
+    pf_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, G, has_shared ? T : 0, g_small_group_max, offsets, ntiles, gv,
+                                              meta);
     const size_t place_smem = (size_t)n * sizeof(short);
     err = cudaFuncSetAttribute(pf_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem);
     if (err != cudaSuccess) return err;
@@ -932,8 +1184,56 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
                         kGStageRowB / 2, 64);
     if (err != cudaSuccess) return err;
     grouped_gemm_kernel<<<(unsigned)n_sm, kGThreads, kGSmemBytes, s>>>(a);
+
+    // the small groups (grouped GEMV), gate|up
+    GvArgs v{};
+    v.D = d.hidden;
+    v.I = d.inter;
+    v.E = E;
+    v.gate_up = a.gate_up;
+    v.down = a.down;
+    v.sh_gate_up = a.sh_gate_up;
+    v.sh_down = a.sh_down;
+    v.gu_expert_bytes = a.gu_expert_bytes;
+    v.dn_expert_bytes = a.dn_expert_bytes;
+    v.gv = gv;
+    v.meta = meta;
+    v.slot_tok = slot_tok;
+    v.slot_w = slot_w;
+    v.xq = reinterpret_cast<int*>(ws + L.xq);
+    v.xs = reinterpret_cast<float*>(ws + L.xs);
+    v.h = h;
+    v.out = out;
+    const int nb = d.hidden / 32;
+    {
+        const size_t n = (size_t)T * nb;
+        const size_t blocks = (n + 7) / 8;
+        pf_xq_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(xb, T, d.hidden, meta,
+                                                                              reinterpret_cast<int*>(ws + L.xq),
+                                                                              reinterpret_cast<float*>(ws + L.xs));
+        const size_t gsm = (size_t)kGvMax * nb * 16 * 4 + (size_t)kGvMax * nb * 4;
+        void (*gk)(GvArgs) = nb <= 32 ? pf_gv_gateup_kernel<1> : nb <= 64 ? pf_gv_gateup_kernel<2>
+                                                                           : pf_gv_gateup_kernel<4>;
+        err = cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+        if (err != cudaSuccess) return err;
+        int per_sm = 1;  // persistent: as many CTAs as stay resident
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gk, kGvWarps * 32, gsm);
+        if (err != cudaSuccess) return err;
+        gk<<<(unsigned)(n_sm * (per_sm > 0 ? per_sm : 1)), kGvWarps * 32, gsm, s>>>(v);
+    }
+
     err = cudaMemsetAsync(out, 0, (size_t)T * d.hidden * 4, s);
     if (err != cudaSuccess) return err;
+    {
+        const int nbh = d.inter / 32;
+        const size_t dsm = (size_t)kGvMax * nbh * 16 * 4 + (size_t)kGvMax * nbh * 4;
+        err = cudaFuncSetAttribute(pf_gv_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm);
+        if (err != cudaSuccess) return err;
+        int per_sm = 1;
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pf_gv_down_kernel, kGvWarps * 32, dsm);
+        if (err != cudaSuccess) return err;
+        pf_gv_down_kernel<<<(unsigned)(n_sm * (per_sm > 0 ? per_sm : 1)), kGvWarps * 32, dsm, s>>>(v);
+    }
     a.mode = 1;
     err = encode_2d(&a.bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, h, (unsigned long long)d.inter, (unsigned long long)L.rows,
                     (unsigned long long)d.inter * 2, kGSlotK, kGNMax, CU_TENSOR_MAP_SWIZZLE_128B);
