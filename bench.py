@@ -265,15 +265,19 @@ def main() -> None:
     e1.record()
     torch.cuda.synchronize(dev)
     ms_e2e = e0.elapsed_time(e1)
+    # The workspace status word after every timed step (0, or the first QMOE_ERR_* a kernel
+    # recorded, e.g. a bounded wait that ran out): a nonzero value makes the timings invalid.
+    device_status = stack.ws.read_status()
 
     # ---- per-kernel durations for the roofline (eager, events per stage) ----
     stage = stage_timings(pkg, layers, xs[0], M, dev, reps=2)
     prefill = prefill_timings(pkg, layers[0], cfg, dev) if world == 1 and not args.no_prefill else None
 
     if world > 1:
-        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+        t = torch.tensor([ms, ms_e2e, float(device_status != 0)], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_e2e = t.tolist()
+        ms, ms_e2e, any_bad = t.tolist()
+        device_status = device_status or int(any_bad)
         # Every CUDA graph holding NCCL work is released before the process group is destroyed
         # (a live one makes destroy_process_group wait forever).
         torch.cuda.synchronize(dev)
@@ -328,6 +332,7 @@ def main() -> None:
             "per_layer_path_stage_us": {k: round(v, 3) for k, v in stage.items()},
             "prefill_config4": prefill,
             "clocks": clocks,
+            "device_status": device_status,
         }
         if bytes_tok:
             gbs = bytes_tok / (us_tok * 1e-6) / 1e9
