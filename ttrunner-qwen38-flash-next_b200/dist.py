@@ -90,16 +90,25 @@ class ShardedMoEStack:
         with torch.cuda.device(self.device):
             check(lib.qmoe_xchg_alloc(world, self.cfg.hidden, ctypes.byref(buf), handle), "qmoe_xchg_alloc")
             self._own_buf = buf.value
-            handles = gather_handles(handle.raw, self.group)
-            xc = Xchg(rank=rank, n_ranks=world)
-            for q, h in enumerate(handles):
-                if q == rank:
-                    xc.buf[q] = self._own_buf
-                    continue
-                peer = ctypes.c_void_p()
-                check(lib.qmoe_xchg_open(h, ctypes.byref(peer)), f"qmoe_xchg_open rank {q}")
-                self._peer_bufs.append(peer.value)
-                xc.buf[q] = peer.value
+            try:
+                handles = gather_handles(handle.raw, self.group)
+                xc = Xchg(rank=rank, n_ranks=world)
+                for q, h in enumerate(handles):
+                    if q == rank:
+                        xc.buf[q] = self._own_buf
+                        continue
+                    peer = ctypes.c_void_p()
+                    check(lib.qmoe_xchg_open(h, ctypes.byref(peer)), f"qmoe_xchg_open rank {q}")
+                    self._peer_bufs.append(peer.value)
+                    xc.buf[q] = peer.value
+            except BaseException:
+                # no kernel has used the buffers yet: unmap and free this rank's share at once
+                for p in self._peer_bufs:
+                    lib.qmoe_xchg_close(p)
+                self._peer_bufs = []
+                lib.qmoe_xchg_free(self._own_buf)
+                self._own_buf = None
+                raise
         self._xchg = xc
         dist.barrier(group=self.group)
 
