@@ -144,13 +144,25 @@ class ExpertSource:
 
 def moe_forward(x: np.ndarray, src: ExpertSource, k: int, with_shared: bool = True,
                 expert_window: tuple[int, int] | None = None,
-                inter_window: tuple[int, int] | None = None) -> dict:
+                inter_window: tuple[int, int] | None = None, cache: dict | None = None) -> dict:
     """Qwen4ExpModel._moe (model.py:387-417) on flat fp32 x [M, D].
 
     expert_window / inter_window restrict the routed experts to a variant-A
     window or every expert (and the shared one) to a variant-B slice of the
     intermediate axis: the partial sum a rank produces before the all-reduce.
+    cache: dequantised experts kept across calls (keys: expert id, "shared"),
+    the role of WeightStore's row cache (reference/weights.py:48-53) when it
+    is warm; None decodes every expert on each use (cold).
     """
+
+    def dq(key, gu_b, dn_b):
+        if cache is None:
+            return dequant_iq4xs(gu_b), dequant_iq4xs(dn_b)
+        got = cache.get(key)
+        if got is None:
+            got = cache[key] = (dequant_iq4xs(gu_b), dequant_iq4xs(dn_b))
+        return got
+
     x = np.ascontiguousarray(x, dtype=np.float32)
     M = x.shape[0]
     I, Ish = src.inter, src.shared_inter
@@ -159,8 +171,7 @@ def moe_forward(x: np.ndarray, src: ExpertSource, k: int, with_shared: bool = Tr
 
     shared = np.zeros_like(x)
     if with_shared and src.sh_gate_up is not None:                                   # :392-397
-        gu = dequant_iq4xs(src.sh_gate_up)
-        dn = dequant_iq4xs(src.sh_down)
+        gu, dn = dq("shared", src.sh_gate_up, src.sh_down)
         h = _silu(x @ gu[slo:shi].T) * (x @ gu[Ish + slo:Ish + shi].T)
         s = h @ dn[:, slo:shi].T
         gate = _sigmoid(x @ src.gate_vec.reshape(-1, 1))
@@ -175,8 +186,7 @@ def moe_forward(x: np.ndarray, src: ExpertSource, k: int, with_shared: bool = Tr
             continue
         slot, tok = np.nonzero(ids == e)                                             # :409
         gu_b, dn_b = src.expert(e)
-        gu = dequant_iq4xs(gu_b)                                                      # :411-413
-        dn = dequant_iq4xs(dn_b)
+        gu, dn = dq(e, gu_b, dn_b)                                                    # :411-413
         xs = x[slot]
         h = _silu(xs @ gu[lo:hi].T) * (xs @ gu[I + lo:I + hi].T)                      # :414
         np.add.at(out, slot, (h @ dn[:, lo:hi].T) * weights[slot, tok, None])        # :415
