@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import golden_cfg, golden_x, host_layer_for, load_golden
+from conftest import golden_x, host_layer_for, load_golden
 
 pytestmark = pytest.mark.gpu
 

@@ -7,7 +7,7 @@ missing, importing this module raises; build it with `build.py`.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
+from ctypes import POINTER, c_float, c_int, c_int64, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libqmoe_b200.so"
