@@ -81,3 +81,18 @@ def test_max_rel_err_definition(oracle):
     ref = np.array([1.0, -4.0, 2.0])
     assert oracle.max_rel_err(ref + np.array([0, 0.04, 0]), ref) == pytest.approx(0.01)
     assert oracle.max_rel_err(np.zeros(3), np.zeros(3)) == 0.0
+
+
+def test_warm_cache_is_the_same_computation(pkg, oracle):
+    """moe_forward with the dequantised experts cached (the warm CPU baseline) equals the cold
+    call bit for bit, on a first and a repeated call."""
+    g = load_golden("moe_small_m4.npz")
+    hl = host_layer_for(pkg, g, all_experts=True)
+    src = oracle.ExpertSource.from_host_layer(hl)
+    x = golden_x(g).float().numpy()
+    cold = oracle.moe_forward(x, src, hl.cfg.top_k)["out"]
+    cache: dict = {}
+    first = oracle.moe_forward(x, src, hl.cfg.top_k, cache=cache)["out"]
+    again = oracle.moe_forward(x, src, hl.cfg.top_k, cache=cache)["out"]
+    assert "shared" in cache and len(cache) > 1
+    assert np.array_equal(cold, first) and np.array_equal(cold, again)
