@@ -141,3 +141,38 @@ def test_prefill_small_group_threshold(pkg):
     assert lib.qmoe_prefill_small_group_max(100) == 3
     assert lib.qmoe_prefill_small_group_max(-1) == 8
     lib.qmoe_prefill_small_group_max(prev)
+
+
+def test_prefill_workspace_grows_with_the_chunk(pkg):
+    """The prefill workspace covers the chunk's buffers (router split partials at small T, the
+    small-group list and block-floating-point x) and grows with T."""
+    import ctypes
+
+    lib = pkg._lib.lib
+    d = pkg.Shard().dims(pkg.C1)
+    sizes = [lib.qmoe_prefill_workspace_bytes(ctypes.byref(d), t) for t in (1, 5, 64, 128, 300, 2048, 8192)]
+    assert all(b > 0 for b in sizes)
+    assert sizes == sorted(sizes)
+    D, E, k = 2048, 512, 10
+    for t, b in zip((128, 2048), (sizes[3], sizes[5])):
+        rows = t * (k + 1)
+        floor = t * D * 2 + t * (E + 1) * 4 + rows * 512 * 2 + rows * D * 2 + t * (D // 32) * 68
+        assert b >= floor, (t, b, floor)
+    # at T = 128 the router splits K eight ways: eight more logit planes than at T = 2048's share
+    assert sizes[3] >= 128 * (E + 1) * 4 * 9
+
+
+def test_single_launch_covers_rank_slices(pkg):
+    """The stack's single launch runs the whole layer and every variant-B rank slice of the
+    config-2 shape (one rank's chain, no exchange), not variant A or sliced-off shared experts."""
+    import ctypes
+
+    lib = pkg._lib.lib
+    for world in (1, 2, 4, 8):
+        for rank in range(world):
+            shard = pkg.Shard("B", rank, world) if world > 1 else pkg.Shard()
+            d = shard.dims(pkg.C2)
+            assert lib.qmoe_stack_single_launch(ctypes.byref(d), 1, 48) == 1, (world, rank)
+            assert lib.qmoe_stack_single_launch(ctypes.byref(d), 2, 48) == 0
+    da = pkg.Shard("A", 1, 2).dims(pkg.C2)
+    assert lib.qmoe_stack_single_launch(ctypes.byref(da), 1, 48) == 0
