@@ -192,6 +192,7 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill timings")
+    ap.add_argument("--no-verify", action="store_true", help="skip the config-3 verify-chunk timings")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -287,6 +288,7 @@ def main() -> None:
     # ---- per-kernel durations for the roofline (eager, events per stage) ----
     stage = stage_timings(pkg, layers, xs[0], M, dev, reps=2)
     prefill = prefill_timings(pkg, layers[0], cfg, dev) if world == 1 and not args.no_prefill else None
+    verify = verify_timings(pkg, layers, cfg, dev) if world == 1 and M == 1 and not args.no_verify else None
 
     if world > 1:
         t = torch.tensor([ms, ms_e2e, float(device_status != 0)], dtype=torch.float64, device=dev)
@@ -346,6 +348,7 @@ def main() -> None:
             },
             "per_layer_path_stage_us": {k: round(v, 3) for k, v in stage.items()},
             "prefill_config4": prefill,
+            "verify_config3": verify,
             "clocks": clocks,
             "device_status": device_status,
         }
@@ -363,6 +366,47 @@ def main() -> None:
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
+
+
+def verify_timings(pkg, layers, cfg, dev, tokens=(4, 8), steps: int = 10, warmup: int = 3) -> list:
+    """BASELINE config 3: the config-2 stack with M = 4 and 8 tokens per step (speculative verify;
+    each token routes on its own, the per-layer kernels share the experts the tokens have in
+    common), one CUDA graph per step, inputs resident.  Bytes = expected distinct experts per layer
+    512 (1 - (1 - 10/512)^M) x expert bytes + shared, x 48.  A failure is reported, not raised."""
+    import torch
+
+    hbm = peaks()[0]
+    out = []
+    for M in tokens:
+        try:
+            stack = pkg.MoEStack(layers, max_tokens=M)
+            xs = [pkg.synth_x(cfg, M, seed=7000 + i).to(dev) for i in range(warmup + steps)]
+            g = stack.graph(M)
+            for i in range(warmup):
+                stack.x_in[:M].copy_(xs[i])
+                g.replay()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(steps):
+                stack.x_in[:M].copy_(xs[warmup + i])
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            status = stack.ws.read_status()
+            us = e0.elapsed_time(e1) * 1000.0 / steps
+            uniq = cfg.n_experts * (1.0 - (1.0 - cfg.top_k / cfg.n_experts) ** M)
+            expert_b = cfg.gate_up_row_bytes * 2 * cfg.inter + cfg.hidden * cfg.down_row_bytes
+            nbytes = cfg.n_layers * (uniq * expert_b + cfg.shared_bytes)
+            gbs = nbytes / (us * 1e-6) / 1e9
+            out.append({"tokens": M, "us_per_step": round(us, 2), "us_per_token": round(us / M, 2),
+                        "launches_per_step": 3 * cfg.n_layers, "expected_experts_per_layer": round(uniq, 1),
+                        "bytes_per_step": round(nbytes), "achieved_gbs": round(gbs, 1),
+                        "frac_of_measured_hbm": round(gbs / hbm, 4), "device_status": status})
+            del g, stack
+        except Exception as exc:  # noqa: BLE001 -- a sub-measurement reports its failure in the line
+            out.append({"tokens": M, "error": f"{type(exc).__name__}: {exc}"[:300]})
+    return out
 
 
 def prefill_timings(pkg, layer, cfg, dev, chunks=(128, 2048), steps: int = 10, warmup: int = 3) -> list:
