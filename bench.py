@@ -111,53 +111,49 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline (the oracle port; test infrastructure used only as the timed
-# CPU arm)
+# CPU baseline and the reference arm: the oracle port of the reference's CPU MoE
+# (test infrastructure, used here only as the timed CPU arm).  Neither loads
+# the product library: the weights are the same device-family bytes, rebuilt
+# on the host by the oracle's own restatement of the generator.
 
-def cpu_baseline(cfg, n_layers_sample: int, budget_s: float, seed: int = 0) -> dict:
-    import numpy as np
+C2_SHAPES = dict(hidden=2048, inter=512, n_experts=512, top_k=10, shared_inter=512, weight_std=0.02)
 
-    from oracle import moe_ref
 
-    pkg = load_pkg()
-    threads = moe_ref.threads()
-    hls = [pkg.synth_host_layer(cfg, layer=l, seed=seed) for l in range(n_layers_sample)]
-    srcs = [moe_ref.ExpertSource.from_host_layer(h) for h in hls]
-    x0 = pkg.synth_x(cfg, 1, seed=seed).float().numpy()
-    # untimed pass: generates the experts this input selects (weight setup)
-    x = x0
-    for s in srcs:
-        x = moe_ref.moe_forward(x, s, cfg.top_k)["out"]
-    per_layer = []
+def reference_stack(n_layers: int, seed: int = 0):
+    from oracle import synth_family
+
+    shapes = synth_family.Shapes(**C2_SHAPES)
+    return shapes, [synth_family.FamilyLayer(shapes, l, seed) for l in range(n_layers)]
+
+
+def reference_xs(shapes, first: int, n: int, tokens: int = 1):
+    from oracle import synth_family
+
+    return [synth_family.synth_x(shapes.hidden, tokens, 1000 + i) for i in range(first, first + n)]
+
+
+def cpu_baseline(n_layers: int, budget_s: float, warm_steps: int = 2) -> dict:
+    """The CPU reference on a bounded sample of the bench's own workload: `warm_steps` untimed
+    decode steps of the 48-layer stack (fresh x each, as the GPU arm), then timed steps until
+    `budget_s` of CPU work (at least 3); median seconds per step."""
+    from oracle import moe_ref, synth_family
+
+    shapes, layers = reference_stack(n_layers)
+    cache = synth_family.RowCache()
+    synth_family.run_steps(layers, reference_xs(shapes, 0, warm_steps), shapes.top_k, cache)
+    times: list[float] = []
+    i = warm_steps
     t_end = time.perf_counter() + budget_s
-    calls = 0
-    while time.perf_counter() < t_end or calls < 2:
-        x = x0
-        for s in srcs:
-            t0 = time.perf_counter()
-            x = moe_ref.moe_forward(x, s, cfg.top_k)["out"]   # cold: dequantises its 11 experts
-            per_layer.append(time.perf_counter() - t0)
-        calls += 1
-    us_layer = statistics.median(per_layer) * 1e6
-    # warm: the selected experts already dequantised (the reference's row cache holding them)
-    caches = [dict() for _ in srcs]
-    x = x0
-    for s, c in zip(srcs, caches):
-        x = moe_ref.moe_forward(x, s, cfg.top_k, cache=c)["out"]
-    warm = []
-    for _ in range(max(5, calls)):
-        x = x0
-        for s, c in zip(srcs, caches):
-            t0 = time.perf_counter()
-            x = moe_ref.moe_forward(x, s, cfg.top_k, cache=c)["out"]
-            warm.append(time.perf_counter() - t0)
+    while len(times) < 3 or time.perf_counter() < t_end:
+        times += synth_family.run_steps(layers, reference_xs(shapes, i, 1), shapes.top_k, cache)
+        i += 1
     return {
-        "value": us_layer * cfg.n_layers, "unit": "us/token", "cores": threads, "kind": "port",
-        "sample": f"{len(per_layer)} layer calls ({n_layers_sample} seeded layers x {calls}), batch 1, "
-                  f"cold IQ4_XS dequant of the selected experts each call, median per layer x {cfg.n_layers}",
-        "warm_value": round(statistics.median(warm) * 1e6 * cfg.n_layers, 1),
-        "warm_sample": f"{len(warm)} layer calls with the selected experts already dequantised, "
-                       f"median per layer x {cfg.n_layers}",
+        "value": round(statistics.median(times) * 1e6, 1), "unit": "us/token", "cores": moe_ref.threads(),
+        "kind": "port",
+        "sample": f"{len(times)} timed decode steps of the {n_layers}-layer stack (fresh x per step, after "
+                  f"{warm_steps} untimed), the oracle port of reference/model.py:387-417 with the reference's "
+                  f"row cache (LRU, 24 GiB): experts missing from it are dequantised in the step; median",
+        "row_cache_hit_rate": round(cache.hits / max(1, cache.hits + cache.misses), 3),
     }
 
 
@@ -360,7 +356,7 @@ def main() -> None:
                 "bytes_with_router": bytes_tok + cfg.n_layers * (cfg.router_bytes + cfg.hidden * 4),
             }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(cfg, n_layers_sample=2, budget_s=args.cpu_budget)
+            line["cpu_baseline"] = cpu_baseline(cfg.n_layers, budget_s=args.cpu_budget)
         print(json.dumps(line), flush=True)
 
     if world > 1:
@@ -490,29 +486,46 @@ def stage_timings(pkg, layers, x, M: int, dev, reps: int = 2) -> dict:
 
 
 def run_reference_arm(args, rank: int, world: int) -> None:
+    """The reference's CPU implementation of the path (the oracle port), timed on this host's cores
+    with every thread, on the GPU arm's config: the same 48 device-family layers (rebuilt on the host,
+    no product library loaded), the same fresh x per step, one token per step; W untimed steps, then
+    K timed ones, each a whole 48-layer decode step.  Rank 0 only."""
     if rank != 0:
         return
-    pkg = load_pkg()
-    cfg = pkg.MoEConfig(n_layers=args.layers)
-    from oracle import moe_ref
+    from oracle import moe_ref, synth_family
 
-    per_step = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(cfg, n_layers_sample=1, budget_s=0.0, seed=i % 2)
-        if i >= args.warmup:
-            per_step.append(r["value"])
-    v = statistics.median(per_step)
+    t_setup = time.perf_counter()
+    shapes, layers = reference_stack(args.layers)
+    cache = synth_family.RowCache()
+    setup_s = time.perf_counter() - t_setup
+    M = args.tokens
+    synth_family.run_steps(layers, reference_xs(shapes, 0, args.warmup, M), shapes.top_k, cache)
+    times = synth_family.run_steps(layers, reference_xs(shapes, args.warmup, args.steps, M), shapes.top_k, cache)
+    us_tok = statistics.median(times) * 1e6 / M
     line = {
-        "metric": METRIC, "value": round(v, 1), "unit": "us/token", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(v / 1000.0, 3), "higher_is_better": False,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "impl": "reference",
-        "dtype": "iq4xs weights, fp32 compute", "data": "synthetic (host-family seeded weights)",
-        "config": {"workload": f"BASELINE config 2 sampled: one layer per step, scaled to {cfg.n_layers} layers",
-                   "tokens_per_step": 1, "layers": cfg.n_layers},
-        "cpu_baseline": {"value": round(v, 1), "unit": "us/token", "cores": moe_ref.threads(), "kind": "port",
-                         "sample": "one seeded layer per step (cold IQ4_XS dequant of the 11 experts used), "
-                                   f"median over {args.steps} steps, x {cfg.n_layers} layers"},
-        "e2e": {"value": round(v, 1), "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "metric": METRIC, "value": round(us_tok, 1), "unit": "us/token", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(statistics.median(times) * 1e3, 3),
+        "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "impl": "reference", "dtype": "iq4xs weights dequantised to fp32, fp32 activations and compute",
+        "data": "synthetic: the GPU arm's device-family weights (seed 0) rebuilt on the host, x ~ N(0,1) "
+                "bf16, fresh x per step (the GPU arm's seeds)",
+        "config": {
+            "workload": f"BASELINE config {'2' if M == 1 else '3'}: {args.layers}-layer MoE stack, {M} token(s)/step, "
+                        f"hidden {shapes.hidden}, inter {shapes.inter}, {shapes.n_experts} experts, "
+                        f"top-{shapes.top_k} + shared",
+            "tokens_per_step": M, "layers": args.layers,
+        },
+        "cpu_baseline": {
+            "value": round(us_tok, 1), "unit": "us/token", "cores": moe_ref.threads(), "kind": "port",
+            "sample": f"{args.steps} whole decode steps (after {args.warmup} untimed), median; the oracle port "
+                      "of reference/model.py:387-417 with the reference's LRU row cache (24 GiB); generating "
+                      "expert bytes not yet held is excluded (the reference reads them from its checkpoint)",
+        },
+        "e2e": {"value": round(us_tok, 1), "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "step_seconds": {"median": round(statistics.median(times), 4), "min": round(min(times), 4),
+                         "max": round(max(times), 4), "mean": round(statistics.mean(times), 4)},
+        "row_cache_hit_rate": round(cache.hits / max(1, cache.hits + cache.misses), 3),
+        "setup_seconds": round(setup_s + sum(l.gen_seconds for l in layers), 1),
     }
     print(json.dumps(line), flush=True)
 

@@ -113,6 +113,13 @@ int qmoe_synth_iq4xs(uint64_t seed, uint64_t stream_id, int64_t n_values, float 
                      void* out_blocks, void* stream);
 int qmoe_synth_f32(uint64_t seed, uint64_t stream_id, int64_t n_values, float std_dev,
                    float* out, void* stream);
+/* The same two generators on the host (OpenMP, n_threads >= 1), bit-identical
+ * to the device ones: every arithmetic step is a correctly rounded binary32
+ * operation.  out: host memory. */
+int qmoe_synth_iq4xs_host(uint64_t seed, uint64_t stream_id, int64_t n_values, float std_dev,
+                          void* out_blocks, int n_threads);
+int qmoe_synth_f32_host(uint64_t seed, uint64_t stream_id, int64_t n_values, float std_dev,
+                        float* out, int n_threads);
 
 /* ---- the MoE block, by stage --------------------------------------------- */
 /* Router + top-k + renormalise.  Replaces reference/model.py:399-403 and the
@@ -173,6 +180,29 @@ int qmoe_stack_single_launch(const qmoe_dims* dims, int n_tokens, int n_layers);
 int qmoe_read_stack_trace(void* workspace, const qmoe_dims* dims, int n_tokens, int n_layers,
                           uint64_t* host_out, void* stream);
 
+/* The single launch's per-layer record of its last call with this workspace
+ * (n_tokens = 1): act_out [n_layers, hidden] bf16 bits, each layer's output
+ * rounded to bf16 (the next layer's input); ids_out [n_layers, top_k] the
+ * selected experts in rank order; weights_out [n_layers, top_k] their
+ * renormalised routing weights.  Any of the three may be NULL.  Host buffers;
+ * synchronises `stream`.  The analogue of the reference's per-layer probe
+ * (reference/model.py:37-40, `probe(layer, hidden)`). */
+int qmoe_read_stack_route_trace(void* workspace, const qmoe_dims* dims, int n_tokens, int n_layers,
+                                uint16_t* act_out, int32_t* ids_out, float* weights_out, void* stream);
+
+/* The single-launch stack with every layer's input supplied: layer L reads
+ * x_layers[L] (device bf16 [n_layers, hidden]) instead of layer L-1's output,
+ * everything else exactly as qmoe_stack_decode with one token (the same
+ * kernel, the same phases and inter-layer handoff of the router logits).
+ * Layer-by-layer checks of the whole launch use it with a well-conditioned
+ * input per layer (the reference's decode_vs_reference harness feeds each
+ * layer the reference's own hidden state, scripts/dev/decode_vs_reference.py).
+ * out: the last layer's fp32 output; the per-layer outputs are in the route
+ * trace.  QMOE_ERR_UNSUPPORTED where the single launch does not apply. */
+int qmoe_stack_decode_teacher(const void* x_layers, const qmoe_layer_weights* layers, int n_layers,
+                              const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* The shared expert alone: sigmoid(x . gate_vec) * down(silu(gate x) * up x).
  * Replaces tt/moe.py:983-1044 (shared_expert) and reference/model.py:392-397.
  * Uses gate_vec, sh_gate_up and sh_down of `w`; routed fields are ignored. */
@@ -209,8 +239,8 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
  * passes all of them in a qmoe_xchg.  The buffers carry a launch counter:
  * every rank must make the same sequence of qmoe_stack_decode_xchg calls with
  * the same n_layers, and after a call that reports an error (a peer that
- * never arrived: QMOE_ERR_TIMEOUT after a bounded wait) the buffers must be
- * freed and allocated anew on every rank.  Unmap peers (qmoe_xchg_close) and
+ * never arrived: QMOE_ERR_TIMEOUT after a bounded wait) every rank resets
+ * its buffer with qmoe_xchg_reset (or frees and allocates them anew).  Unmap peers (qmoe_xchg_close) and
  * free (qmoe_xchg_free) only when no rank has a launch in flight. */
 typedef struct qmoe_xchg {
     int rank;
@@ -228,6 +258,13 @@ int qmoe_xchg_alloc(int n_ranks, int hidden, void** buf, void* ipc_handle);
 int qmoe_xchg_open(const void* ipc_handle, void** peer_buf);
 int qmoe_xchg_close(void* peer_buf);
 int qmoe_xchg_free(void* buf);
+/* Zeroes this rank's own exchange buffer (launch counter and receive words),
+ * stream-ordered.  After a call that failed on any rank (a host-side launch
+ * error, or QMOE_ERR_TIMEOUT from a peer that never arrived), the ranks'
+ * launch counters disagree; every rank then calls this on its own buffer,
+ * with no launch in flight anywhere and a barrier across the ranks before
+ * and after, and the exchange starts again from launch 0. */
+int qmoe_xchg_reset(void* buf, int n_ranks, int hidden, void* stream);
 /* 1 when qmoe_stack_decode_xchg runs these dims (this rank's slice) on
  * n_ranks ranks: the shapes of qmoe_stack_single_launch with
  * inter_local * n_ranks == inter. */
@@ -256,6 +293,13 @@ int qmoe_stack_decode_xchg(const void* x, int n_tokens, const qmoe_layer_weights
 #define QMOE_NOALLOC_SCRATCH_BYTES (1u << 20)
 int qmoe_moe_block_noalloc(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
                            const qmoe_dims* dims, float* out, void* stream);
+/* The device-side status of the no-allocation calls on the current device:
+ * the first error any of them recorded since the last read (QMOE_OK if none;
+ * QMOE_ERR_NOT_FINITE for a non-finite router logit), copied to *status_out,
+ * then cleared.  Synchronises `stream`; order it after the calls it reports
+ * on.  No counterpart in the reference (its fused kernels have no status
+ * word); it allocates nothing. */
+int qmoe_noalloc_read_status(int* status_out, void* stream);
 
 /* ---- Chunked prefill and large verify chunks: T tokens through one layer ----
  * Replaces TTModel._prefill_ffn_half (tt/model.py:2812-2907): moe.route
@@ -276,7 +320,9 @@ int qmoe_prefill_max_tokens(void);
  * decoded once with the decode path's integer core and dotted with every
  * token of the group; larger groups take the tcgen05 grouped GEMM.  n >= 0
  * sets it (0: every group on the tensor cores), n < 0 only queries; returns
- * the previous value.  Process-wide, read when a call is issued.  The
+ * the previous value.  One process-wide setting for every device and thread
+ * (an atomic: setting it while another thread issues a prefill is safe), read
+ * once when a call is issued.  The
  * reference has no counterpart (its prefill runs every group through the
  * same matmul, tt/moe.py:330-368). */
 int qmoe_prefill_small_group_max(int n);

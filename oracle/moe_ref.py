@@ -35,9 +35,9 @@ _SO = HERE / "liboracle_iq4xs.so"
 
 
 def build() -> Path:
-    """Compile the C restatement (make in this directory)."""
-    src = HERE / "iq4xs_ref.c"
-    if not _SO.exists() or _SO.stat().st_mtime < src.stat().st_mtime:
+    """Compile the C restatements (make in this directory)."""
+    srcs = [HERE / "iq4xs_ref.c", HERE / "synth_ref.c", HERE / "Makefile"]
+    if not _SO.exists() or any(_SO.stat().st_mtime < s.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return _SO
 
@@ -51,7 +51,37 @@ def _c() -> ctypes.CDLL:
         _lib = ctypes.CDLL(str(build()))
         _lib.oracle_dequant_iq4xs.restype = None
         _lib.oracle_dequant_iq4xs.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+        for name in ("oracle_synth_f32", "oracle_synth_iq4xs"):
+            fn = getattr(_lib, name)
+            fn.restype = None
+            fn.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p]
+        _lib.oracle_quantize_iq4xs.restype = None
+        _lib.oracle_quantize_iq4xs.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
     return _lib
+
+
+def synth_f32(seed: int, sid: int, n: int, std: float) -> np.ndarray:
+    """n values of the synthetic generator's stream (seed, sid), fp32 (synth_ref.c)."""
+    out = np.empty(n, dtype=np.float32)
+    _c().oracle_synth_f32(seed, sid, n, std, out.ctypes.data)
+    return out
+
+
+def synth_iq4xs(seed: int, sid: int, n_values: int, std: float) -> np.ndarray:
+    """The same stream quantised to IQ4_XS: n_values / 256 * 136 bytes (synth_ref.c)."""
+    if n_values % 256:
+        raise ValueError("n_values must be a multiple of 256")
+    out = np.empty(n_values // 256 * 136, dtype=np.uint8)
+    _c().oracle_synth_iq4xs(seed, sid, n_values, std, out.ctypes.data)
+    return out
+
+
+def quantize_iq4xs(values: np.ndarray) -> np.ndarray:
+    """fp32 [..., n] (n % 256 == 0) -> IQ4_XS bytes [..., n / 256 * 136] (synth_ref.c)."""
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    out = np.empty(v.shape[:-1] + (v.shape[-1] // 256 * 136,), dtype=np.uint8)
+    _c().oracle_quantize_iq4xs(v.ctypes.data, v.size, out.ctypes.data)
+    return out
 
 
 def dequant_iq4xs(raw: np.ndarray) -> np.ndarray:

@@ -1,9 +1,10 @@
 """Generate the golden fixtures of this directory from the reference itself.
 
-Run in a container that has the reference checkout (read-only) at
-REFERENCE_SRC (default /root/reference/src) and its `gguf` 0.19 dependency:
+Run where the reference checkout is available (read-only is enough), with
+the environment variable REFERENCE_SRC naming its `src` directory, and its
+`gguf` 0.19 dependency installed:
 
-    python tests/golden/make_golden.py
+    REFERENCE_SRC=<checkout>/src python tests/golden/make_golden.py
 
 What it records (all small, committed as .npz):
 
@@ -42,7 +43,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF = Path(os.environ.get("REFERENCE_SRC", "/root/reference/src"))
+if not os.environ.get("REFERENCE_SRC"):
+    sys.exit("set REFERENCE_SRC to the reference checkout's src directory")
+REF = Path(os.environ["REFERENCE_SRC"])
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(ROOT))
 

@@ -96,3 +96,62 @@ def test_warm_cache_is_the_same_computation(pkg, oracle):
     again = oracle.moe_forward(x, src, hl.cfg.top_k, cache=cache)["out"]
     assert "shared" in cache and len(cache) > 1
     assert np.array_equal(cold, first) and np.array_equal(cold, again)
+
+
+# ---- the synthetic-weight generator: the oracle's C restatement vs the product ----------------
+
+GEN_CASES = [(0, (3 << 40) | (4 << 32) | 17, 2 * 512 * 2048, 0.02), (7, 12345, 256 * 64, 1.0),
+             (2**40 + 5, 2**63 + 9, 256 * 8, 0.5), (0, (47 << 40) | (5 << 32) | 511, 2048 * 512, 0.02)]
+
+
+@pytest.mark.parametrize("seed,sid,n,std", GEN_CASES)
+def test_generator_restatement_is_byte_exact(pkg, oracle, seed, sid, n, std):
+    """The oracle's own generator (synth_ref.c) gives the product host generator's bytes, both the
+    fp32 stream and its IQ4_XS form; the oracle's quantiser matches the product's on that stream."""
+    L = pkg._lib
+    want_q = np.empty(n // 256 * 136, np.uint8)
+    want_f = np.empty(n, np.float32)
+    L.check(L.lib.qmoe_synth_iq4xs_host(seed, sid, n, std, want_q.ctypes.data, 4), "synth_iq4xs_host")
+    L.check(L.lib.qmoe_synth_f32_host(seed, sid, n, std, want_f.ctypes.data, 4), "synth_f32_host")
+    got_f = oracle.synth_f32(seed, sid, n, std)
+    got_q = oracle.synth_iq4xs(seed, sid, n, std)
+    assert np.array_equal(got_f.view(np.uint32), want_f.view(np.uint32))
+    assert np.array_equal(got_q, want_q)
+    assert np.array_equal(oracle.quantize_iq4xs(got_f.reshape(-1, 256)).reshape(-1), want_q)
+    assert np.array_equal(pkg.weights.quantize_host(got_f.reshape(-1, 256)).reshape(-1), want_q)
+
+
+def test_generator_is_standard_normal(oracle):
+    z = oracle.synth_f32(1, 1, 1 << 22, 1.0).astype(np.float64)
+    assert abs(z.mean()) < 3e-3 and abs(z.std() - 1.0) < 3e-3
+    assert abs((np.abs(z) > 2).mean() - 0.0455) < 2e-3
+    assert abs((np.abs(z) > 3).mean() - 0.0027) < 4e-4
+    # odd sizes: the tail of the last counter group is cut, the rest is the same stream
+    assert np.array_equal(oracle.synth_f32(1, 1, 7, 1.0), z[:7].astype(np.float32))
+
+
+def test_family_layer_matches_product_device_family_layout(pkg):
+    """oracle.synth_family numbers the streams as the product's generator does (layer << 40 |
+    tag << 32 | expert, with the product's tag values)."""
+    from oracle import synth_family
+
+    assert synth_family.sid(3, synth_family.TAG_DOWN, 9) == pkg.weights._sid(3, pkg.weights.TAG_DOWN, 9)
+    for name in ("TAG_ROUTER", "TAG_GATE_VEC", "TAG_SH_GATE_UP", "TAG_SH_DOWN", "TAG_GATE_UP", "TAG_DOWN",
+                 "TAG_X"):
+        assert getattr(synth_family, name) == getattr(pkg.weights, name)
+    x = synth_family.synth_x(512, 3, seed=5)
+    assert np.array_equal(x, pkg.synth_x(pkg.MoEConfig(hidden=512), 3, seed=5).float().numpy())
+
+
+def test_row_cache_is_lru_by_bytes():
+    from oracle import synth_family
+
+    c = synth_family.RowCache(limit_bytes=3 * 400)
+    v0, v1 = c.view(0), c.view(1)
+    row = (np.zeros(50, np.float64), np.zeros(50, np.float32))  # 600 bytes
+    v0[1] = row
+    v1[1] = row
+    assert v0.get(1) is row                  # hit: (0, 1) becomes the most recent
+    v1[2] = row                              # over the limit: evicts the least recent, (1, 1)
+    assert v1.get(1) is None and v0.get(1) is row and v1.get(2) is row
+    assert c.hits == 3 and c.misses == 1

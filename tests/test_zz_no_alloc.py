@@ -3,7 +3,8 @@ device memory (hosts bound through a plain C ABI without a device allocator,
 plug-ins whose process's device memory is owned by another framework's
 allocator, serving loops that forbid allocation after start-up).  Its scratch
 is a fixed 1 MiB device array inside the library instead of a caller
-workspace.
+workspace; qmoe_noalloc_read_status reads back the status word that array
+holds.
 
 This file is named to be collected last, so a run that stops at the first
 failure has run every other test before it.
@@ -48,6 +49,61 @@ def test_noalloc_matches_workspace_entry_point_twice(pkg, oracle):
         assert torch.isfinite(got).all()
         assert oracle.max_rel_err(got.cpu().numpy(), want.cpu().numpy()) <= TOL
         assert torch.equal(got, want)   # same kernels, same inputs: same bits
+
+
+def _noalloc_status(pkg) -> int:
+    L = pkg._lib
+    st = ctypes.c_int(-1)
+    L.check(L.lib.qmoe_noalloc_read_status(ctypes.byref(st), torch.cuda.current_stream().cuda_stream),
+            "qmoe_noalloc_read_status")
+    return st.value
+
+
+@pytest.mark.gpu
+def test_noalloc_at_the_config1_shape(pkg):
+    """BASELINE config 1's block (hidden 2048, 512 experts, top-10 + shared) with 16 tokens, the
+    most the decode entry points take, fits the fixed array; two calls in a row equal the
+    workspace entry point bit for bit."""
+    L = pkg._lib
+    cfg = pkg.C1
+    d = pkg.Shard().dims(cfg)
+    assert L.lib.qmoe_workspace_bytes(ctypes.byref(d), 16) <= (1 << 20)
+    layer = pkg.MoELayer(pkg.synth_device_layer(cfg, 0, seed=11))
+    _noalloc_status(pkg)  # start from a clear status word
+    for seed in (1, 2):
+        x = pkg.synth_x(cfg, 16, seed=seed).cuda()
+        want = layer(x)
+        got = _noalloc(pkg, layer, x)
+        torch.cuda.synchronize()
+        assert torch.isfinite(got).all()
+        assert oracle_free_rel_err(got, want) <= TOL
+        assert torch.equal(got, want)
+    assert _noalloc_status(pkg) == L.QMOE_OK
+
+
+@pytest.mark.gpu
+def test_noalloc_reports_a_non_finite_router_logit(pkg):
+    """The status the kernels record on the library's array is not lost: a non-finite input
+    makes the router flag QMOE_ERR_NOT_FINITE, which qmoe_noalloc_read_status returns once."""
+    L = pkg._lib
+    g = load_golden("moe_small_m1.npz")
+    hl = host_layer_for(pkg, g, all_experts=True)
+    layer = pkg.MoELayer(pkg.upload_host_layer(hl, device="cuda"))
+    _noalloc_status(pkg)
+    x = golden_x(g).cuda().clone()
+    x[0, 5] = float("inf")
+    _noalloc(pkg, layer, x)
+    torch.cuda.synchronize()
+    assert _noalloc_status(pkg) == L.QMOE_ERR_NOT_FINITE
+    assert _noalloc_status(pkg) == L.QMOE_OK  # the read cleared it
+    out = _noalloc(pkg, layer, golden_x(g).cuda())  # and the next call is clean
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all() and _noalloc_status(pkg) == L.QMOE_OK
+
+
+def oracle_free_rel_err(got: torch.Tensor, want: torch.Tensor) -> float:
+    denom = want.abs().max().item()
+    return (got.double() - want.double()).abs().max().item() / denom if denom else 0.0
 
 
 def test_noalloc_rejects_oversized_scratch(pkg):

@@ -101,6 +101,8 @@ _SIGS = {
     "qmoe_quantize_iq4xs": (c_int, [_P, c_int64, _P, _P]),
     "qmoe_synth_iq4xs": (c_int, [c_uint64, c_uint64, c_int64, c_float, _P, _P]),
     "qmoe_synth_f32": (c_int, [c_uint64, c_uint64, c_int64, c_float, _P, _P]),
+    "qmoe_synth_iq4xs_host": (c_int, [c_uint64, c_uint64, c_int64, c_float, _P, c_int]),
+    "qmoe_synth_f32_host": (c_int, [c_uint64, c_uint64, c_int64, c_float, _P, c_int]),
     "qmoe_route": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P, _P, _P,
                            c_size_t, _P]),
     "qmoe_gateup_swiglu": (c_int, [_P, c_int, c_int, _P, POINTER(LayerWeights), POINTER(Dims), _P,
@@ -115,15 +117,19 @@ _SIGS = {
                                   c_size_t, _P]),
     "qmoe_read_stack_trace": (c_int, [_P, POINTER(Dims), c_int, c_int, _P, _P]),
     "qmoe_stack_single_launch": (c_int, [POINTER(Dims), c_int, c_int]),
+    "qmoe_read_stack_route_trace": (c_int, [_P, POINTER(Dims), c_int, c_int, _P, _P, _P, _P]),
+    "qmoe_stack_decode_teacher": (c_int, [_P, POINTER(LayerWeights), c_int, POINTER(Dims), _P, _P, c_size_t, _P]),
     "qmoe_xchg_bytes": (c_size_t, [c_int, c_int]),
     "qmoe_xchg_alloc": (c_int, [c_int, c_int, POINTER(c_void_p), _P]),
     "qmoe_xchg_open": (c_int, [_P, POINTER(c_void_p)]),
     "qmoe_xchg_close": (c_int, [_P]),
     "qmoe_xchg_free": (c_int, [_P]),
+    "qmoe_xchg_reset": (c_int, [_P, c_int, c_int, _P]),
     "qmoe_stack_xchg_supported": (c_int, [POINTER(Dims), c_int, c_int, c_int]),
     "qmoe_stack_decode_xchg": (c_int, [_P, c_int, POINTER(LayerWeights), c_int, POINTER(Dims), POINTER(Xchg), _P,
                                        _P, c_size_t, _P]),
     "qmoe_moe_block_noalloc": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P]),
+    "qmoe_noalloc_read_status": (c_int, [POINTER(c_int), _P]),
     "qmoe_prefill_max_tokens": (c_int, []),
     "qmoe_prefill_small_group_max": (c_int, [c_int]),
     "qmoe_prefill_workspace_bytes": (c_size_t, [POINTER(Dims), c_int]),

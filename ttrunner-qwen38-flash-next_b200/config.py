@@ -35,6 +35,13 @@ class MoEConfig:
     shared_inter: int = 512
     n_layers: int = 1
     weight_std: float = 0.02
+    # std of the down projections (routed and shared); None: weight_std.  Tests use a larger one
+    # so that a literal stack keeps its activations near unit RMS through every layer.
+    down_std: float | None = None
+
+    @property
+    def dn_std(self) -> float:
+        return self.weight_std if self.down_std is None else self.down_std
 
     @property
     def gate_up_row_bytes(self) -> int:

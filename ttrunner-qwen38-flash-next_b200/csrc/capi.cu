@@ -130,6 +130,15 @@ struct Ws {
     float* act() const { return (float*)(base + L.act); }
     unsigned* sync() const { return (unsigned*)(base + L.sync); }
     unsigned long long* trace() const { return (unsigned long long*)(base + L.trace); }
+    StackTraceBufs trace_bufs(int top_k, const void* teacher = nullptr) const {
+        StackTraceBufs t{};
+        t.act = (__nv_bfloat16*)(base + L.act_trace);
+        t.ids = (int*)(base + L.route_trace);
+        t.weights = (float*)(base + L.route_trace) + 64 * kMaxTopK;
+        t.teacher = (const __nv_bfloat16*)teacher;
+        (void)top_k;
+        return t;
+    }
 };
 
 int get_ws(void* workspace, size_t bytes, const qmoe_dims* d, int M, Ws* ws) {
@@ -203,6 +212,10 @@ WsLayout ws_layout(const qmoe_dims& d, int max_tokens) {
     off = align_up(off + stack_sync_bytes(d.n_experts), 256);
     L.trace = off;
     off = align_up(off + 2 * 64 * kTraceSlots * 8, 256);
+    L.act_trace = off;
+    off = align_up(off + (size_t)64 * d.hidden * 2, 256);
+    L.route_trace = off;
+    off = align_up(off + (size_t)64 * kMaxTopK * 8, 256);
     L.total = off;
     return L;
 }
@@ -451,7 +464,7 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
     }
     if (aligned16 && stack_kernel_supported(*dims, n_tokens, n_layers, 1))
         return cuda_status(launch_stack_kernel(x, out, ws.act(), ws.h(), ws.sync(), ws.trace(), ws.status(), layers,
-                                               n_layers, *dims, nullptr, s));
+                                               n_layers, *dims, nullptr, ws.trace_bufs(dims->top_k), s));
     // Otherwise three launches per layer. Layer L+1 reads `out` (layer L's result) in its router and gate|up
     // launches; its down launch overwrites `out` only after both, in stream
     // order, so one buffer carries the activation through the stack.
@@ -461,6 +474,51 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
         QMOE_TRY(run_block(in, dt, n_tokens, &layers[l], dims, out, ws, s));
     }
     return QMOE_OK;
+}
+
+int qmoe_stack_decode_teacher(const void* x_layers, const qmoe_layer_weights* layers, int n_layers,
+                              const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_act(x_layers, QMOE_ACT_BF16));
+    if (!layers || n_layers < 1 || !out) return QMOE_ERR_INVALID_ARG;
+    if (!aligned(x_layers, 16) || !aligned(out, 16)) return QMOE_ERR_ALIGNMENT;
+    for (int l = 0; l < n_layers; ++l) {
+        const qmoe_layer_weights& w = layers[l];
+        QMOE_TRY(check_weights_route(&w));
+        QMOE_TRY(check_weights_experts(&w, dims));
+        if (!w.gate_vec || !w.sh_gate_up || !w.sh_down) return QMOE_ERR_UNSUPPORTED;
+        if (!aligned(w.gate_up, 16) || !aligned(w.down, 16) || !aligned(w.sh_gate_up, 16) || !aligned(w.sh_down, 16))
+            return QMOE_ERR_ALIGNMENT;
+    }
+    if (!stack_kernel_supported(*dims, 1, n_layers, 1)) return QMOE_ERR_UNSUPPORTED;
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, 1, &ws));
+    return cuda_status(launch_stack_kernel(x_layers, out, ws.act(), ws.h(), ws.sync(), ws.trace(), ws.status(),
+                                           layers, n_layers, *dims, nullptr, ws.trace_bufs(dims->top_k, x_layers),
+                                           (cudaStream_t)stream));
+}
+
+int qmoe_read_stack_route_trace(void* workspace, const qmoe_dims* dims, int n_tokens, int n_layers,
+                                uint16_t* act_out, int32_t* ids_out, float* weights_out, void* stream) {
+    QMOE_TRY(check_dims(dims));
+    if (!workspace || n_layers < 1 || n_layers > 64) return QMOE_ERR_INVALID_ARG;
+    QMOE_TRY(check_tokens(n_tokens));
+    Ws ws;
+    ws.L = ws_layout(*dims, n_tokens);
+    ws.base = (unsigned char*)workspace;
+    const StackTraceBufs t = ws.trace_bufs(dims->top_k);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (act_out)
+        QMOE_TRY(cuda_status(cudaMemcpyAsync(act_out, t.act, (size_t)n_layers * dims->hidden * 2,
+                                             cudaMemcpyDeviceToHost, s)));
+    if (ids_out)
+        QMOE_TRY(cuda_status(cudaMemcpyAsync(ids_out, t.ids, (size_t)n_layers * dims->top_k * 4,
+                                             cudaMemcpyDeviceToHost, s)));
+    if (weights_out)
+        QMOE_TRY(cuda_status(cudaMemcpyAsync(weights_out, t.weights, (size_t)n_layers * dims->top_k * 4,
+                                             cudaMemcpyDeviceToHost, s)));
+    return cuda_status(cudaStreamSynchronize(s));
 }
 
 // ---- the stack sharded over ranks, exchange inside the kernel ----------------
@@ -519,6 +577,13 @@ int qmoe_xchg_free(void* buf) {
     return cuda_status(cudaFree(buf));
 }
 
+int qmoe_xchg_reset(void* buf, int n_ranks, int hidden, void* stream) {
+    if (!buf) return QMOE_ERR_INVALID_ARG;
+    const size_t bytes = qmoe_xchg_bytes(n_ranks, hidden);
+    if (!bytes) return QMOE_ERR_UNSUPPORTED;
+    return cuda_status(cudaMemsetAsync(buf, 0, bytes, (cudaStream_t)stream));
+}
+
 int qmoe_stack_xchg_supported(const qmoe_dims* dims, int n_ranks, int n_tokens, int n_layers) {
     if (check_dims(dims) != QMOE_OK || n_ranks < 2 || n_ranks > kMaxXchgRanks) return 0;
     return stack_kernel_supported(*dims, n_tokens, n_layers, n_ranks) ? 1 : 0;
@@ -550,7 +615,7 @@ int qmoe_stack_decode_xchg(const void* x, int n_tokens, const qmoe_layer_weights
     Ws ws;
     QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
     return cuda_status(launch_stack_kernel(x, out, ws.act(), ws.h(), ws.sync(), ws.trace(), ws.status(), layers,
-                                           n_layers, *dims, &desc, (cudaStream_t)stream));
+                                           n_layers, *dims, &desc, ws.trace_bufs(dims->top_k), (cudaStream_t)stream));
 }
 
 // ---- prefill / large verify chunks ------------------------------------------

@@ -29,6 +29,8 @@ struct WsLayout {
     size_t sync;        // grid-barrier counters (8 x 128 B), the abort word, then the stack
                         // kernel's two router-logit accumulators (stack_sync_bytes)
     size_t trace;       // u64 [64 layers][8]: the stack kernel's phase timestamps
+    size_t act_trace;   // bf16 [64 layers][hidden]: the single launch's per-layer outputs
+    size_t route_trace; // int32 [64][16] ids, then fp32 [64][16] weights, per layer
     size_t total;
     int h_stride;
 };
@@ -118,13 +120,21 @@ cudaError_t launch_synth_f32(uint64_t seed, uint64_t sid, int64_t n, float std_d
 
 int device_sm_count();
 
+// Per-layer records of the single-launch stack and its teacher input (all may be null).
+struct StackTraceBufs {
+    __nv_bfloat16* act;              // [n_layers][hidden] each layer's output, bf16
+    int* ids;                        // [n_layers][top_k]
+    float* weights;                  // [n_layers][top_k]
+    const __nv_bfloat16* teacher;    // [n_layers][hidden] each layer's input, or null (the chain)
+};
+
 // The single-launch decode stack kernel (stack_kernel.cu).  R ranks exchange
 // their partial rows inside the kernel when R > 1.
 // xc: null for one rank.
 bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers, int R);
 cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* h, unsigned* sync,
                                 unsigned long long* trace, int* status, const qmoe_layer_weights* layers, int n_layers,
-                                const qmoe_dims& d, const XchgDesc* xc, cudaStream_t stream);
+                                const qmoe_dims& d, const XchgDesc* xc, const StackTraceBufs& tb, cudaStream_t stream);
 
 // Prefill / large verify chunks (prefill.cu).
 int prefill_max_tokens();

@@ -1,5 +1,6 @@
 // IQ4_XS decode, the device quantiser and the seeded weight generator.
 #include "common.cuh"
+#include "synth.cuh"
 
 namespace qmoe {
 namespace {
@@ -62,62 +63,24 @@ __global__ void quantize_kernel(const float* __restrict__ x, int64_t n_blocks,
     }
 }
 
-// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
-// easy as 1, 2, 3", SC 2011): counter = (group lo, group hi, stream lo,
-// stream hi), key = seed.
-__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
-#pragma unroll
-    for (int r = 0; r < 10; ++r) {
-        const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
-        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
-        c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
-        k.x += 0x9E3779B9u;
-        k.y += 0xBB67AE85u;
-    }
-    return c;
-}
-
-// Four N(0,1) values for counter group g (Box-Muller on two uniform pairs).
-__device__ __forceinline__ float4 normal4(uint64_t seed, uint64_t sid, uint64_t g) {
-    const uint4 r = philox4x32_10(make_uint4((uint32_t)g, (uint32_t)(g >> 32), (uint32_t)sid,
-                                             (uint32_t)(sid >> 32)),
-                                  make_uint2((uint32_t)seed, (uint32_t)(seed >> 32)));
-    const float u0 = (float)(r.x >> 8) * 5.9604644775390625e-8f + 2.98023223876953125e-8f;
-    const float u1 = (float)(r.y >> 8) * 5.9604644775390625e-8f;
-    const float u2 = (float)(r.z >> 8) * 5.9604644775390625e-8f + 2.98023223876953125e-8f;
-    const float u3 = (float)(r.w >> 8) * 5.9604644775390625e-8f;
-    const float a = sqrtf(-2.0f * logf(u0));
-    const float b = sqrtf(-2.0f * logf(u2));
-    float s0, c0, s1, c1;
-    sincospif(2.0f * u1, &s0, &c0);
-    sincospif(2.0f * u3, &s1, &c1);
-    return make_float4(a * c0, a * s0, b * c1, b * s1);
-}
-
+// One counter group (four values) per thread; the arithmetic is the shared
+// exact generator of synth.cuh, so the host entry points give the same bits.
 __global__ void synth_f32_kernel(uint64_t seed, uint64_t sid, int64_t n, float std_dev,
                                  float* __restrict__ out) {
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (4 * g >= n) return;
-    const float4 z = normal4(seed, sid, (uint64_t)g);
-    const float v[4] = {z.x * std_dev, z.y * std_dev, z.z * std_dev, z.w * std_dev};
+    float v[4];
+    qmoe_synth_values4(seed, sid, (uint64_t)g, std_dev, v);
     for (int i = 0; i < 4 && 4 * g + i < n; ++i) out[4 * g + i] = v[i];
 }
 
+// One super-block (64 counter groups, then the quantiser) per thread.
 __global__ void synth_iq4xs_kernel(uint64_t seed, uint64_t sid, int64_t n_blocks, float std_dev,
                                    uint8_t* __restrict__ out) {
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= n_blocks) return;
-    float v[256];
-#pragma unroll 4
-    for (int i = 0; i < 64; ++i) {
-        const float4 z = normal4(seed, sid, (uint64_t)(b * 64 + i));
-        v[4 * i] = z.x * std_dev;
-        v[4 * i + 1] = z.y * std_dev;
-        v[4 * i + 2] = z.z * std_dev;
-        v[4 * i + 3] = z.w * std_dev;
-    }
     uint8_t blk[QMOE_SB_BYTES];
-    qmoe_quantize_superblock(v, blk);
+    qmoe_synth_superblock(seed, sid, (uint64_t)b, std_dev, blk);
     uint8_t* dst = out + b * QMOE_SB_BYTES;
 #pragma unroll
     for (int i = 0; i < QMOE_SB_BYTES / 8; ++i) {

@@ -19,15 +19,16 @@
 //   * Every call on a device shares the one array and it keeps the last
 //     call's contents, so two calls that overlap on the GPU (different
 //     streams, or different host threads) race and corrupt each other;
-//     callers must order them.  The words that must start at zero (status and
-//     router arrival counter) are cleared, stream-ordered, at the start of
-//     every call.
-//   * The first call on a device looks up the array's device address
-//     (cudaGetSymbolAddress with that device current) and caches it; make
-//     that first call before any stream capture.
-//   * Device-side status (the workspace status word of qmoe_moe_block) is not
-//     reported back: this variant routes with its own router, so expert ids
-//     are always in range.
+//     callers must order them.  The router's arrival counter, which must
+//     start at zero, is cleared (stream-ordered) at the start of every call.
+//   * The first call on a device (of either entry point below) looks up the
+//     array's device address (cudaGetSymbolAddress with that device current),
+//     caches it and zeroes the status word once; make that first call before
+//     any stream capture.
+//   * Device-side status: the kernels record the first error they meet (a
+//     non-finite router logit, QMOE_ERR_NOT_FINITE; a bounded wait that ran
+//     out) in the array's status word, which keeps it across calls until
+//     qmoe_noalloc_read_status copies it out and clears it.
 #include <mutex>
 
 #include "common.cuh"
@@ -51,6 +52,8 @@ int scratch_on_current_device(void** out) {
     if (!g_scratch_by_device[dev]) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_qmoe_noalloc_scratch) != cudaSuccess || !p) return QMOE_ERR_CUDA;
+        // The status word (and the rest of the first 256 bytes) starts at zero.
+        if (cudaMemset(p, 0, 256) != cudaSuccess) return QMOE_ERR_CUDA;
         g_scratch_by_device[dev] = p;
     }
     *out = g_scratch_by_device[dev];
@@ -68,7 +71,17 @@ extern "C" int qmoe_moe_block_noalloc(const void* x, int x_dtype, int n_tokens,
     void* scratch = nullptr;
     const int rc = scratch_on_current_device(&scratch);
     if (rc != QMOE_OK) return rc;
-    // Status word and router arrival counter start at zero for every call.
-    if (cudaMemsetAsync(scratch, 0, 256, (cudaStream_t)stream) != cudaSuccess) return QMOE_ERR_CUDA;
+    // The router's arrival counter (at byte 64, after the status word) starts
+    // at zero for every call; the status word keeps errors until read.
+    if (cudaMemsetAsync(static_cast<unsigned char*>(scratch) + 64, 0, 192, (cudaStream_t)stream) != cudaSuccess)
+        return QMOE_ERR_CUDA;
     return qmoe_moe_block(x, x_dtype, n_tokens, w, dims, out, scratch, QMOE_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+extern "C" int qmoe_noalloc_read_status(int* status_out, void* stream) {
+    if (!status_out) return QMOE_ERR_INVALID_ARG;
+    void* scratch = nullptr;
+    const int rc = scratch_on_current_device(&scratch);
+    if (rc != QMOE_OK) return rc;
+    return qmoe_read_status(scratch, status_out, stream);
 }

@@ -21,6 +21,8 @@
 //   6. out = 0, then the down grouped GEMM and the small groups' down GEMV,
 //      both with a gate-weighted scatter-add.
 // The shared expert is group E: every token, weight sigmoid(x . gate_vec).
+#include <atomic>
+
 #include <math.h>
 
 #include "common.cuh"
@@ -1052,12 +1054,13 @@ PfLayout pf_layout(const qmoe_dims& d, int T) {
 int prefill_max_tokens() { return kPfMaxTokens; }
 
 // Largest expert group the grouped GEMV takes (0: every group goes to the
-// tensor-core path).
-static int g_small_group_max = kGvMax;
+// tensor-core path).  One process-wide setting for every device and thread,
+// read once per call when the call is issued; atomic, so a setter on one
+// thread and a prefill issued on another do not race.
+static std::atomic<int> g_small_group_max{kGvMax};
 int prefill_small_group_max(int n) {
-    const int prev = g_small_group_max;
-    if (n >= 0) g_small_group_max = n < kGvMax ? n : kGvMax;
-    return prev;
+    if (n < 0) return g_small_group_max.load();
+    return g_small_group_max.exchange(n < kGvMax ? n : kGvMax);
 }
 
 size_t prefill_workspace_bytes(const qmoe_dims& d, int T) { return pf_layout(d, T).total; }
@@ -1137,7 +1140,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     const int n = T * k;
     pf_count_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ids, n, E, counts, status);
     int4* gv = reinterpret_cast<int4*>(ws + L.gv);
-    pf_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, G, has_shared ? T : 0, g_small_group_max, offsets, ntiles, gv,
+    pf_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, G, has_shared ? T : 0, g_small_group_max.load(), offsets, ntiles, gv,
                                               meta);
     const size_t place_smem = (size_t)n * sizeof(short);
     err = cudaFuncSetAttribute(pf_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem);

@@ -93,6 +93,10 @@ struct SKArgs {
     float* h;                // [(K + 1) * I] (workspace)
     unsigned* sync;          // 8 counters, 128 B apart, then the abort word
     unsigned long long* trace;  // [2][64][kTraceSlots] phase stamps of CTA 0 and the last CTA, or null
+    __nv_bfloat16* act_trace;      // [n_layers][D]: every layer's output rounded to bf16, or null
+    int* ids_trace;                // [n_layers][K]: the selected ids in rank order, or null
+    float* w_trace;                // [n_layers][K]: their renormalised weights, or null
+    const __nv_bfloat16* teacher;  // [n_layers][D]: layer L's input in place of layer L-1's output, or null
     int* status;
     int n_layers, D, I, E, K;
     SKLayer L[kSKMaxLayers];
@@ -628,7 +632,8 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     // ---------------- prologue: layer 0's router logits --------------------
     if (tid < kRColW) {
         const int j = tid - xw;
-        xo[tid] = j >= 0 && j < nj ? __bfloat162float(a.x[p.j_lo + j]) : 0.0f;
+        const __nv_bfloat16* x0 = a.teacher ? a.teacher : a.x;
+        xo[tid] = j >= 0 && j < nj ? __bfloat162float(x0[p.j_lo + j]) : 0.0f;
     }
     bool ok = !__syncthreads_or(!mbar_wait(bar_rc, 0));
     if (ok) router_partial(p, S, sm, a.logits + (size_t)(blockIdx.x % kStackLogitReplicas) * G * 32, xchg);
@@ -657,9 +662,10 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             const int b = warp + i * kSKWarps;
             xv[i] = 0.0f;
             if (b < NXB)
-                xv[i] = L == 0 ? __bfloat162float(a.x[b * 32 + lane])
-                               : __bfloat162float(__ushort_as_bfloat16(
-                                     __ldcg(reinterpret_cast<const unsigned short*>(a.act) + b * 32 + lane)));
+                xv[i] = a.teacher ? __bfloat162float(a.teacher[(size_t)L * D + b * 32 + lane])
+                        : L == 0  ? __bfloat162float(a.x[b * 32 + lane])
+                                  : __bfloat162float(__ushort_as_bfloat16(
+                                       __ldcg(reinterpret_cast<const unsigned short*>(a.act) + b * 32 + lane)));
         }
         // logit i: fp32 at float (i / 4) * 32 + i % 4, or fp64 at double (i / 4) * 16 + i % 4
         const double* lg64 = reinterpret_cast<const double*>(lg);
@@ -678,6 +684,12 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             },
             [&](int pt, unsigned long long d) { trace_mark_after(a, L, 12 + pt, d); });
         trace_mark(a, L, 1);
+        if (a.ids_trace && blockIdx.x == 0 && tid < K) {
+            float ps = 0.0f;
+            for (int s2 = 0; s2 < K; ++s2) ps += tkv[s2];
+            a.ids_trace[L * K + tid] = tki[tid];
+            a.w_trace[L * K + tid] = tkv[tid] * (1.0f / ps);
+        }
         // Warps 0 and 1 issue the routed copies; the others stay off the
         // shared-memory pipe meanwhile (traffic there slows the issue).
         if (warp == 0) {
@@ -874,7 +886,8 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                     const __nv_bfloat16 xb = __float2bfloat16_rn(acc);
                     if (last) a.out[p.j_lo + j] = acc;
                     else a.act[p.j_lo + j] = xb;
-                    xo[xw + j] = __bfloat162float(xb);
+                    if (a.act_trace) a.act_trace[(size_t)L * D + p.j_lo + j] = xb;
+                    xo[xw + j] = __bfloat162float(a.teacher && !last ? a.teacher[(size_t)(L + 1) * D + p.j_lo + j] : xb);
                 }
             } else {
                 // this rank's partial of row j: kept, and stored into every
@@ -919,7 +932,9 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 const __nv_bfloat16 xb = __float2bfloat16_rn(v);
                 if (last) a.out[p.j_lo + tid] = v;
                 else a.act[p.j_lo + tid] = xb;
-                xo[xw + tid] = __bfloat162float(xb);
+                if (a.act_trace) a.act_trace[(size_t)L * D + p.j_lo + tid] = xb;
+                xo[xw + tid] =
+                    __bfloat162float(a.teacher && !last ? a.teacher[(size_t)(L + 1) * D + p.j_lo + tid] : xb);
             }
             if (__syncthreads_or(!x_ok)) {
                 if (tid == 0) {
@@ -1046,8 +1061,12 @@ bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers, int R) {
 
 cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* h, unsigned* sync,
                                 unsigned long long* trace, int* status, const qmoe_layer_weights* layers, int n_layers,
-                                const qmoe_dims& d, const XchgDesc* xc, cudaStream_t stream) {
+                                const qmoe_dims& d, const XchgDesc* xc, const StackTraceBufs& tb, cudaStream_t stream) {
     SKArgs a{};
+    a.act_trace = tb.act;
+    a.ids_trace = tb.ids;
+    a.w_trace = tb.weights;
+    a.teacher = tb.teacher;
     a.R = xc ? xc->R : 1;
     a.rank = xc ? xc->rank : 0;
     a.ib0 = d.down_ib0;

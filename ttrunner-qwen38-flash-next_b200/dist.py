@@ -79,6 +79,7 @@ class ShardedMoEStack:
         self._xchg = None
         self._own_buf = None
         self._peer_bufs: list[int] = []
+        self._needs_reset = False
         if exchange == "kernel":
             self._open_exchange()
 
@@ -112,15 +113,46 @@ class ShardedMoEStack:
         self._xchg = xc
         dist.barrier(group=self.group)
 
+    def reset_exchange(self) -> None:
+        """Every rank zeroes its own exchange buffer (launch counter and receive words), with no
+        launch in flight and a barrier before and after: the in-kernel exchange starts again from
+        launch 0.  Collective: every rank calls it (check_and_recover does, when any rank failed)."""
+        if self._xchg is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            check(lib.qmoe_xchg_reset(self._own_buf, self.shard.world, self.cfg.hidden, _stream()), "qmoe_xchg_reset")
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._needs_reset = False
+
+    def check_and_recover(self) -> int:
+        """Collective status check after a step: every rank reads its workspace status word; if
+        any rank saw an error (or failed to launch), every rank resets the exchange so that the
+        launch counters agree again.  Returns this rank's status (0 when all went well)."""
+        st = self.ws.read_status()
+        bad = torch.tensor([float(st != 0 or self._needs_reset)], device=self.device)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX, group=self.group)
+        if bad.item() > 0:
+            self.reset_exchange()
+        return st
+
     # ---- launches ------------------------------------------------------------
     def _launch(self, m: int) -> None:
         if self.exchange == "kernel":
             if m != 1:
                 raise ValueError("the in-kernel exchange runs one token per step")
-            check(lib.qmoe_stack_decode_xchg(self.x_in.data_ptr(), m, self.c_layer_array, len(self.c_layers),
-                                             ctypes.byref(self.dims), ctypes.byref(self._xchg),
-                                             self.act.data_ptr(), self.ws.ptr, self.ws.nbytes, _stream()),
-                  "qmoe_stack_decode_xchg")
+            try:
+                check(lib.qmoe_stack_decode_xchg(self.x_in.data_ptr(), m, self.c_layer_array, len(self.c_layers),
+                                                 ctypes.byref(self.dims), ctypes.byref(self._xchg),
+                                                 self.act.data_ptr(), self.ws.ptr, self.ws.nbytes, _stream()),
+                      "qmoe_stack_decode_xchg")
+            except BaseException:
+                # this rank's launch counter did not advance: the peers' next launches would wait
+                # for flags it never writes until every rank resets (check_and_recover)
+                self._needs_reset = True
+                raise
             return
         part = self.act[:m]
         for l, w in enumerate(self.c_layers):

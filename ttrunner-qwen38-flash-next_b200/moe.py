@@ -110,6 +110,13 @@ def prefill_workspace_for(dims: Dims, n_tokens: int, device: torch.device) -> Pr
     return ws
 
 
+def _shaped(out: torch.Tensor, x: torch.Tensor, out_dtype: torch.dtype | None) -> torch.Tensor:
+    """[M, K] fp32 -> x's leading shape ([1, 1, M, K] for the reference's operators) and dtype
+    `out_dtype` (None: fp32, the accumulation type; torch.bfloat16: the reference's device dtype)."""
+    out = out.view(*x.shape[:-1], out.shape[-1])
+    return out if out_dtype is None or out_dtype == torch.float32 else out.to(out_dtype)
+
+
 def _act(x: torch.Tensor) -> tuple[torch.Tensor, int]:
     """[.., M, D] bf16/fp32 -> contiguous [M, D] and its act dtype code."""
     if not x.is_cuda:
@@ -140,14 +147,18 @@ class MoELayer:
             raise ValueError(f"{m} tokens outside [1, {self.max_tokens}]")
         return m
 
-    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None,
+                 out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        """x [.., M, hidden] (e.g. the reference's [1, 1, M, K]) -> the same leading shape, fp32 (or
+        `out_dtype`).  `out`: an fp32 buffer of M x hidden values to write into (kept as given)."""
         x2, dt = _act(x)
         m = self._m(x2)
+        given = out is not None
         if out is None:
             out = torch.empty(m, self.cfg.hidden, dtype=torch.float32, device=x2.device)
         check(lib.qmoe_moe_block(x2.data_ptr(), dt, m, ctypes.byref(self.weights), ctypes.byref(self.dims),
                                  out.data_ptr(), self.ws.ptr, self.ws.nbytes, _stream()), "qmoe_moe_block")
-        return out
+        return out if given else _shaped(out, x, out_dtype)
 
     # ---- chunked prefill (tt/model.py:2812-2907 _prefill_ffn_half) ------------
     def prefill(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -264,8 +275,9 @@ def _check_u8(t: torch.Tensor, name: str) -> None:
 
 def moe_block(x: torch.Tensor, router_w: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor | None,
               down_w: torch.Tensor, top_k: int, num_experts: int, hidden_size: int,
-              intermediate_size: int) -> torch.Tensor:
-    """Routed experts only, x [.., M, K] -> [M, K] fp32 (tt/moe.py:159-295)."""
+              intermediate_size: int, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Routed experts only (tt/moe.py:159-295): x [1, 1, M, K] (or any [.., M, K]) -> the same
+    leading shape, fp32, or `out_dtype` (torch.bfloat16 for the reference's device dtype)."""
     _check_u8(gate_w, "gate_w")
     _check_u8(down_w, "down_w")
     x2, dt = _act(x)
@@ -280,12 +292,13 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, gate_w: torch.Tensor, up_
     out = torch.empty(m, hidden_size, dtype=torch.float32, device=x2.device)
     check(lib.qmoe_moe_block(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), out.data_ptr(),
                              ws.ptr, ws.nbytes, _stream()), "moe_block")
-    return out
+    return _shaped(out, x, out_dtype)
 
 
 def shared_expert(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, down_w: torch.Tensor,
-                  gate_vec: torch.Tensor) -> torch.Tensor:
-    """sigmoid(x . gate_vec) * down(silu(gate x) * up x) (tt/moe.py:983-1044)."""
+                  gate_vec: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """sigmoid(x . gate_vec) * down(silu(gate x) * up x) (tt/moe.py:983-1044): x [1, 1, M, K] (or
+    any [.., M, K]) -> the same leading shape, fp32 or `out_dtype`."""
     _check_u8(gate_w, "gate_w")
     _check_u8(up_w, "up_w")
     _check_u8(down_w, "down_w")
@@ -302,7 +315,7 @@ def shared_expert(x: torch.Tensor, gate_w: torch.Tensor, up_w: torch.Tensor, dow
     out = torch.empty(m, hidden, dtype=torch.float32, device=x2.device)
     check(lib.qmoe_shared_expert(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), out.data_ptr(),
                                  ws.ptr, ws.nbytes, _stream()), "shared_expert")
-    return out
+    return _shaped(out, x, out_dtype)
 
 
 def route_topk(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -327,26 +340,31 @@ def route_topk(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[tor
 
 
 def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Dense routing as tt/moe.py:308-327 returns it: (weights, keep), both [M, E]."""
+    """Dense routing as tt/moe.py:308-327 returns it: (weights, keep), both with x's leading shape
+    and E last ([1, 1, M, E] for the reference's [1, 1, M, K] activations)."""
     ids, wt = route_topk(x, router_w, top_k)
     E = router_w.shape[0]
     dense = torch.zeros(ids.shape[0], E, dtype=torch.float32, device=ids.device)
     dense.scatter_(1, ids.long(), wt)
     keep = torch.zeros_like(dense).scatter_(1, ids.long(), 1.0)
-    return dense, keep
+    lead = x.shape[:-1]
+    return dense.view(*lead, E), keep.view(*lead, E)
 
 
 def apply_experts(x: torch.Tensor, weights: torch.Tensor, keep: torch.Tensor, gate_w: torch.Tensor,
                   up_w: torch.Tensor | None, down_w: torch.Tensor, num_experts: int, hidden_size: int,
-                  intermediate_size: int) -> torch.Tensor:
-    """Routed output for dense routing (tt/moe.py:330-368): the experts kept per row."""
+                  intermediate_size: int, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Routed output for dense routing (tt/moe.py:330-368): the experts kept per row.  x [1, 1, M, K]
+    (or any [.., M, K]) with weights / keep [.., M, E] -> x's leading shape, fp32 or `out_dtype`."""
     _check_u8(gate_w, "gate_w")
     _check_u8(down_w, "down_w")
     x2, dt = _act(x)
     m = x2.shape[0]
+    weights = weights.reshape(m, -1)
+    keep = keep.reshape(m, -1)
     k = int(keep.sum(dim=-1).max().item())
     if k < 1:
-        return torch.zeros(m, hidden_size, dtype=torch.float32, device=x2.device)
+        return _shaped(torch.zeros(m, hidden_size, dtype=torch.float32, device=x2.device), x, out_dtype)
     kv, ids = torch.topk(keep.float() * 2.0 + weights.float(), k, dim=-1)
     wt = torch.gather(weights.float(), 1, ids)
     wt = torch.where(torch.gather(keep.float(), 1, ids) > 0, wt, torch.zeros_like(wt))
@@ -362,7 +380,7 @@ def apply_experts(x: torch.Tensor, weights: torch.Tensor, keep: torch.Tensor, ga
         check(lib.qmoe_prefill_experts(x2.data_ptr(), dt, m, ids32.data_ptr(), wt.data_ptr(), None, ctypes.byref(lw),
                                        ctypes.byref(dims), out.data_ptr(), pws.ptr, pws.nbytes, _stream()),
               "apply_experts")
-        return out
+        return _shaped(out, x, out_dtype)
     ws = workspace_for(dims, max(m, 1), x2.device)
     hs = intermediate_size
     h = torch.empty(m, k + 1, hs, dtype=torch.float32, device=x2.device)
@@ -374,4 +392,4 @@ def apply_experts(x: torch.Tensor, weights: torch.Tensor, keep: torch.Tensor, ga
     check(lib.qmoe_down_combine(h.data_ptr(), hs, m, ids32.data_ptr(), wt.data_ptr(), None, ctypes.byref(lw),
                                 ctypes.byref(dims), out.data_ptr(), ws.ptr, ws.nbytes, _stream()),
           "apply_experts down")
-    return out
+    return _shaped(out, x, out_dtype)

@@ -66,6 +66,32 @@ class MoEStack:
                                         buf.ctypes.data, _stream()), "qmoe_read_stack_trace")
         return buf
 
+    def route_trace(self, n_layers: int | None = None):
+        """The single launch's per-layer record of its last one-token call: (act [L, hidden] fp32
+        holding each layer's bf16 output, ids [L, k] int32, weights [L, k] fp32)."""
+        import numpy as np
+
+        n = self.n_layers if n_layers is None else n_layers
+        k, D = self.cfg.top_k, self.cfg.hidden
+        act = np.zeros((n, D), dtype=np.uint16)
+        ids = np.zeros((n, k), dtype=np.int32)
+        w = np.zeros((n, k), dtype=np.float32)
+        check(lib.qmoe_read_stack_route_trace(self.ws.ptr, ctypes.byref(self.dims), 1, n, act.ctypes.data,
+                                              ids.ctypes.data, w.ctypes.data, _stream()), "qmoe_read_stack_route_trace")
+        return (act.astype(np.uint32) << 16).view(np.float32), ids, w
+
+    def decode_teacher(self, x_layers: torch.Tensor) -> torch.Tensor:
+        """The single launch with layer L's input taken from x_layers[L] (bf16 [n_layers, hidden])
+        instead of layer L-1's output; returns the last layer's fp32 output.  Per-layer outputs,
+        ids and weights: route_trace()."""
+        xl = x_layers.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        if xl.shape != (self.n_layers, self.cfg.hidden):
+            raise ValueError(f"x_layers must be [{self.n_layers}, {self.cfg.hidden}]")
+        check(lib.qmoe_stack_decode_teacher(xl.data_ptr(), self.c_layers, self.n_layers, ctypes.byref(self.dims),
+                                            self.out.data_ptr(), self.ws.ptr, self.ws.nbytes, _stream()),
+              "qmoe_stack_decode_teacher")
+        return self.out[:1]
+
     def single_launch(self, m: int = 1) -> bool:
         """True when a step of m tokens is one persistent kernel launch."""
         return bool(lib.qmoe_stack_single_launch(ctypes.byref(self.dims), m, self.n_layers))

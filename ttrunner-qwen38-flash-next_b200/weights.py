@@ -95,7 +95,7 @@ class HostLayer:
 def _host_expert(cfg: MoEConfig, layer: int, seed: int, e: int, threads: int = _THREADS):
     D, I = cfg.hidden, cfg.inter
     gu = quantize_host(_normal([seed, layer, TAG_GATE_UP, e], 2 * I * D, cfg.weight_std).reshape(2 * I, D), threads)
-    dn = quantize_host(_normal([seed, layer, TAG_DOWN, e], D * I, cfg.weight_std).reshape(D, I), threads)
+    dn = quantize_host(_normal([seed, layer, TAG_DOWN, e], D * I, cfg.dn_std).reshape(D, I), threads)
     return gu, dn
 
 
@@ -107,7 +107,7 @@ def synth_host_layer(cfg: MoEConfig, layer: int = 0, seed: int = 0, all_experts:
         router=_normal([seed, layer, TAG_ROUTER], cfg.n_experts * D, cfg.weight_std).reshape(cfg.n_experts, D),
         gate_vec=_normal([seed, layer, TAG_GATE_VEC], D, cfg.weight_std),
         sh_gate_up=quantize_host(_normal([seed, layer, TAG_SH_GATE_UP], 2 * Ish * D, cfg.weight_std).reshape(2 * Ish, D)),
-        sh_down=quantize_host(_normal([seed, layer, TAG_SH_DOWN], D * Ish, cfg.weight_std).reshape(D, Ish)),
+        sh_down=quantize_host(_normal([seed, layer, TAG_SH_DOWN], D * Ish, cfg.dn_std).reshape(D, Ish)),
     )
     if all_experts:
         hl.ensure_all()
@@ -237,12 +237,12 @@ def synth_device_layer(cfg: MoEConfig, layer: int, seed: int = 0, shard: Shard =
     for j, e in enumerate(range(e_lo, e_hi)):
         if sliced:
             _dev_iq4(seed, _sid(layer, TAG_GATE_UP, e), 2 * I * D, std, gu_full, stream)
-            _dev_iq4(seed, _sid(layer, TAG_DOWN, e), D * I, std, dn_full, stream)
+            _dev_iq4(seed, _sid(layer, TAG_DOWN, e), D * I, cfg.dn_std, dn_full, stream)
             gate_up[j].copy_(slice_gate_up(gu_full, I, i_lo, i_hi))
             down[j].copy_(slice_down(dn_full, i_lo, i_hi))
         else:
             _dev_iq4(seed, _sid(layer, TAG_GATE_UP, e), 2 * I * D, std, gate_up[j], stream)
-            _dev_iq4(seed, _sid(layer, TAG_DOWN, e), D * I, std, down[j], stream)
+            _dev_iq4(seed, _sid(layer, TAG_DOWN, e), D * I, cfg.dn_std, down[j], stream)
     gv = sh_gu = sh_dn = None
     if shard.has_shared():
         Ish = cfg.shared_inter
@@ -252,7 +252,7 @@ def synth_device_layer(cfg: MoEConfig, layer: int, seed: int = 0, shard: Shard =
         full_gu = torch.empty(2 * Ish, rb, dtype=torch.uint8, device=dev)
         full_dn = torch.empty(D, iq4xs_bytes(Ish), dtype=torch.uint8, device=dev)
         _dev_iq4(seed, _sid(layer, TAG_SH_GATE_UP), 2 * Ish * D, std, full_gu, stream)
-        _dev_iq4(seed, _sid(layer, TAG_SH_DOWN), D * Ish, std, full_dn, stream)
+        _dev_iq4(seed, _sid(layer, TAG_SH_DOWN), D * Ish, cfg.dn_std, full_dn, stream)
         sh_gu = slice_gate_up(full_gu, Ish, s_lo, s_hi).contiguous()
         sh_dn = slice_down(full_dn, s_lo, s_hi).contiguous()
     return DeviceLayer(cfg=cfg, shard=shard, router=router, gate_vec=gv, gate_up=gate_up, down=down,
