@@ -166,17 +166,17 @@ int qmoe_moe_block(const void* x, int x_dtype, int n_tokens, const qmoe_layer_we
 int qmoe_stack_single_launch(const qmoe_dims* dims, int n_tokens, int n_layers);
 
 /* Tracing: the single-launch stack kernel stamps its SM's cycle counter at 24
- * points of every layer in CTA 0 into the workspace (unused points stay 0):
- * B start, top-k done, gate|up copies issued, down copies issued, copies
- * done, gate|up rows done, h written, after barrier H, h converted, down
- * resident, down done, router partial done (0-11); inside the top-k: logits
- * loaded, x converted, threshold found, ranked (12-15); with an exchange
- * between ranks: partial rows sent, peers' rows summed (16-17); gate|up
- * chunks 0-5 landed, as seen by the warp of the chunk's first pair (18-23).  The last
- * CTA stamps the same points.  Copies the n_layers x 24 stamps of CTA 0 and
- * then those of the last CTA (2 x n_layers x 24 values) of the last launch
- * made with this workspace and n_tokens to host_out (synchronises `stream`).
- * The reference's analogue is its section profiler (tt/bench.py:33-78). */
+ * points of every layer into the workspace (unused points stay 0): CTA 0
+ * and the last CTA each at layer start, logit round complete, ranked and
+ * copies issued, x ready, shared pairs done, gate|up pairs done, h words
+ * written, h round complete, h converted, down rows landed, down done,
+ * output rows written, logit partials added (0-12), gate|up chunks 0-5
+ * landed (16-21), and with an exchange between ranks partial rows sent,
+ * peers' rows summed (22-23).  Copies the n_layers x 24 stamps of CTA 0 and
+ * then those of the last CTA (2 x n_layers x 24 values; the two are
+ * different SMs' clocks) of the last launch made with this workspace and
+ * n_tokens to host_out (synchronises `stream`).  The reference's analogue is
+ * its section profiler (tt/bench.py:33-78). */
 int qmoe_read_stack_trace(void* workspace, const qmoe_dims* dims, int n_tokens, int n_layers,
                           uint64_t* host_out, void* stream);
 

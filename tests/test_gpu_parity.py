@@ -271,11 +271,12 @@ def test_stack_kernel_matches_layer_chain(pkg, oracle):
             checked += 1
         act = want.to(torch.bfloat16)
     assert checked >= 2
-    # Repeated launches reuse the workspace.  The single launch sums each layer's router logits
-    # from per-CTA partials with fp32 atomics, so reruns agree to fp32 rounding, not bit for bit.
+    # Repeated launches reuse the workspace (its tagged words and launch counter).  The single
+    # launch sums each layer's router logits from per-CTA partials in fp64, exactly, so a rerun
+    # gives the same bits even where routing sits near a tie (this shape's third layer).
     again = stack.decode(x).clone()
     torch.cuda.synchronize()
-    assert oracle.max_rel_err(again.cpu().numpy(), got.cpu().numpy()) <= 1e-4
+    assert torch.equal(again, got)
 
 
 def test_deterministic_reruns(pkg):

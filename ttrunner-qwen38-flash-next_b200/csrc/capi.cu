@@ -209,9 +209,9 @@ WsLayout ws_layout(const qmoe_dims& d, int max_tokens) {
     L.act = off;
     off = align_up(off + (size_t)M * d.hidden * 4, 256);
     L.sync = off;
-    off = align_up(off + stack_sync_bytes(d.n_experts), 256);
+    off = align_up(off + stack_sync_bytes(d.n_experts, d.hidden, d.top_k, d.inter_local), 256);
     L.trace = off;
-    off = align_up(off + 2 * 64 * kTraceSlots * 8, 256);
+    off = align_up(off + kTraceBytes, 256);
     L.act_trace = off;
     off = align_up(off + (size_t)64 * d.hidden * 2, 256);
     L.route_trace = off;
@@ -421,6 +421,12 @@ int qmoe_read_stack_trace(void* workspace, const qmoe_dims* dims, int n_tokens, 
     if (!workspace || !host_out || n_layers < 1 || n_layers > 64) return QMOE_ERR_INVALID_ARG;
     const WsLayout L = ws_layout(*dims, n_tokens);
     cudaStream_t s = (cudaStream_t)stream;
+#if defined(QMOE_SK_FULLTRACE)
+    QMOE_TRY(cuda_status(cudaMemcpyAsync(host_out, (unsigned char*)workspace + L.trace,
+                                         (size_t)n_layers * kFullTraceCtas * kTraceSlots * 8, cudaMemcpyDeviceToHost,
+                                         s)));
+    return cuda_status(cudaStreamSynchronize(s));
+#endif
     const size_t rows = (size_t)n_layers * kTraceSlots * sizeof(uint64_t);
     QMOE_TRY(cuda_status(cudaMemcpyAsync(host_out, (unsigned char*)workspace + L.trace, rows,
                                          cudaMemcpyDeviceToHost, s)));
@@ -463,7 +469,7 @@ int qmoe_stack_decode(const void* x, int n_tokens, const qmoe_layer_weights* lay
                     aligned(w.sh_down, 16);
     }
     if (aligned16 && stack_kernel_supported(*dims, n_tokens, n_layers, 1))
-        return cuda_status(launch_stack_kernel(x, out, ws.act(), ws.h(), ws.sync(), ws.trace(), ws.status(), layers,
+        return cuda_status(launch_stack_kernel(x, out, (unsigned char*)ws.sync(), ws.trace(), ws.status(), layers,
                                                n_layers, *dims, nullptr, ws.trace_bufs(dims->top_k), s));
     // Otherwise three launches per layer. Layer L+1 reads `out` (layer L's result) in its router and gate|up
     // launches; its down launch overwrites `out` only after both, in stream
@@ -494,7 +500,7 @@ int qmoe_stack_decode_teacher(const void* x_layers, const qmoe_layer_weights* la
     if (!stack_kernel_supported(*dims, 1, n_layers, 1)) return QMOE_ERR_UNSUPPORTED;
     Ws ws;
     QMOE_TRY(get_ws(workspace, workspace_bytes, dims, 1, &ws));
-    return cuda_status(launch_stack_kernel(x_layers, out, ws.act(), ws.h(), ws.sync(), ws.trace(), ws.status(),
+    return cuda_status(launch_stack_kernel(x_layers, out, (unsigned char*)ws.sync(), ws.trace(), ws.status(),
                                            layers, n_layers, *dims, nullptr, ws.trace_bufs(dims->top_k, x_layers),
                                            (cudaStream_t)stream));
 }
@@ -614,7 +620,7 @@ int qmoe_stack_decode_xchg(const void* x, int n_tokens, const qmoe_layer_weights
     if (!stack_kernel_supported(*dims, n_tokens, n_layers, xc->n_ranks)) return QMOE_ERR_UNSUPPORTED;
     Ws ws;
     QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
-    return cuda_status(launch_stack_kernel(x, out, ws.act(), ws.h(), ws.sync(), ws.trace(), ws.status(), layers,
+    return cuda_status(launch_stack_kernel(x, out, (unsigned char*)ws.sync(), ws.trace(), ws.status(), layers,
                                            n_layers, *dims, &desc, ws.trace_bufs(dims->top_k), (cudaStream_t)stream));
 }
 

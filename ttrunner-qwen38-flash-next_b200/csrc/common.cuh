@@ -5,6 +5,10 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "../../include/qmoe_b200.h"
 #include "iq4xs.cuh"
 
@@ -26,9 +30,8 @@ struct WsLayout {
     size_t shared;      // fp32 [max_tokens]
     size_t h;           // fp32 [max_tokens][top_k + 1][h_stride]
     size_t act;         // fp32 [max_tokens][hidden]: the stack kernel's layer activation
-    size_t sync;        // grid-barrier counters (8 x 128 B), the abort word, then the stack
-                        // kernel's two router-logit accumulators (stack_sync_bytes)
-    size_t trace;       // u64 [64 layers][8]: the stack kernel's phase timestamps
+    size_t sync;        // the stack kernel's synchronisation area (stack_sync_bytes)
+    size_t trace;       // u64: the stack kernel's phase timestamps (kTraceBytes)
     size_t act_trace;   // bf16 [64 layers][hidden]: the single launch's per-layer outputs
     size_t route_trace; // int32 [64][16] ids, then fp32 [64][16] weights, per layer
     size_t total;
@@ -37,21 +40,54 @@ struct WsLayout {
 
 WsLayout ws_layout(const qmoe_dims& d, int max_tokens);
 
-// The stack kernel's zero-initialised words: 8 barrier counters 128 B apart and
-// the abort word (1152 B), then two accumulators of E + 1 router logits, each
-// in kStackLogitReplicas replicas (CTA c adds into replica c % replicas), four
-// logits per 128-byte line so that the CTAs' atomic adds spread over lines.
-// After them, two buffers of per-32-value block maxima of h (|h| bits, for
-// atomicMax), one per layer parity, one word per 128-byte line.
-constexpr int kStackLogitReplicas = 1;
-constexpr int kStackHmaxBlocks = (kMaxTopK + 1) * 16;     // (k + 1) slots x 512 / 32 blocks
-constexpr int kStackHmaxWords = kStackHmaxBlocks * 32;    // a line per block
-inline size_t stack_logit_groups(int E) { return (size_t)(E + 1 + 3) / 4; }
-inline size_t stack_logit_bytes(int E) { return 2 * (size_t)kStackLogitReplicas * stack_logit_groups(E) * 128; }
-inline size_t stack_sync_bytes(int E) { return 1152 + stack_logit_bytes(E) + 2 * kStackHmaxWords * 4; }
+// A kernel's opt-in to at least `bytes` of dynamic shared memory, made only
+// when it raises what this process already set for (kernel, device), instead
+// of before every launch.
+inline cudaError_t smem_opt_in(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> set_to;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> g(mu);
+    int& cur = set_to[std::make_pair(fn, dev)];
+    if (bytes <= cur) return cudaSuccess;
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err == cudaSuccess) cur = bytes;
+    return err;
+}
+
+// The stack kernel's synchronisation area (the workspace's `sync` region),
+// byte offsets from its base, every item on its own 128-byte lines:
+//   0      launch counter (u32; kept across launches: the tags below use it)
+//   128    abort word (u32)
+//   256    arrival counters of the logit rounds: 8 lines (u32 at each start)
+//   1280   arrival counters of the h rounds: 8 lines
+//   2304   router-logit accumulators: 3 buffers (layer % 3) x (E + 1)
+//          lines, one fp64 logit at the start of each line
+//   then   the layer activation as tagged words: D u32
+//   then   SwiGLU activations h as tagged words: (k + 1) x I u32
+// [128, end of the accumulators) is zeroed before every launch; the tagged
+// words carry the launch counter in their tags instead.
+constexpr size_t kStackAbortOff = 128;
+constexpr size_t kStackXCountOff = 256;
+constexpr size_t kStackHCountOff = 1280;
+constexpr size_t kStackLogitOff = 2304;
+__host__ __device__ constexpr size_t stack_logit_bytes(int E) { return (size_t)3 * (E + 1) * 128; }
+__host__ __device__ constexpr size_t stack_xw_off(int E) { return kStackLogitOff + stack_logit_bytes(E); }
+__host__ __device__ constexpr size_t stack_hw_off(int E, int D) { return stack_xw_off(E) + (((size_t)D * 4 + 127) & ~(size_t)127); }
+__host__ __device__ constexpr size_t stack_sync_bytes(int E, int D, int K, int I) {
+    return stack_hw_off(E, D) + (size_t)(K + 1) * I * 4;
+}
 
 // Phase stamps per layer in the stack kernel's trace ([2][64 layers][slots]).
 constexpr int kTraceSlots = 24;
+#if defined(QMOE_SK_FULLTRACE)
+constexpr int kFullTraceCtas = 160;  // development builds: every CTA's stamps
+constexpr size_t kTraceBytes = (size_t)64 * kFullTraceCtas * kTraceSlots * 8;
+#else
+constexpr size_t kTraceBytes = (size_t)2 * 64 * kTraceSlots * 8;
+#endif
 
 // In-kernel exchange between ranks: a rank's exchange buffer holds its
 // launch counter (first 128 bytes), then the receive words
@@ -132,9 +168,9 @@ struct StackTraceBufs {
 // their partial rows inside the kernel when R > 1.
 // xc: null for one rank.
 bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers, int R);
-cudaError_t launch_stack_kernel(const void* x, float* out, float* act, float* h, unsigned* sync,
-                                unsigned long long* trace, int* status, const qmoe_layer_weights* layers, int n_layers,
-                                const qmoe_dims& d, const XchgDesc* xc, const StackTraceBufs& tb, cudaStream_t stream);
+cudaError_t launch_stack_kernel(const void* x, float* out, unsigned char* sync, unsigned long long* trace,
+                                int* status, const qmoe_layer_weights* layers, int n_layers, const qmoe_dims& d,
+                                const XchgDesc* xc, const StackTraceBufs& tb, cudaStream_t stream);
 
 // Prefill / large verify chunks (prefill.cu).
 int prefill_max_tokens();

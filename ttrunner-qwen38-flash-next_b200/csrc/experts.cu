@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
 template <typename K>
 cudaError_t launch_with_smem(K kernel, unsigned grid, size_t smem, const ExpertArgs& a,
                              cudaStream_t s) {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t err = smem_opt_in(reinterpret_cast<const void*>(kernel), (int)smem);
     if (err != cudaSuccess) return err;
     kernel<<<grid, kWarps * 32, smem, s>>>(a);
     return cudaGetLastError();

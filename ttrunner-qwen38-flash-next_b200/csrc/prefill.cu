@@ -1143,7 +1143,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     pf_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, G, has_shared ? T : 0, g_small_group_max.load(), offsets, ntiles, gv,
                                               meta);
     const size_t place_smem = (size_t)n * sizeof(short);
-    err = cudaFuncSetAttribute(pf_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem);
+    err = smem_opt_in(reinterpret_cast<const void*>(pf_place_kernel), (int)place_smem);
     if (err != cudaSuccess) return err;
     pf_place_kernel<<<(unsigned)((G + kPlaceWarps - 1) / kPlaceWarps), kPlaceWarps * 32, place_smem, s>>>(
         ids, weights, shared_logit, T, k, E, has_shared ? 1 : 0, offsets, slot_tok, slot_w);
@@ -1168,7 +1168,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     a.out = out;
     a.status = status;
     a.trace = reinterpret_cast<unsigned long long*>(ws + L.trace);
-    err = cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemBytes);
+    err = smem_opt_in(reinterpret_cast<const void*>(grouped_gemm_kernel), kGSmemBytes);
     if (err != cudaSuccess) return err;
     const int n_sm = device_sm_count();
     const unsigned long long rb = (unsigned long long)(d.hidden / 256) * QMOE_SB_BYTES;
@@ -1217,7 +1217,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
         const size_t gsm = (size_t)kGvMax * nb * 16 * 4 + (size_t)kGvMax * nb * 4;
         void (*gk)(GvArgs) = nb <= 32 ? pf_gv_gateup_kernel<1> : nb <= 64 ? pf_gv_gateup_kernel<2>
                                                                            : pf_gv_gateup_kernel<4>;
-        err = cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+        err = smem_opt_in(reinterpret_cast<const void*>(gk), (int)gsm);
         if (err != cudaSuccess) return err;
         int per_sm = 1;  // persistent: as many CTAs as stay resident
         err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gk, kGvWarps * 32, gsm);
@@ -1230,7 +1230,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     {
         const int nbh = d.inter / 32;
         const size_t dsm = (size_t)kGvMax * nbh * 16 * 4 + (size_t)kGvMax * nbh * 4;
-        err = cudaFuncSetAttribute(pf_gv_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm);
+        err = smem_opt_in(reinterpret_cast<const void*>(pf_gv_down_kernel), (int)dsm);
         if (err != cudaSuccess) return err;
         int per_sm = 1;
         err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pf_gv_down_kernel, kGvWarps * 32, dsm);

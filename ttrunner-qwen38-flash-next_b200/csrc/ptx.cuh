@@ -80,6 +80,12 @@ __device__ __forceinline__ void cp_async_wait() {
 // Makes this thread's generic-proxy shared-memory writes visible to the async
 // proxy (bulk copies, tensor core operand reads).
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Orders this thread's generic-proxy view of global memory (e.g. data another
+// CTA published and this thread acquired) before its later async-proxy
+// (bulk-copy) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 
 // 8-byte stores and loads at system scope: a word another GPU stores into
 // this GPU's memory over NVLink (or this GPU into a peer's) is seen whole.

@@ -112,8 +112,7 @@ cudaError_t launch_route_t(const RouteArgs& a, cudaStream_t s) {
     const int rows = a.E + (a.gate_vec ? 1 : 0);
     const unsigned grid = (unsigned)((rows + kRouteWarps - 1) / kRouteWarps);
     const size_t smem = (size_t)a.M * a.D * sizeof(float);
-    cudaError_t err = cudaFuncSetAttribute(route_kernel<MAXM>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t err = smem_opt_in(reinterpret_cast<const void*>(route_kernel<MAXM>), (int)smem);
     if (err != cudaSuccess) return err;
     route_kernel<MAXM><<<grid, kRouteWarps * 32, smem, s>>>(a);
     return cudaGetLastError();

@@ -24,12 +24,11 @@ from .weights import DeviceLayer
 
 # The single-launch kernel's phase stamps per layer (qmoe_read_stack_trace).
 TRACE_SLOTS = 24
-TRACE_POINTS = ("B start", "top-k done", "gate|up copies issued", "down copies issued (warp 1)",
-                "copies done", "gate|up rows done", "h written", "after barrier H", "h converted",
-                "down resident", "down done", "router partial done", "top-k: logits loaded", "top-k: x converted",
-                "top-k: threshold found", "top-k: ranked", "exchange: partial rows sent",
-                "exchange: peers' rows summed", "gate|up chunk 0 landed", "chunk 1 landed", "chunk 2 landed",
-                "chunk 3 landed", "chunk 4 landed", "chunk 5 landed")
+TRACE_POINTS = ("layer start", "logit round complete", "ranked, copies issued", "x ready", "shared pairs done",
+                "gate|up pairs done", "h words written", "h round complete", "h converted", "down rows landed",
+                "down done", "output rows written", "logit partials added", "", "", "",
+                "gate|up chunk 0 landed", "chunk 1 landed", "chunk 2 landed", "chunk 3 landed", "chunk 4 landed",
+                "chunk 5 landed", "exchange: partial rows sent", "exchange: peers' rows summed")
 
 
 class MoEStack:
@@ -58,7 +57,7 @@ class MoEStack:
     def phase_trace(self, m: int = 1):
         """Raw SM cycle-counter stamps of the last single-launch step,
         [2, n_layers, TRACE_SLOTS]: CTA 0 then the last CTA, in the order of
-        TRACE_POINTS (later slots unused)."""
+        TRACE_POINTS (unnamed slots unused)."""
         import numpy as np
 
         buf = np.zeros((2, self.n_layers, TRACE_SLOTS), dtype=np.uint64)
