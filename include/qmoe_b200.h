@@ -136,6 +136,21 @@ int qmoe_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weight
  * Replaces tt/moe.py:946-953 (gather_gemv MODE 2 + fused_swiglu) and the
  * shared half of tt/moe.py:999-1028.  h: device fp32 [M, k+1, h_stride]; slot
  * k holds the shared expert. */
+/* Router with the tie-admitting threshold select: the reference device
+ * select's other mode (scripts/kernels/router_select.cpp:223-255,
+ * TT_ROUTER_EXACT_TOPK=0; the ttnn chain tt/moe.py:308-327).  Softmax
+ * probabilities p_e over all E experts (rounded to bf16 when probs_bf16 = 1,
+ * as the ttnn chain compares them); t = the top_k-th largest p counting
+ * equal values separately; total = the sum of every p_e >= t.  The
+ * dims->top_k slots (K_SEL, >= top_k) take the largest positive p_e >= t
+ * among experts [expert_lo, expert_hi), descending, ties to the lower id, as
+ * (id, p_e * (1 / total)); slots left over hold (expert_lo, 0), which the
+ * expert stages compute with weight 0.  The probability sums run over each
+ * lane's ids in order and then a butterfly over 32 lanes (the oracle's
+ * route_threshold restates that order).  ids/weights: device [M, dims->top_k]. */
+int qmoe_route_threshold(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                         const qmoe_dims* dims, int top_k, int probs_bf16, int32_t* ids, float* weights,
+                         float* shared_logit, void* workspace, size_t workspace_bytes, void* stream);
 int qmoe_gateup_swiglu(const void* x, int x_dtype, int n_tokens, const int32_t* ids,
                        const qmoe_layer_weights* w, const qmoe_dims* dims, float* h,
                        int h_stride, void* workspace, size_t workspace_bytes, void* stream);
@@ -167,10 +182,10 @@ int qmoe_stack_single_launch(const qmoe_dims* dims, int n_tokens, int n_layers);
 
 /* Tracing: the single-launch stack kernel stamps its SM's cycle counter at 24
  * points of every layer into the workspace (unused points stay 0): CTA 0
- * and the last CTA each at layer start, logit round complete, ranked and
- * copies issued, x ready, shared pairs done, gate|up pairs done, h words
+ * and the last CTA each at layer start, x gathered, x checked, ranked and
+ * gate|up copies issued, shared pairs done, gate|up pairs done, h words
  * written, h round complete, h converted, down rows landed, down done,
- * output rows written, logit partials added (0-12), gate|up chunks 0-5
+ * output rows written, arrived (0-12), gate|up chunks 0-5
  * landed (16-21), and with an exchange between ranks partial rows sent,
  * peers' rows summed (22-23).  Copies the n_layers x 24 stamps of CTA 0 and
  * then those of the last CTA (2 x n_layers x 24 values; the two are
@@ -332,6 +347,11 @@ size_t qmoe_prefill_workspace_bytes(const qmoe_dims* dims, int n_tokens);
 int qmoe_prefill_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
                        const qmoe_dims* dims, int32_t* ids, float* weights, float* shared_logit,
                        void* workspace, size_t workspace_bytes, void* stream);
+/* The same with the tie-admitting threshold select (as qmoe_route_threshold;
+ * the whole expert range only); ids/weights [T, dims->top_k]. */
+int qmoe_prefill_route_threshold(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                                 const qmoe_dims* dims, int top_k, int probs_bf16, int32_t* ids, float* weights,
+                                 float* shared_logit, void* workspace, size_t workspace_bytes, void* stream);
 /* out [T, hidden] fp32 = sum_s weights[t,s] * expert_{ids[t,s]}(x_t)
  *                      + sigmoid(shared_logit[t]) * shared(x_t) (when the dims
  * carry a shared expert; shared_logit is then required).  Out-of-range ids

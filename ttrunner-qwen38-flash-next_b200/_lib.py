@@ -105,6 +105,8 @@ _SIGS = {
     "qmoe_synth_f32_host": (c_int, [c_uint64, c_uint64, c_int64, c_float, _P, c_int]),
     "qmoe_route": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P, _P, _P,
                            c_size_t, _P]),
+    "qmoe_route_threshold": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), c_int, c_int, _P,
+                                     _P, _P, _P, c_size_t, _P]),
     "qmoe_gateup_swiglu": (c_int, [_P, c_int, c_int, _P, POINTER(LayerWeights), POINTER(Dims), _P,
                                    c_int, _P, c_size_t, _P]),
     "qmoe_down_combine": (c_int, [_P, c_int, c_int, _P, _P, _P, POINTER(LayerWeights),
@@ -135,6 +137,8 @@ _SIGS = {
     "qmoe_prefill_workspace_bytes": (c_size_t, [POINTER(Dims), c_int]),
     "qmoe_prefill_route": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P, _P, _P,
                                    c_size_t, _P]),
+    "qmoe_prefill_route_threshold": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), c_int, c_int,
+                                             _P, _P, _P, _P, c_size_t, _P]),
     "qmoe_prefill_experts": (c_int, [_P, c_int, c_int, _P, _P, _P, POINTER(LayerWeights), POINTER(Dims), _P,
                                      _P, c_size_t, _P]),
     "qmoe_prefill": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P, c_size_t, _P]),

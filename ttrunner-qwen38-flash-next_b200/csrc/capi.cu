@@ -157,7 +157,8 @@ int get_ws(void* workspace, size_t bytes, const qmoe_dims* d, int M, Ws* ws) {
     } while (0)
 
 int run_route(const void* x, int x_dtype, int M, const qmoe_layer_weights* w, const qmoe_dims* d,
-              int32_t* ids, float* weights, float* shared_logit, const Ws& ws, cudaStream_t s) {
+              int32_t* ids, float* weights, float* shared_logit, const Ws& ws, cudaStream_t s, int thr_mode = 0,
+              int thr_k = 0) {
     RouteArgs r{};
     r.x = x;
     r.x_f32 = x_dtype == QMOE_ACT_F32;
@@ -173,6 +174,10 @@ int run_route(const void* x, int x_dtype, int M, const qmoe_layer_weights* w, co
     r.weights = weights;
     r.shared_logit = shared_logit;
     r.status = ws.status();
+    r.thr_mode = thr_mode;
+    r.thr_k = thr_k;
+    r.e_lo = d->expert_lo;
+    r.e_hi = d->expert_hi;
     return cuda_status(launch_route(r, s));
 }
 
@@ -318,6 +323,22 @@ int qmoe_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weight
     Ws ws;
     QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
     return run_route(x, x_dtype, n_tokens, w, dims, ids, weights, shared_logit, ws, (cudaStream_t)stream);
+}
+
+int qmoe_route_threshold(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                         const qmoe_dims* dims, int top_k, int probs_bf16, int32_t* ids, float* weights,
+                         float* shared_logit, void* workspace, size_t workspace_bytes, void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_act(x, x_dtype));
+    QMOE_TRY(check_weights_route(w));
+    QMOE_TRY(route_smem_ok(n_tokens, dims->hidden));
+    if (!ids || !weights) return QMOE_ERR_INVALID_ARG;
+    if (top_k < 1 || top_k > kMaxTopK || (probs_bf16 != 0 && probs_bf16 != 1)) return QMOE_ERR_INVALID_ARG;
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    return run_route(x, x_dtype, n_tokens, w, dims, ids, weights, shared_logit, ws, (cudaStream_t)stream,
+                     probs_bf16 ? 2 : 1, top_k);
 }
 
 int qmoe_gateup_swiglu(const void* x, int x_dtype, int n_tokens, const int32_t* ids,
@@ -660,9 +681,10 @@ size_t qmoe_prefill_workspace_bytes(const qmoe_dims* dims, int n_tokens) {
     return prefill_workspace_bytes(*dims, n_tokens);
 }
 
-int qmoe_prefill_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+namespace {
+int prefill_route_impl(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
                        const qmoe_dims* dims, int32_t* ids, float* weights, float* shared_logit,
-                       void* workspace, size_t workspace_bytes, void* stream) {
+                       void* workspace, size_t workspace_bytes, void* stream, int thr_mode, int thr_k) {
     // Routing alone needs only valid dims and a chunk size the workspace covers.
     QMOE_TRY(check_dims(dims));
     if (n_tokens < 1 || n_tokens > prefill_max_tokens()) return QMOE_ERR_UNSUPPORTED;
@@ -674,7 +696,25 @@ int qmoe_prefill_route(const void* x, int x_dtype, int n_tokens, const qmoe_laye
     unsigned char* ws = (unsigned char*)workspace;
     const bool x_ok = x_dtype == QMOE_ACT_BF16 && aligned(x, 16);
     const __nv_bfloat16* xb = prefill_act_bf16(x, x_dtype == QMOE_ACT_F32, x_ok, n_tokens, *dims, ws, s);
-    return cuda_status(launch_prefill_route(xb, n_tokens, *w, *dims, ws, ids, weights, shared_logit, s));
+    return cuda_status(
+        launch_prefill_route(xb, n_tokens, *w, *dims, ws, ids, weights, shared_logit, s, thr_mode, thr_k));
+}
+}  // namespace
+
+int qmoe_prefill_route(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                       const qmoe_dims* dims, int32_t* ids, float* weights, float* shared_logit,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+    return prefill_route_impl(x, x_dtype, n_tokens, w, dims, ids, weights, shared_logit, workspace,
+                              workspace_bytes, stream, 0, 0);
+}
+
+int qmoe_prefill_route_threshold(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                                 const qmoe_dims* dims, int top_k, int probs_bf16, int32_t* ids, float* weights,
+                                 float* shared_logit, void* workspace, size_t workspace_bytes, void* stream) {
+    if (top_k < 1 || top_k > kMaxTopK || (probs_bf16 != 0 && probs_bf16 != 1)) return QMOE_ERR_INVALID_ARG;
+    if (dims && (dims->expert_lo != 0 || dims->expert_hi != dims->n_experts)) return QMOE_ERR_UNSUPPORTED;
+    return prefill_route_impl(x, x_dtype, n_tokens, w, dims, ids, weights, shared_logit, workspace,
+                              workspace_bytes, stream, probs_bf16 ? 2 : 1, top_k);
 }
 
 int qmoe_prefill_experts(const void* x, int x_dtype, int n_tokens, const int32_t* ids, const float* weights,

@@ -61,19 +61,20 @@ inline cudaError_t smem_opt_in(const void* fn, int bytes) {
 // byte offsets from its base, every item on its own 128-byte lines:
 //   0      launch counter (u32; kept across launches: the tags below use it)
 //   128    abort word (u32)
-//   256    arrival counters of the logit rounds: 8 lines (u32 at each start)
+//   256    arrival counters of the activation rounds: 8 lines (u32 at each start)
 //   1280   arrival counters of the h rounds: 8 lines
-//   2304   router-logit accumulators: 3 buffers (layer % 3) x (E + 1)
-//          lines, one fp64 logit at the start of each line
+//   2304   arrival counters of the logit rounds: 8 lines
+//   3328   the router logits as tagged words: E + 1 u64
 //   then   the layer activation as tagged words: D u32
 //   then   SwiGLU activations h as tagged words: (k + 1) x I u32
-// [128, end of the accumulators) is zeroed before every launch; the tagged
-// words carry the launch counter in their tags instead.
+// [128, 3328) is zeroed before every launch; the tagged words carry the
+// launch counter in their tags instead.
 constexpr size_t kStackAbortOff = 128;
 constexpr size_t kStackXCountOff = 256;
 constexpr size_t kStackHCountOff = 1280;
-constexpr size_t kStackLogitOff = 2304;
-__host__ __device__ constexpr size_t stack_logit_bytes(int E) { return (size_t)3 * (E + 1) * 128; }
+constexpr size_t kStackLCountOff = 2304;
+constexpr size_t kStackLogitOff = 3328;
+__host__ __device__ constexpr size_t stack_logit_bytes(int E) { return ((size_t)(E + 2) * 8 + 127) & ~(size_t)127; }
 __host__ __device__ constexpr size_t stack_xw_off(int E) { return kStackLogitOff + stack_logit_bytes(E); }
 __host__ __device__ constexpr size_t stack_hw_off(int E, int D) { return stack_xw_off(E) + (((size_t)D * 4 + 127) & ~(size_t)127); }
 __host__ __device__ constexpr size_t stack_sync_bytes(int E, int D, int K, int I) {
@@ -81,11 +82,12 @@ __host__ __device__ constexpr size_t stack_sync_bytes(int E, int D, int K, int I
 }
 
 // Phase stamps per layer in the stack kernel's trace ([2][64 layers][slots]).
-constexpr int kTraceSlots = 24;
 #if defined(QMOE_SK_FULLTRACE)
-constexpr int kFullTraceCtas = 160;  // development builds: every CTA's stamps
+constexpr int kTraceSlots = 32;      // development builds: more points,
+constexpr int kFullTraceCtas = 160;  // every CTA's stamps
 constexpr size_t kTraceBytes = (size_t)64 * kFullTraceCtas * kTraceSlots * 8;
 #else
+constexpr int kTraceSlots = 24;
 constexpr size_t kTraceBytes = (size_t)2 * 64 * kTraceSlots * 8;
 #endif
 
@@ -115,6 +117,10 @@ struct RouteArgs {
     float* weights;         // [M][k]
     float* shared_logit;    // [M] or null
     int* status;
+    // Selection: 0 exact top-k (k slots); 1, 2 tie-admitting threshold at the
+    // thr_k-th probability (fp32, bf16 probabilities), the k slots filled from
+    // experts [e_lo, e_hi).
+    int thr_mode, thr_k, e_lo, e_hi;
 };
 
 // Arguments shared by the two expert kernels.
@@ -182,9 +188,10 @@ size_t prefill_workspace_bytes(const qmoe_dims& d, int T);
 // in the workspace.
 const __nv_bfloat16* prefill_act_bf16(const void* x, int x_f32, bool x_ok, int T, const qmoe_dims& d,
                                       unsigned char* ws, cudaStream_t s);
+// thr_mode, thr_k: as RouteArgs (0: exact top-k).
 cudaError_t launch_prefill_route(const __nv_bfloat16* xb, int T, const qmoe_layer_weights& w, const qmoe_dims& d,
                                  unsigned char* ws, int32_t* ids, float* weights, float* shared_logit,
-                                 cudaStream_t s);
+                                 cudaStream_t s, int thr_mode = 0, int thr_k = 0);
 cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t* ids, const float* weights,
                                    const float* shared_logit, const qmoe_layer_weights& w, const qmoe_dims& d,
                                    float* out, unsigned char* ws, cudaStream_t s);

@@ -612,9 +612,12 @@ constexpr int kTopkWarps = 8;
 
 // Top-k per token, warp per token; weights renormalised over the k; the
 // shared-expert logit is the gate-vector row (0 without a gate vector).
+// thr_mode != 0: the tie-admitting threshold select at the thr_k-th
+// probability instead (warp_select_threshold), k slots.
 __global__ void __launch_bounds__(kTopkWarps * 32) pf_topk_kernel(const float* __restrict__ logits, int T, int E,
                                                                   int k, int has_gate, int32_t* ids, float* weights,
-                                                                  float* shared_logit, int* status) {
+                                                                  float* shared_logit, int* status, int thr_mode,
+                                                                  int thr_k) {
     __shared__ float cv[kTopkWarps][kCandCap];
     __shared__ int ci[kTopkWarps][kCandCap];
     __shared__ float sv[kTopkWarps][kMaxTopK];
@@ -623,6 +626,15 @@ __global__ void __launch_bounds__(kTopkWarps * 32) pf_topk_kernel(const float* _
     const int t = blockIdx.x * kTopkWarps + warp;
     if (t >= T) return;
     const float* lg = logits + (size_t)t * (E + 1);
+    if (thr_mode) {
+        const float lmax = warp_select_threshold(lg, E, thr_k, k, 0, E, thr_mode == 2, ids + (size_t)t * k,
+                                                 weights + (size_t)t * k);
+        if (lane == 0) {
+            if (!(fabsf(lmax) <= 3.0e38f)) record_status(status, QMOE_ERR_NOT_FINITE);
+            if (shared_logit) shared_logit[t] = has_gate ? __ldcg(lg + E) : 0.0f;
+        }
+        return;
+    }
     const float lmax = warp_topk(lg, E, k, cv[warp], ci[warp], sv[warp], si[warp]);
     const float e = lane < k ? sv[warp][lane] : 0.0f;
     const float sum = warp_sum(e);
@@ -1099,7 +1111,7 @@ const __nv_bfloat16* prefill_act_bf16(const void* x, int x_f32, bool x_ok, int T
 
 cudaError_t launch_prefill_route(const __nv_bfloat16* xb, int T, const qmoe_layer_weights& w, const qmoe_dims& d,
                                  unsigned char* ws, int32_t* ids, float* weights, float* shared_logit,
-                                 cudaStream_t s) {
+                                 cudaStream_t s, int thr_mode, int thr_k) {
     const PfLayout L = pf_layout(d, T);
     int* status = reinterpret_cast<int*>(ws + L.status);
     const int E = d.n_experts;
@@ -1116,7 +1128,7 @@ cudaError_t launch_prefill_route(const __nv_bfloat16* xb, int T, const qmoe_laye
     }
     pf_topk_kernel<<<(unsigned)((T + kTopkWarps - 1) / kTopkWarps), kTopkWarps * 32, 0, s>>>(
         reinterpret_cast<const float*>(ws + L.logits), T, E, d.top_k, w.gate_vec ? 1 : 0, ids, weights,
-        shared_logit, status);
+        shared_logit, status, thr_mode, thr_k);
     return cudaGetLastError();
 }
 

@@ -4,7 +4,9 @@
 // softmax, top-k, weights divided by their sum.  The global softmax
 // denominator is common to every expert, so ranking and renormalising use the
 // numerators exp(l_i - l_max) alone: w_i = p_i / sum_topk p_j.  Ties go to the lower expert id, the
-// rule of scripts/kernels/router_select.cpp:163-164 (EXACT_TOPK mode).
+// rule of scripts/kernels/router_select.cpp:163-164 (EXACT_TOPK mode).  The
+// same launch also runs that select's tie-admitting threshold mode
+// (router_select.cpp:223-255; warp_select_threshold in topk.cuh).
 //
 // Layout: every warp owns one router row (512 rows + the shared-expert gate
 // vector as row E), reads it once with 128-bit loads and dots it with all M
@@ -88,6 +90,16 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
         const float* lg = a.logits + (size_t)m * (E + 1);
         if (E == 0) {  // gate-vector row only (standalone shared expert)
             if (lane == 0 && a.shared_logit) a.shared_logit[m] = __ldcg(lg);
+            continue;
+        }
+        if (a.thr_mode) {
+            const float lmax = warp_select_threshold(lg, E, a.thr_k, a.k, a.e_lo, a.e_hi, a.thr_mode == 2,
+                                                     a.ids + m * a.k, a.weights + m * a.k);
+            if (lane == 0) {
+                if (!(fabsf(lmax) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
+                if (a.shared_logit) a.shared_logit[m] = a.gate_vec ? __ldcg(lg + E) : 0.0f;
+            }
+            __syncwarp();
             continue;
         }
         const float lmax = warp_topk(lg, E, a.k, s_cv[warp], s_ci[warp], s_sv[warp], s_si[warp]);

@@ -4,46 +4,46 @@
 // may wait on one another), every CTA doing the same work on its own slices.
 // Every layer is the reference's `_moe` (reference/model.py:387-417):
 //
-//   routing  once every CTA has added its share of the layer's router
-//            logits (below) and arrived on the logit counters, every CTA
-//            reads the E + 1 exact sums and ranks them itself (block top-k on
-//            the softmax numerators, ties to the lower id): the same logits
-//            give every CTA the same experts.
-//   B        a CTA then starts all its copies at once: its fixed slice of the
-//            k * I routed (gate row, up row) pairs of the selected experts,
-//            then its rows of their down projections (cp.async.bulk into
-//            shared memory, an mbarrier per chunk, several lanes issuing).
-//            While they stream in it reads the layer input x, converts it to
-//            block floating point and decodes its slice of the shared
-//            expert's pairs (rows prefetched); then the routed pairs as their
-//            chunks land, each pair split over D / 1024 warps (one 32-value
-//            sub-block of each row per lane), two pairs at a time per warp,
-//            decoded from IQ4_XS in registers; SwiGLU; its h values go out as
-//            words and it arrives on the h counters.
-//   C        once the h round is complete, every CTA copies all (k + 1) * I h
-//            words into shared memory with one bulk copy, converts them to
-//            block floating point, starts the next layer's prefetches,
-//            computes its D / 148 output rows of the routed experts'
-//            weighted down projections plus the gated shared expert,
-//            publishes them as the next layer's activation words, adds its
-//            share of the next layer's logits, sum_{j in its rows} R[e][j]
-//            x[j] for every expert e (and the gate vector, row E), into the
-//            fp64 accumulators, and arrives on the logit counters.
+//   A        every CTA gathers the layer input x (the D activation words
+//            that all CTAs published at the end of the last layer),
+//            converts it to block floating point, computes its own few of
+//            the E + 1 router logits (the expert rows and the gate vector
+//            are split over the CTAs, each row a fixed-order fp32 dot
+//            product with x) and publishes them as words; then it gathers
+//            all E + 1 and ranks them itself (block top-k on the softmax
+//            numerators, ties to the lower id): the same logits give every
+//            CTA the same experts.
+//   B        a CTA starts the copies of its fixed slice of the k * I routed
+//            (gate row, up row) pairs of the selected experts (cp.async.bulk
+//            into shared memory, an mbarrier per chunk, several lanes
+//            issuing), decodes its slice of the shared expert's pairs (rows
+//            prefetched), then the routed pairs as their chunks land, each
+//            pair split over D / 1024 warps (one 32-value sub-block of each
+//            row per lane), two pairs at a time per warp, decoded from IQ4_XS
+//            in registers; SwiGLU; its h values go out as words, and it
+//            starts the copies of its rows of the selected experts' down
+//            projections.
+//   C        once every CTA's h is in, a CTA copies all (k + 1) * I h words
+//            into shared memory with one bulk copy, converts them to block
+//            floating point, starts the next layer's prefetches (shared
+//            gate|up rows, its router rows), computes its D / 148 output rows
+//            of the routed experts' weighted down projections plus the gated
+//            shared expert, and publishes them as the next layer's
+//            activation words.
 //
-// A round's counters are 8 words on separate lines: a CTA arrives on word
-// c % 8 with release semantics; a waiter's 8 lanes poll the 8 words, then
-// acquire.  fp32 partials whose magnitudes span less than 2^21 sum exactly in
-// fp64, in any order: the logits do not depend on arrival order, so reruns
-// give the same bits and every rank of a sharded stack selects the same
-// experts.  The accumulators rotate over three buffers (layer % 3): a CTA
-// clears its lines of the buffer two layers on after the h round, when every
-// CTA has read it, and its arrival on the logit counters orders the clearing
-// before anyone adds into it again.  The activation and h words carry tags
-// derived from the layer's stamp, launch_counter * 64 + layer + 1 (the
-// counter lives in the workspace and advances every launch), checked when
-// they are read: activation words are bf16 with a 16-bit tag, h words fp32
+// Every word one CTA publishes for others carries a tag derived from the
+// layer's stamp, launch_counter * 64 + layer + 1 (the counter lives in the
+// workspace and advances every launch): activation words are bf16 with a
+// 16-bit tag, logit words fp32 with the whole stamp beside it, h words fp32
 // with their low 8 mantissa bits replaced by an 8-bit tag (the block floating
-// point they feed keeps 14 bits of the block maximum).
+// point they feed keeps 14 bits of the block maximum).  A reader checks the
+// tags and re-reads what is not yet there, so no fence orders the data: each
+// round (activation, logits, h) also has arrival counters (8 words on
+// separate lines; a CTA adds 1 to word c % 8 after its words, relaxed; a
+// waiter's 8 lanes poll them) that only say when to start reading, so that
+// the CTAs do not poll the data itself.  Each logit is one
+// CTA's fixed-order sum, so reruns give the same bits and every rank of a
+// sharded stack selects the same experts.
 //
 // Sharded over R ranks (one process and one GPU each; the reference's split
 // of every expert's intermediate rows, tt/plan.py:70-103), each rank runs
@@ -57,11 +57,8 @@
 // QMOE_ERR_TIMEOUT and an abort word that every other wait checks; each CTA
 // then waits (bounded) for its own copies in flight and returns.  No trap,
 // no unbounded spin.
-#include <cuda.h>  // CUtensorMap
-
 #include "common.cuh"
 #include "ptx.cuh"
-#include "tma_host.cuh"
 #include "topk.cuh"
 
 namespace qmoe {
@@ -74,8 +71,7 @@ constexpr unsigned long long kTimeoutNs = 200ull * 1000 * 1000;
 constexpr unsigned long long kXchgTimeoutNs = 4000ull * 1000 * 1000;
 constexpr int kSKChunk = 8;      // routed row pairs per gate|up copy chunk
 constexpr int kSKMaxChunks = 6;  // chunks of a worker's pairs (<= 48 pairs)
-constexpr int kRColW = 20;      // router columns per tensor-copy box (80 B): covers 16 from a 16-byte-aligned start
-constexpr int kRBoxRows = 256;  // router rows per tensor-copy box
+constexpr int kSKMaxRRows = 4;   // router rows (logits) per CTA
 
 struct SKLayer {
     const float* router;
@@ -101,7 +97,7 @@ struct SKArgs {
     const __nv_bfloat16* x;  // [D] layer-0 input
     float* out;              // [D] last layer's output
     unsigned char* sync;     // the synchronisation area (common.cuh)
-    unsigned long long* trace;     // phase stamps of worker 0 and the routing CTA, or null
+    unsigned long long* trace;     // phase stamps of CTA 0 and the last CTA, or null
     __nv_bfloat16* act_trace;      // [n_layers][D]: every layer's output rounded to bf16, or null
     int* ids_trace;                // [n_layers][K]: the selected ids in rank order, or null
     float* w_trace;                // [n_layers][K]: their renormalised weights, or null
@@ -109,17 +105,13 @@ struct SKArgs {
     int* status;
     int n_layers;
     SKLayer L[kSKMaxLayers];
-    // Per layer: the router [E][D] and the gate vector [1][D] as 2-D tensors
-    // for TMA copies of a worker's column slice (boxes of kRColW columns).
-    CUtensorMap rmap[kSKMaxLayers];
-    CUtensorMap gmap[kSKMaxLayers];
 };
 
 // Shared-memory carve-up (byte offsets), a function of the shape.
 struct SKLayout {
     int NSQ, NP, NJ, NJR;
-    unsigned xq, xs, rcol, xo, sgu, sdn, gbuf, ubuf, dbuf, hq, hs, gp, up, sgp, sup, dpart, cand, wmax, red, tkv,
-        tki, misc, bars, total;
+    unsigned xq, xs, xstage, rrow, rpart, sgu, sdn, gbuf, ubuf, dbuf, hq, hs, gp, up, sgp, sup, dpart, cand,
+        wmax, red, lf, tkv, tki, misc, bars, total;
 };
 
 __host__ __device__ constexpr unsigned sk_take(unsigned& o, unsigned bytes) {
@@ -151,8 +143,9 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     unsigned o = 0;
     s.xq = sk_take(o, NSB * 64);
     s.xs = sk_take(o, NSB * 4);
-    s.rcol = sk_take(o, (unsigned)(((E + kRBoxRows - 1) / kRBoxRows) * kRBoxRows + 1) * kRColW * 4);
-    s.xo = sk_take(o, (unsigned)(s.NJ > kRColW ? s.NJ : kRColW) * 4);  // the router-column window's x
+    s.xstage = sk_take(o, (unsigned)D * 4);                   // the activation words
+    s.rrow = sk_take(o, (unsigned)kSKMaxRRows * D * 4);       // this CTA's router rows
+    s.rpart = sk_take(o, (unsigned)kSKWarps * kSKMaxRRows * 4);
     s.sgu = sk_take(o, 2u * s.NSQ * RB);
     s.sdn = sk_take(o, (unsigned)s.NJR * DRB);
     s.gbuf = sk_take(o, (unsigned)s.NP * RB);
@@ -165,9 +158,10 @@ __host__ __device__ constexpr SKLayout sk_layout(int D, int I, int E, int K, int
     s.sgp = sk_take(o, s.NSQ * SPL * 4);
     s.sup = sk_take(o, s.NSQ * SPL * 4);
     s.dpart = sk_take(o, kSKWarps * 16 * 4);
-    s.cand = sk_take(o, 256 * 8);
-    s.wmax = sk_take(o, (kSKWarps + 1) * 8);
+    s.cand = sk_take(o, kCandCap * 8);  // the top-k's candidates
+    s.wmax = sk_take(o, kSKWarps * 8);
     s.red = sk_take(o, kSKWarps * 4);
+    s.lf = sk_take(o, (unsigned)E * 4);  // the logits
     s.tkv = sk_take(o, kMaxTopK * 4);
     s.tki = sk_take(o, kMaxTopK * 4);
     s.misc = sk_take(o, 64);
@@ -187,13 +181,14 @@ struct SKShape {
     static constexpr int DRB = sk_down_row_bytes(I_);
     static constexpr bool kPairRows = DRB % 16 != 0;
     static constexpr SKLayout S = sk_layout(D_, I_, E_, K_, NW);
-    static_assert(E_ <= kSKThreads && E_ % 32 == 0, "one logit per thread");
+    static_assert(E_ <= kSKThreads && E_ % 32 == 0 && E_ >= kSKWarps, "one logit per thread");
     static_assert(I_ % 32 == 0 && I_ <= 512 && (I_ >= 256 ? I_ % 256 == 0 : 256 % I_ == 0), "intermediate slice");
-    static_assert(K_ <= kMaxTopK && 2 * K_ < 32, "routing record: one word per lane");
+    static_assert(K_ <= kMaxTopK && K_ <= kSKWarps && 2 * K_ < 32, "top-k");
     static_assert(K_ * I_ / NW + 1 <= I_, "a worker's routed rows span at most two experts");
     static_assert((K_ * I_ + NW - 1) / NW <= kSKChunk * kSKMaxChunks, "chunks of a worker's pairs");
     static_assert((D_ + NW - 1) / NW <= 16, "a lane per output row in the down phase");
-    static_assert((D_ + NW - 1) / NW + 3 <= kRColW, "router column slice: one box per worker");
+    static_assert((E_ + 1 + NW - 1) / NW <= kSKMaxRRows, "router rows per CTA");
+    static_assert(D_ % kSKThreads == 0 && D_ / kSKThreads <= 4, "router dot: columns per thread");
     static_assert(D_ % 1024 == 0 && kSKWarps % (D_ / 1024) == 0, "gate|up column splits");
     static_assert((K_ * I_ + NW - 1) / NW <= kSKThreads, "h writers");
     static_assert(D_ % 2 == 0, "down rows copied in pairs");
@@ -213,15 +208,25 @@ __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ double ld_relaxed_f64(const double* p) {
-    double v;
-    asm volatile("ld.relaxed.gpu.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint4 ld_relaxed_v4(const unsigned* p) {
+    uint4 v;
+    asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 __device__ __forceinline__ void st_relaxed_u32(unsigned* p, unsigned v) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 // Bounded wait for the phase of `bar` with parity `par`; false on timeout.
 __device__ bool mbar_wait(uint64_t* bar, uint32_t par) {
@@ -233,13 +238,15 @@ __device__ bool mbar_wait(uint64_t* bar, uint32_t par) {
     return true;
 }
 
-// Phase trace: thread `rec` (0 unless stated) of worker 0 and of the routing
-// CTA stamp their SM's cycle counter (clock64) at each phase boundary.
+// Phase trace: thread `rec` (0 unless stated) of CTA 0 and of the last CTA
+// stamp their SM's cycle counter (clock64) at each phase boundary.
 __device__ __forceinline__ void trace_mark(const SKArgs& a, int L, int k, int rec = 0) {
 #if defined(QMOE_SK_FULLTRACE)
-    // development builds: every CTA, on the GPU-wide clock (ns)
+    // development builds: every CTA; slot 13 holds the GPU-wide clock (ns)
+    // taken with slot 0, to place the CTAs' cycle counts on one time line
     if (a.trace && (int)threadIdx.x == rec)
-        a.trace[((size_t)L * kFullTraceCtas + blockIdx.x) * kTraceSlots + k] = now_ns();
+        a.trace[((size_t)L * kFullTraceCtas + blockIdx.x) * kTraceSlots + k] =
+            k == 13 ? now_ns() : (unsigned long long)clock64();
 #else
     if (a.trace && (int)threadIdx.x == rec) {
         if (blockIdx.x == 0) a.trace[L * kTraceSlots + k] = (unsigned long long)clock64();
@@ -248,14 +255,23 @@ __device__ __forceinline__ void trace_mark(const SKArgs& a, int L, int k, int re
 #endif
 }
 
+// Development-build stamps (slots the product build leaves to the exchange
+// or unused).
+__device__ __forceinline__ void dev_mark(const SKArgs& a, int L, int k, int rec = 0) {
+#if defined(QMOE_SK_FULLTRACE)
+    trace_mark(a, L, k, rec);
+#endif
+}
+
 // The sync area as the kernel sees it.
 struct SKSync {
     unsigned* abortw;
-    unsigned* xcnt;              // logit-round counters: 8 words, 32 apart
-    unsigned* hcnt;              // h-round counters
-    double* logits;              // [3 buffers][E + 1 lines][16 doubles]: logit i at the start of line i
-    unsigned* xw;                // the activation words [D]
-    unsigned* hw;                // the h words [(K + 1) I]
+    unsigned* xcnt;           // activation-round counters: 8 words, 32 apart
+    unsigned* hcnt;           // h-round counters
+    unsigned* lcnt;           // logit-round counters
+    unsigned long long* lw;   // the logit words [E + 1]: fp32 bits | stamp << 32
+    unsigned* xw;             // the activation words [D]
+    unsigned* hw;             // the h words [(K + 1) I]
 };
 
 __device__ __forceinline__ void sk_fail(const SKSync& s, int* status) {
@@ -285,24 +301,20 @@ __device__ __forceinline__ bool poll_warp(More more, const SKSync& s, int* statu
     }
 }
 
-// Arrival of worker c on a round's counters (one thread; every earlier write
-// of the CTA ordered before it by the caller's barrier and the release).
+// Arrival of worker c on a round's counters (one thread, after the CTA's
+// words of the round: a hint for when to read them, the tags decide).
 __device__ __forceinline__ void arrive(unsigned* cnt, int c) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt + 32 * (c & 7)) : "memory");
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(cnt + 32 * (c & 7)) : "memory");
 }
 
 // One warp waits until round r (1-based) of nw workers is complete on the 8
-// counters (lane i < 8 polls word i, whose workers number (nw - i + 7) / 8),
-// then acquires.  Bounded; false on a timeout or an abort.
+// counters (lane i < 8 polls word i, whose workers number (nw - i + 7) / 8).
+// Bounded; false on a timeout or an abort.
 __device__ bool wait_round(const unsigned* cnt, unsigned r, int nw, const SKSync& s, int* status) {
     const int lane = threadIdx.x & 31;
     const unsigned target = lane < 8 && lane < nw ? r * (unsigned)((nw - lane + 7) / 8) : 0u;
     const unsigned* w = cnt + 32 * (lane & 7);
-    const bool got = poll_warp(
-        [&]() { return lane < 8 && (int)(ld_relaxed_u32(w) - target) < 0; }, s, status);
-    fence_acq_rel_gpu();
-    __syncwarp();
-    return got;
+    return poll_warp([&]() { return lane < 8 && (int)(ld_relaxed_u32(w) - target) < 0; }, s, status);
 }
 
 // ---- the decode core --------------------------------------------------------
@@ -381,6 +393,7 @@ struct SKPart {
     size_t GUE, DNE;
     int sq_lo, sq_hi, p_lo, p_hi, j_lo, j_hi;
     int jc_lo, jc_hi;  // down rows copied: [j_lo, j_hi), widened to even bounds for rows of 8 mod 16 bytes
+    int e_lo, e_hi;    // router logits [e_lo, e_hi) of the E + 1 (row E: the gate vector)
 };
 
 template <class SH>
@@ -406,6 +419,8 @@ __device__ __forceinline__ SKPart sk_part() {
     p.j_hi = (c + 1) * SH::D / n;
     p.jc_lo = SH::kPairRows ? p.j_lo & ~1 : p.j_lo;
     p.jc_hi = SH::kPairRows ? (p.j_hi + 1) & ~1 : p.j_hi;
+    p.e_lo = c * (SH::E + 1) / n;
+    p.e_hi = (c + 1) * (SH::E + 1) / n;
     return p;
 }
 
@@ -430,57 +445,15 @@ __device__ __forceinline__ void issue_sdn(const SKLayer& W, const SKPart& p, con
     if (nc > 0) ptx::bulk_g2s(sm + S.sdn, W.sh_down + (size_t)p.jc_lo * p.DRB, (uint32_t)(nc * p.DRB), bar);
 }
 
-// Router columns of this worker's output rows, for every router row and the
-// gate vector (row E), as 2-D tensor copies (one thread): boxes of kRColW
-// columns from j_lo rounded down to a 16-byte boundary, kRBoxRows rows each;
-// rcol row e at e * kRColW floats, the gate vector after the last box.
-__device__ __forceinline__ void issue_rcol(const CUtensorMap* rmap, const CUtensorMap* gmap, const SKPart& p,
-                                           const SKLayout& S, unsigned char* sm, uint64_t* bar) {
-    float* rcol = reinterpret_cast<float*>(sm + S.rcol);
-    const int nbox = (p.E + kRBoxRows - 1) / kRBoxRows, rows = p.E < kRBoxRows ? p.E : kRBoxRows;
-    const int x = p.j_lo & ~3;
-    mbar_expect_tx(bar, (uint32_t)((nbox * rows + 1) * kRColW * 4));
-    for (int b = 0; b < nbox; ++b) ptx::tma_load_2d(rcol + b * rows * kRColW, rmap, x, b * rows, bar);
-    ptx::tma_load_2d(rcol + nbox * kRBoxRows * kRColW, gmap, x, 0, bar);
-}
-
-// Row r of the router-column window (kRColW floats from column j_lo & ~3)
-// dotted with x over the same window: 16-byte loads (the 8 rows a quarter
-// warp reads, 80 bytes apart, fall in 8 distinct bank groups).  The window's
-// columns outside this worker's rows hold x = 0 and add exact zeros, so the
-// sum runs over its columns in order, as a plain loop over them would
-// (router weights are finite).
-__device__ __forceinline__ float rcol_dot(const float* row, const float4* x4) {
-    const float4* r4 = reinterpret_cast<const float4*>(row);
-    float v = 0.0f;
-#pragma unroll
-    for (int q = 0; q < kRColW / 4; ++q) {
-        const float4 r = r4[q], x = x4[q];
-        v = fmaf(r.x, x.x, v);
-        v = fmaf(r.y, x.y, v);
-        v = fmaf(r.z, x.z, v);
-        v = fmaf(r.w, x.w, v);
-    }
-    return v;
-}
-
-// This worker's share of the router logits: thread e (and thread 0 for the
-// gate row E) sums rcol[e][j] * x[j] over its columns j in fp32 and adds it to
-// logit e's fp64 accumulator, one per 128-byte line.
-__device__ __forceinline__ void router_partial(const SKPart& p, const SKLayout& S, const unsigned char* sm,
-                                               double* acc) {
-    const float4* x4 = reinterpret_cast<const float4*>(sm + S.xo);
-    const float* rcol = reinterpret_cast<const float*>(sm + S.rcol);
-    const int e = threadIdx.x;
-    const int gate_row = ((p.E + kRBoxRows - 1) / kRBoxRows) * kRBoxRows;
-    if (e < p.E) {
-        const float v = rcol_dot(rcol + e * kRColW, x4);
-        asm volatile("red.global.add.f64 [%0], %1;" ::"l"(acc + (size_t)e * 16), "d"((double)v) : "memory");
-    }
-    if (e == 0) {
-        const float g = rcol_dot(rcol + gate_row * kRColW, x4);
-        asm volatile("red.global.add.f64 [%0], %1;" ::"l"(acc + (size_t)p.E * 16), "d"((double)g) : "memory");
-    }
+// This CTA's router rows of a layer (one thread): rows [e_lo, e_hi) of the
+// router, the gate vector in place of row E.
+__device__ __forceinline__ void issue_rrow(const SKLayer& W, const SKPart& p, const SKLayout& S, unsigned char* sm,
+                                           uint64_t* bar) {
+    const int ne = p.e_hi - p.e_lo, nr = min(p.e_hi, p.E) - p.e_lo;
+    float* rrow = reinterpret_cast<float*>(sm + S.rrow);
+    mbar_expect_tx(bar, (uint32_t)(ne * p.D * 4));
+    if (nr > 0) ptx::bulk_g2s(rrow, W.router + (size_t)p.e_lo * p.D, (uint32_t)(nr * p.D * 4), bar);
+    if (p.e_hi > p.E) ptx::bulk_g2s(rrow + (size_t)(p.E - p.e_lo) * p.D, W.gate_vec, (uint32_t)(p.D * 4), bar);
 }
 
 // This worker's routed pairs [p_lo, p_hi) fall in at most two expert slots: the
@@ -532,22 +505,17 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     constexpr int D = SH::D, I = SH::I, E = SH::E, K = SH::K, NW = SH::NW;
     constexpr int NSB = D / 32, NSBH = I / 32, NH = (K + 1) * I, NHB = NH / 32;
     constexpr int SPL = sk_splits(D), NSTREAM = kSKWarps / SPL;
-    constexpr size_t G = (size_t)(E + 1) * 16;  // doubles per logit buffer
     static_assert(NH * 4 <= (int)(S.ubuf - S.gbuf) + S.NP * (D / 256) * 136, "h words staged in the gate|up buffers");
-    static_assert(D * 4 <= (((E + kRBoxRows - 1) / kRBoxRows) * kRBoxRows + 1) * kRColW * 4,
-                  "activation words staged in the router-column buffer");
 
     const SKPart p = sk_part<SH>();
-    const int nsq = p.sq_hi - p.sq_lo, np = p.p_hi - p.p_lo, nj = p.j_hi - p.j_lo;
+    const int nsq = p.sq_hi - p.sq_lo, np = p.p_hi - p.p_lo, nj = p.j_hi - p.j_lo, ne = p.e_hi - p.e_lo;
     const int nch = (np + kSKChunk - 1) / kSKChunk;
     const int c = blockIdx.x;
     int* xq = reinterpret_cast<int*>(sm + S.xq);
     float* xs = reinterpret_cast<float*>(sm + S.xs);
-    // xo: x over the router-column window [j_lo & ~3, +kRColW); row j of this
-    // CTA's slice at xo[xwin + j], the rest zero
-    float* xo = reinterpret_cast<float*>(sm + S.xo);
-    const int xwin = p.j_lo & 3;
-    unsigned* xstage = reinterpret_cast<unsigned*>(sm + S.rcol);  // the activation words, between uses of rcol
+    unsigned* xstage = reinterpret_cast<unsigned*>(sm + S.xstage);
+    const float* rrow = reinterpret_cast<const float*>(sm + S.rrow);
+    float* rpart = reinterpret_cast<float*>(sm + S.rpart);
     unsigned* hstage = reinterpret_cast<unsigned*>(sm + S.gbuf);  // the h words, once the gate|up rows are used
     const uint8_t* sgu = sm + S.sgu;
     const uint8_t* sdn = sm + S.sdn;
@@ -564,16 +532,18 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(sm + S.cand);
     unsigned long long* wmax = reinterpret_cast<unsigned long long*>(sm + S.wmax);
     unsigned* red = reinterpret_cast<unsigned*>(sm + S.red);
+    float* lf = reinterpret_cast<float*>(sm + S.lf);
+    int* s_cnt = reinterpret_cast<int*>(sm + S.misc) + 8;
     float* tkv = reinterpret_cast<float*>(sm + S.tkv);
     int* tki = reinterpret_cast<int*>(sm + S.tki);
-    // s_misc: [0] ok flag, [1] launch counter, [2] exchange counter, [8] top-k count; float [12] the gate
+    // s_misc: [0] ok flag, [1] launch counter, [2] exchange counter, [3] down
+    // copies issued (by the last warp), [8] top-k candidates; float [12] the gate
     unsigned* s_misc = reinterpret_cast<unsigned*>(sm + S.misc);
-    int* s_cnt = reinterpret_cast<int*>(sm + S.misc) + 8;
     float* s_gate = reinterpret_cast<float*>(sm + S.misc) + 12;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S.bars);
     uint64_t* bar_sgu = bars;
     uint64_t* bar_sdn = bars + 1;
-    uint64_t* bar_rc = bars + 2;
+    uint64_t* bar_rr = bars + 2;
     uint64_t* bar_dn = bars + 3;
     uint64_t* bar_h = bars + 4;
     uint64_t* bar_ch = bars + 5;
@@ -584,7 +554,8 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
     sy.abortw = reinterpret_cast<unsigned*>(a.sync + kStackAbortOff);
     sy.xcnt = reinterpret_cast<unsigned*>(a.sync + kStackXCountOff);
     sy.hcnt = reinterpret_cast<unsigned*>(a.sync + kStackHCountOff);
-    sy.logits = reinterpret_cast<double*>(a.sync + kStackLogitOff);
+    sy.lcnt = reinterpret_cast<unsigned*>(a.sync + kStackLCountOff);
+    sy.lw = reinterpret_cast<unsigned long long*>(a.sync + kStackLogitOff);
     sy.xw = reinterpret_cast<unsigned*>(a.sync + stack_xw_off(E));
     sy.hw = reinterpret_cast<unsigned*>(a.sync + stack_hw_off(E, D));
 
@@ -593,33 +564,20 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
         ptx::fence_mbar_init();
         s_misc[1] = ld_relaxed_u32(reinterpret_cast<const unsigned*>(a.sync));
         s_misc[2] = XC ? __ldcg(a.xepoch) : 0u;
+        s_misc[3] = 0u;
     }
     __syncthreads();
     const unsigned lc = s_misc[1];      // this launch's counter (tags)
     const unsigned xepoch = s_misc[2];  // exchange launch counter (peer flags)
     auto stamp_of = [&](int L) { return lc * 64u + (unsigned)L + 1u; };
     // Phases issued (kept by thread 0 in registers), for the bounded drain.
-    int iss_sgu = 0, iss_rc = 0, iss_sdn = 0, iss_routed = 0, iss_h = 0;
+    int iss_sgu = 0, iss_rr = 0, iss_sdn = 0, iss_gu = 0, iss_h = 0;
     bool ok = true;
     if (tid == 0) {
-        issue_rcol(&a.rmap[0], &a.gmap[0], p, S, sm, bar_rc);
+        issue_rrow(a.L[0], p, S, sm, bar_rr);
         issue_sgu(a.L[0], p, S, sm, bar_sgu);
         issue_sdn(a.L[0], p, S, sm, bar_sdn);
-        iss_sgu = iss_rc = iss_sdn = 1;
-    }
-
-    // ---------------- prologue: layer 0's router logits --------------------
-    if (tid < kRColW) {
-        const int j = tid - xwin;
-        const __nv_bfloat16* x0 = a.teacher ? a.teacher : a.x;
-        xo[tid] = j >= 0 && j < nj ? __bfloat162float(x0[p.j_lo + j]) : 0.0f;
-    }
-    ok = !__syncthreads_or(!mbar_wait(bar_rc, 0));
-    if (!ok && tid == 0) sk_fail(sy, a.status);
-    if (ok) {
-        router_partial(p, S, sm, sy.logits);
-        __syncthreads();
-        if (tid == 0) arrive(sy.xcnt, c);
+        iss_sgu = iss_rr = iss_sdn = 1;
     }
 
     for (int L = 0; L < a.n_layers && ok; ++L) {
@@ -627,70 +585,33 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
         const uint32_t par = (uint32_t)(L & 1);
         const bool last = L + 1 == a.n_layers;
         const unsigned stamp = stamp_of(L);
-        double* lg = sy.logits + (size_t)(L % 3) * G;
+        const unsigned t16 = stamp & 0xFFFFu;
         trace_mark(a, L, 0);
+        dev_mark(a, L, 13);
 
-        // ---- routing: every CTA's logit partials of the layer are in ---------
-        if (warp == 0) {
-            const bool got = wait_round(sy.xcnt, (unsigned)(L + 1), NW, sy, a.status);
-            if (lane == 0) s_misc[0] = got ? 1u : 0u;
-        }
-        __syncthreads();
-        if (!s_misc[0]) {
-            ok = false;
-            break;
-        }
-        trace_mark(a, L, 1);
-        {
-            // logit i: the fp64 word at the start of line i
-            auto logit_at = [&](int i) { return (float)ld_relaxed_f64(lg + (size_t)i * 16); };
-            if (tid == 0) *s_gate = logit_at(E);
-            const float lmax = block_topk_threshold(logit_at, E, K, cand, wmax, red, s_cnt, tkv, tki, []() {});
+        // ---- A: x_L, this CTA's logits, all logits, the experts -------------
+        if (L > 0 && !a.teacher) {
+            // every CTA's output rows of the last layer: the counters say when
+            // to read, the tags check what was read
             if (warp == 0) {
-                float ps = 0.0f;
-                for (int i = 0; i < K; ++i) ps += tkv[i];
-                const float inv = 1.0f / ps;
-                __syncwarp();
-                if (lane < K) tkv[lane] = tkv[lane] * inv;
-                if (lane == 0) {
-                    *s_gate = sigmoid(*s_gate);
-                    if (!(fabsf(lmax) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
-                }
-                __syncwarp();
-                if (a.ids_trace && c == 0 && lane < K) {
-                    a.ids_trace[L * K + lane] = tki[lane];
-                    a.w_trace[L * K + lane] = tkv[lane];
-                }
-                // all of this CTA's copies at once: the gate|up chunks (lane
-                // c: chunk c), then the down rows (lanes 0..k-1)
-                ptx::fence_proxy_async();  // every issuing lane
-                if (lane < nch) issue_chunk(W, p, S, sm, tki, lane, bar_ch + lane);
-                issue_down(W, p, S, sm, tki, bar_dn, lane);
-                if (lane == 0) ++iss_routed;
-            }
-        }
-        __syncthreads();
-        trace_mark(a, L, 2);
-
-        // ---- x_L: block floating point (xq, xs) ------------------------------
-        // (complete: every CTA wrote its rows before arriving on the logit
-        // counters this CTA acquired)
-        {
-            const unsigned t16 = stamp & 0xFFFFu;
-            if (L > 0 && !a.teacher) {
-                for (int i = tid * 4; i < D; i += kSKThreads * 4) {
-                    uint4 v;
-                    asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                                 : "l"(sy.xw + i)
-                                 : "memory");
-                    *reinterpret_cast<uint4*>(xstage + i) = v;
-                }
-            } else {
-                const __nv_bfloat16* src = a.teacher ? a.teacher + (size_t)L * D : a.x;
-                for (int i = tid; i < D; i += kSKThreads) xstage[i] = (t16 << 16) | __bfloat16_as_ushort(src[i]);
+                const bool got = wait_round(sy.xcnt, (unsigned)L, NW, sy, a.status);
+                if (lane == 0) s_misc[0] = got ? 1u : 0u;
             }
             __syncthreads();
+            if (!s_misc[0]) {
+                ok = false;
+                break;
+            }
+            for (int i = tid * 4; i < D; i += kSKThreads * 4)
+                *reinterpret_cast<uint4*>(xstage + i) = ld_relaxed_v4(sy.xw + i);
+        } else {
+            const __nv_bfloat16* src = a.teacher ? a.teacher + (size_t)L * D : a.x;
+            for (int i = tid; i < D; i += kSKThreads) xstage[i] = (t16 << 16) | __bfloat16_as_ushort(src[i]);
+        }
+        __syncthreads();
+        trace_mark(a, L, 1);
+        {
+            // the tags: bounded re-reads of what is missing, written back
             constexpr int XPW = (NSB + kSKWarps - 1) / kSKWarps;
             unsigned xv[XPW];
 #pragma unroll
@@ -698,8 +619,8 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 const int b = warp + i * kSKWarps;
                 xv[i] = b < NSB ? xstage[b * 32 + lane] : (t16 << 16);
             }
-            // the tags check what the counters guarantee (bounded, normally no round)
-            const bool got = poll_warp(
+            bool miss_any = false;
+            bool got = poll_warp(
                 [&]() {
                     bool miss = false;
 #pragma unroll
@@ -710,28 +631,263 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                             miss = true;
                         }
                     }
+                    miss_any = miss_any || miss;
                     return miss;
                 },
                 sy, a.status);
-            if (got) {
+            if (__any_sync(0xffffffffu, miss_any)) {
 #pragma unroll
                 for (int i = 0; i < XPW; ++i) {
                     const int b = warp + i * kSKWarps;
-                    if (b < NSB) {
-                        float st;
-                        const int pw =
-                            warp_block_fp(__bfloat162float(__ushort_as_bfloat16((unsigned short)xv[i])), &st);
-                        if (lane < 16) xq[b * 16 + lane] = pw;
-                        if (lane == 0) xs[b] = st;
-                    }
+                    if (b < NSB) xstage[b * 32 + lane] = xv[i];
                 }
             }
+            const bool rr_ok = mbar_wait(bar_rr, par);
+            if (!rr_ok && tid == 0) sk_fail(sy, a.status);
+            if (__syncthreads_or(!got || !rr_ok)) {
+                ok = false;
+                break;
+            }
+        }
+        trace_mark(a, L, 2);
+        {
+            // this CTA's logits: each a fixed-order fp32 dot product (a
+            // thread's CPT columns in order, the warp's lanes by a butterfly,
+            // the warps in order), published as words
+            constexpr int CPT = D / kSKThreads;
+            float xf[CPT];
+#pragma unroll
+            for (int j = 0; j < CPT; ++j)
+                xf[j] = __bfloat162float(__ushort_as_bfloat16((unsigned short)xstage[tid * CPT + j]));
+            float acc[kSKMaxRRows];
+#pragma unroll
+            for (int r = 0; r < kSKMaxRRows; ++r) {
+                acc[r] = 0.0f;
+                if (r < ne) {
+#pragma unroll
+                    for (int j = 0; j < CPT; ++j) acc[r] = fmaf(rrow[(size_t)r * D + tid * CPT + j], xf[j], acc[r]);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int r = 0; r < kSKMaxRRows; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+            }
+            if (lane < kSKMaxRRows) {
+                float mine = acc[0];
+#pragma unroll
+                for (int r = 1; r < kSKMaxRRows; ++r) mine = lane == r ? acc[r] : mine;
+                rpart[warp * kSKMaxRRows + lane] = mine;
+            }
+            __syncthreads();
+            if (warp == 0) {
+                if (lane < ne) {
+                    float v = 0.0f;
+                    for (int w = 0; w < kSKWarps; ++w) v += rpart[w * kSKMaxRRows + lane];
+                    st_relaxed_u64(sy.lw + p.e_lo + lane, ((unsigned long long)stamp << 32) | __float_as_uint(v));
+                }
+                __syncwarp();
+                if (lane == 0) arrive(sy.lcnt, c);
+            }
+        }
+        dev_mark(a, L, 22);
+        // Every logit once the round is counted in (thread t: logit t, thread
+        // 0 also the gate's; tags checked), into lf[] with each warp's
+        // largest in red[].
+        if (warp == 0) {
+            const bool got = wait_round(sy.lcnt, (unsigned)(L + 1), NW, sy, a.status);
+            if (lane == 0) s_misc[0] = got ? 1u : 0u;
+        }
+        __syncthreads();
+        if (!s_misc[0]) {
+            ok = false;
+            break;
+        }
+        {
+            unsigned long long w = 0ull, wg = 0ull;
+            bool have = tid >= E, hg = tid != 0;
+            const bool got = poll_warp(
+                [&]() {
+                    if (!have) w = ld_relaxed_u64(sy.lw + tid);
+                    if (!hg) wg = ld_relaxed_u64(sy.lw + E);
+                    have = have || (unsigned)(w >> 32) == stamp;
+                    hg = hg || (unsigned)(wg >> 32) == stamp;
+                    return !have || !hg;
+                },
+                sy, a.status);
+            float l = -INFINITY;
+            if (tid < E) {
+                l = __uint_as_float((unsigned)w);
+                if (l != l) l = -INFINITY;  // NaN ranks last
+                lf[tid] = l;
+            }
+            if (tid == 0) {
+                *s_gate = __uint_as_float((unsigned)wg);
+                *s_cnt = 0;
+            }
+            const unsigned m = __reduce_max_sync(0xffffffffu, topk_ord(l));
+            if (lane == 0) red[warp] = m;
             if (__syncthreads_or(!got)) {
                 ok = false;
                 break;
             }
         }
-        trace_mark(a, L, 3);
+        dev_mark(a, L, 23);
+        // Top-k on keys (p bits << 32 | ~id), p = exp(l - l_max): thread
+        // (warp w, lane l) takes id l * 16 + w, so every warp sees ids spread
+        // over the whole range; t0 = the k-th largest of the 16 warp maxima
+        // (k distinct keys reach it, so every member of the top k does); the
+        // keys >= t0 are the candidates, about k even when all tie.
+        float lmax;
+        int n_cand;
+        unsigned long long key;
+        {
+            const unsigned mm = __reduce_max_sync(0xffffffffu, lane < kSKWarps ? red[lane] : 0u);
+            lmax = __uint_as_float((mm & 0x80000000u) ? (mm & 0x7FFFFFFFu) : ~mm);
+            const int e = lane * kSKWarps + warp;
+            key = e < E ? ((unsigned long long)__float_as_uint(expf(lf[e] - lmax)) << 32) | (0xFFFFFFFFu - (unsigned)e)
+                        : 0ull;
+            const unsigned kh = (unsigned)(key >> 32), kl = (unsigned)key;
+            const unsigned mh = __reduce_max_sync(0xffffffffu, kh);
+            const unsigned ml = __reduce_max_sync(0xffffffffu, kh == mh ? kl : 0u);
+            if (lane == 0) wmax[warp] = ((unsigned long long)mh << 32) | ml;
+            __syncthreads();
+            const unsigned long long wv = lane < kSKWarps ? wmax[lane] : 0ull;
+            int gt = 0;
+#pragma unroll
+            for (int j = 0; j < kSKWarps; ++j) gt += __shfl_sync(0xffffffffu, wv, j) > wv ? 1 : 0;
+            const unsigned sel = __ballot_sync(0xffffffffu, lane < kSKWarps && gt == K - 1);
+            const unsigned long long t0 = __shfl_sync(0xffffffffu, wv, __ffs(sel) - 1);
+            const bool is_c = e < E && key >= t0;
+            const unsigned bal = __ballot_sync(0xffffffffu, is_c);
+            int base = 0;
+            if (lane == 0 && bal) base = atomicAdd(s_cnt, __popc(bal));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            const int pos = base + __popc(bal & ((1u << lane) - 1u));
+            if (is_c && pos < kCandCap) cand[pos] = key;
+            __syncthreads();
+            n_cand = *s_cnt;
+            if (n_cand > 32) {
+                // adversarial ties: the whole CTA ranks (up to kCandCap
+                // candidates), or k rounds of block arg-max
+                if (n_cand <= kCandCap) {
+                    for (int i = tid; i < n_cand; i += kSKThreads) {
+                        const unsigned long long ci = cand[i];
+                        int rr = 0;
+                        for (int j = 0; j < n_cand; ++j) rr += cand[j] > ci ? 1 : 0;
+                        if (rr < K) {
+                            tkv[rr] = __uint_as_float((unsigned)(ci >> 32));
+                            tki[rr] = (int)(0xFFFFFFFFu - (unsigned)ci);
+                        }
+                    }
+                    __syncthreads();
+                } else {
+                    unsigned long long mine = key;
+                    for (int rd = 0; rd < K; ++rd) {
+                        const unsigned h = (unsigned)(mine >> 32), lo = (unsigned)mine;
+                        const unsigned wh = __reduce_max_sync(0xffffffffu, h);
+                        const unsigned wl = __reduce_max_sync(0xffffffffu, h == wh ? lo : 0u);
+                        if (lane == 0) cand[warp] = ((unsigned long long)wh << 32) | wl;
+                        __syncthreads();
+                        unsigned long long best = 0ull;
+                        for (int w2 = 0; w2 < kSKWarps; ++w2) best = cand[w2] > best ? cand[w2] : best;
+                        if (tid == 0) {
+                            tkv[rd] = __uint_as_float((unsigned)(best >> 32));
+                            tki[rd] = (int)(0xFFFFFFFFu - (unsigned)best);
+                        }
+                        if (mine == best) mine = 0ull;
+                        __syncthreads();
+                    }
+                }
+            }
+        }
+        if (tid == 0 && !(fabsf(lmax) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
+        // Warp 0: the ranking of up to 32 candidates, this CTA's gate|up
+        // copies, the weights.  Warps 1..: x to block floating point, then the
+        // shared expert's pairs.
+        bool a_ok = true;
+        if (warp == 0) {
+            if (n_cand <= 32) {
+                const unsigned long long ci = lane < n_cand ? cand[lane] : 0ull;
+                int rr = 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const unsigned long long o = __shfl_sync(0xffffffffu, ci, j);
+                    rr += (j < n_cand && o > ci) ? 1 : 0;
+                }
+                if (lane < n_cand && rr < K) {
+                    tkv[rr] = __uint_as_float((unsigned)(ci >> 32));
+                    tki[rr] = (int)(0xFFFFFFFFu - (unsigned)ci);
+                }
+                __syncwarp();
+            }
+            dev_mark(a, L, 15);
+            ptx::fence_proxy_async();  // every issuing lane
+            if (lane < nch) issue_chunk(W, p, S, sm, tki, lane, bar_ch + lane);
+            if (lane == 0) ++iss_gu;
+            trace_mark(a, L, 3);
+            float ps = 0.0f;
+            for (int i = 0; i < K; ++i) ps += tkv[i];
+            const float inv = 1.0f / ps;
+            __syncwarp();
+            if (lane < K) tkv[lane] = tkv[lane] * inv;
+            if (lane == 0) *s_gate = sigmoid(*s_gate);
+            __syncwarp();
+            if (a.ids_trace && c == 0 && lane < K) {
+                a.ids_trace[L * K + lane] = tki[lane];
+                a.w_trace[L * K + lane] = tkv[lane];
+            }
+            dev_mark(a, L, 24);
+        } else {
+            constexpr int XW = kSKWarps - 1, XPW = (NSB + XW - 1) / XW;
+#pragma unroll
+            for (int i = 0; i < XPW; ++i) {
+                const int b = warp - 1 + i * XW;
+                if (b < NSB) {
+                    float st;
+                    const int pw =
+                        warp_block_fp(__bfloat162float(__ushort_as_bfloat16((unsigned short)xstage[b * 32 + lane])), &st);
+                    if (lane < 16) xq[b * 16 + lane] = pw;
+                    if (lane == 0) xs[b] = st;
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(XW * 32) : "memory");
+            dev_mark(a, L, 14, 32);
+            // the shared expert's pairs (rows prefetched), on the streams
+            // without warp 0
+            const int hf = warp % SPL, stream = warp / SPL, sb = hf * 32 + lane;
+            if (stream > 0) {
+                int xr[16];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int4 w4 = reinterpret_cast<const int4*>(xq + sb * 16)[q];
+                    xr[4 * q] = w4.x;
+                    xr[4 * q + 1] = w4.y;
+                    xr[4 * q + 2] = w4.z;
+                    xr[4 * q + 3] = w4.w;
+                }
+                const float xst = xs[sb];
+                if (!mbar_wait(bar_sgu, par)) {
+                    a_ok = false;
+                } else {
+                    for (int t = stream - 1; t < nsq; t += NSTREAM - 1) {
+                        float g, u;
+                        pair_dot(sgu + (size_t)t * p.RB, sgu + (size_t)(S.NSQ + t) * p.RB, sb, xr, xst, g, u);
+                        const float v = pair_reduce(g, u, lane);
+                        if (lane == 0) sgp[t * SPL + hf] = v;
+                        if (lane == 16) sup[t * SPL + hf] = v;
+                    }
+                }
+            }
+        }
+        if (__syncthreads_or(!a_ok)) {
+            if (tid == 0) sk_fail(sy, a.status);
+            ok = false;
+            break;
+        }
+        trace_mark(a, L, 4);
+
+        // ---- B: gate|up pairs ------------------------------------------------
         // This warp's column split of every row pair: lane l owns sub-block
         // hf * 32 + l; the activation block in registers.
         const int hf = warp % SPL, stream = warp / SPL, sb = hf * 32 + lane;
@@ -745,22 +901,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             xr[4 * q + 3] = w4.w;
         }
         const float xst = xs[sb];
-        // ---- the shared expert's pairs (rows prefetched) --------------------
-        if (__syncthreads_or(!mbar_wait(bar_sgu, par))) {
-            if (tid == 0) sk_fail(sy, a.status);
-            ok = false;
-            break;
-        }
-        for (int t = stream; t < nsq; t += NSTREAM) {
-            float g, u;
-            pair_dot(sgu + (size_t)t * p.RB, sgu + (size_t)(S.NSQ + t) * p.RB, sb, xr, xst, g, u);
-            const float v = pair_reduce(g, u, lane);
-            if (lane == 0) sgp[t * SPL + hf] = v;
-            if (lane == 16) sup[t * SPL + hf] = v;
-        }
-        trace_mark(a, L, 4);
-
-        // ---- routed pairs as their chunks land, two per warp at a time ------
+        // the routed pairs as their chunks land, two per warp at a time
         for (int u = stream; u < np && ok; u += 2 * NSTREAM) {
             const int u2 = u + NSTREAM;
             const bool two = u2 < np;
@@ -800,29 +941,37 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             st_relaxed_u32(sy.hw + (routed ? p.p_lo + i : K * I + p.sq_lo + i),
                            (__float_as_uint(h) & 0xFFFFFF00u) | (stamp & 0xFFu));
         }
+        dev_mark(a, L, 25);
         __syncthreads();
         if (tid == 0) arrive(sy.hcnt, c);
         trace_mark(a, L, 6);
+        // the down rows of the selected experts, needed once every h is in:
+        // issued now, behind the gate|up rows
+        if (warp == kSKWarps - 1) {
+            ptx::fence_proxy_async();  // every issuing lane (dbuf was read in the last layer's phase C)
+            issue_down(W, p, S, sm, tki, bar_dn, lane);
+            if (lane == 0) s_misc[3] += 1u;
+            dev_mark(a, L, 26, 32 * (kSKWarps - 1));
+        }
 
-        // ---------------- phase C --------------------------------------------
-        // Every CTA's h is in once the h round is complete: one bulk copy of
-        // all of it into the (consumed) gate|up buffers, then the next layer's
-        // prefetches behind it.
+        // ---- C: down, the next layer's input ---------------------------------
+        // Once every CTA's h is counted in: one bulk copy of all of it into
+        // the (consumed) gate|up buffers, then the next layer's prefetches
+        // behind it.
         if (warp == 0) {
             const bool got = wait_round(sy.hcnt, (unsigned)(L + 1), NW, sy, a.status);
             if (lane == 0) {
                 s_misc[0] = got ? 1u : 0u;
                 if (got) {
-                    ptx::fence_proxy_async_global();  // the acquired h words, then the async-proxy read
-                    ptx::fence_proxy_async();
+                    ptx::fence_proxy_async();  // gbuf was read by the generic proxy
                     mbar_expect_tx(bar_h, (uint32_t)(NH * 4));
                     ptx::bulk_g2s(hstage, sy.hw, (uint32_t)(NH * 4), bar_h);
                     ++iss_h;
                     if (!last) {
                         issue_sgu(a.L[L + 1], p, S, sm, bar_sgu);
-                        issue_rcol(&a.rmap[L + 1], &a.gmap[L + 1], p, S, sm, bar_rc);
+                        issue_rrow(a.L[L + 1], p, S, sm, bar_rr);
                         ++iss_sgu;
-                        ++iss_rc;
+                        ++iss_rr;
                     }
                 }
             }
@@ -833,10 +982,6 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             break;
         }
         trace_mark(a, L, 7);
-        // this CTA's lines of the accumulator two layers on: every CTA has read
-        // it (layer L - 1's logits) before arriving on this h round
-        for (int i = c + tid * NW; i <= E; i += kSKThreads * NW)
-            sy.logits[(size_t)((L + 2) % 3) * G + (size_t)i * 16] = 0.0;
         {
             // the h words -> block floating point (hq, hs)
             if (__syncthreads_or(!mbar_wait(bar_h, par))) {
@@ -844,6 +989,7 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
                 ok = false;
                 break;
             }
+            dev_mark(a, L, 27);
             constexpr int HPW = (NHB + kSKWarps - 1) / kSKWarps;
             const unsigned t8 = stamp & 0xFFu;
             unsigned hv[HPW];
@@ -989,39 +1135,31 @@ __global__ void __launch_bounds__(kSKThreads, 1) stack_kernel(const __grid_const
             if (last) a.out[p.j_lo + tid] = v;
             else st_relaxed_u32(sy.xw + p.j_lo + tid, ((stamp_of(L + 1) & 0xFFFFu) << 16) | __bfloat16_as_ushort(xb));
             if (a.act_trace) a.act_trace[(size_t)L * D + p.j_lo + tid] = xb;
-            xo[xwin + tid] =
-                __bfloat162float(a.teacher && !last ? a.teacher[(size_t)(L + 1) * D + p.j_lo + tid] : xb);
         }
         trace_mark(a, L, 11);
         if (last) break;
-        // the next layer's router partial, then the arrival on the logit counters
-        if (__syncthreads_or(!mbar_wait(bar_rc, (uint32_t)((L + 1) & 1)))) {
-            if (tid == 0) sk_fail(sy, a.status);
-            ok = false;
-            break;
-        }
-        router_partial(p, S, sm, sy.logits + (size_t)((L + 1) % 3) * G);
         __syncthreads();
         if (tid == 0) arrive(sy.xcnt, c);
         trace_mark(a, L, 12);
     }
 
-    // The launch counters, read by every CTA at its start (before its first
-    // arrival, which every CTA waits for before its first layer).
+    // The launch counter, read by every CTA at its start (before its first
+    // arrival on the h counters, which every CTA waits for in every layer).
     if (c == 0 && tid == 0) {
         st_relaxed_u32(reinterpret_cast<unsigned*>(a.sync), lc + 1u);
         if (XC) *a.xepoch = xepoch + 1u;
     }
 
     // Stopped early: let this CTA's copies in flight land (bounded) before exit.
+    __syncthreads();
     if (!ok && tid == 0) {
         if (iss_sgu > 0) (void)mbar_wait(bar_sgu, (uint32_t)((iss_sgu - 1) & 1));
-        if (iss_rc > 0) (void)mbar_wait(bar_rc, (uint32_t)((iss_rc - 1) & 1));
+        if (iss_rr > 0) (void)mbar_wait(bar_rr, (uint32_t)((iss_rr - 1) & 1));
         if (iss_sdn > 0) (void)mbar_wait(bar_sdn, (uint32_t)((iss_sdn - 1) & 1));
         if (iss_h > 0) (void)mbar_wait(bar_h, (uint32_t)((iss_h - 1) & 1));
-        if (iss_routed > 0) {
-            const uint32_t q = (uint32_t)((iss_routed - 1) & 1);
-            (void)mbar_wait(bar_dn, q);
+        if (s_misc[3] > 0u) (void)mbar_wait(bar_dn, (s_misc[3] - 1u) & 1u);
+        if (iss_gu > 0) {
+            const uint32_t q = (uint32_t)((iss_gu - 1) & 1);
             for (int ch = 0; ch < nch; ++ch) (void)mbar_wait(bar_ch + ch, q);
         }
     }
@@ -1073,14 +1211,6 @@ bool down_format_ok(int I, int nseg, int nsub) {
 
 }  // namespace
 
-// fp32 [rows][cols] row-major (cols * 4 bytes a multiple of 16, base 16-byte
-// aligned) as a 2-D tensor with boxes of kRColW columns x min(rows, kRBoxRows)
-// rows; reads past the last column return zeros.
-static cudaError_t encode_rows_map(CUtensorMap* m, const float* base, int cols, int rows) {
-    return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, (unsigned long long)cols, (unsigned long long)rows,
-                     (unsigned long long)cols * 4, kRColW, (unsigned)(rows < kRBoxRows ? rows : kRBoxRows));
-}
-
 bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers, int R) {
     if (M != 1 || n_layers < 1 || n_layers > kSKMaxLayers || R < 1 || R > kMaxXchgRanks) return false;
     if (d.expert_lo != 0 || d.expert_hi != d.n_experts) return false;
@@ -1129,18 +1259,11 @@ cudaError_t launch_stack_kernel(const void* x, float* out, unsigned char* sync, 
     unsigned smem = 0;
     void (*kern)(SKArgs) = pick_kernel(d, n, &smem, xc != nullptr);
     if (!kern) return cudaErrorInvalidValue;
-    for (int l = 0; l < n_layers; ++l) {
-        cudaError_t e = encode_rows_map(&a.rmap[l], layers[l].router, d.hidden, d.n_experts);
-        if (e == cudaSuccess) e = encode_rows_map(&a.gmap[l], layers[l].gate_vec, d.hidden, 1);
-        if (e != cudaSuccess) return e;
-    }
     cudaError_t err = smem_opt_in(reinterpret_cast<const void*>(kern), (int)smem);
     if (err != cudaSuccess) return err;
-    // The abort word, the round counters and the three logit accumulators
-    // start at zero for every launch; the launch counter (offset 0) and the
-    // tagged words are kept.
-    err = cudaMemsetAsync(sync + kStackAbortOff, 0, kStackLogitOff + stack_logit_bytes(d.n_experts) - kStackAbortOff,
-                          stream);
+    // The abort word and the round counters start at zero for every launch;
+    // the launch counter (offset 0) and the tagged words are kept.
+    err = cudaMemsetAsync(sync + kStackAbortOff, 0, kStackLogitOff - kStackAbortOff, stream);
     if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)n);

@@ -11,6 +11,12 @@ __device__ __forceinline__ bool topk_better(float a, int ia, float b, int ib) {
     return a > b || (a == b && ia < ib);
 }
 
+// Order-preserving map of a float to an unsigned integer (for redux.sync max).
+__device__ __forceinline__ unsigned topk_ord(float f) {
+    const unsigned b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 // Top-k of E logits (E % 32 == 0, E <= 1024, k <= 16) for one token, by one
 // warp.  Selection is on p_i = exp(l_i - l_max), the softmax numerators: the
 // reference ranks fp32 softmax probabilities (reference/model.py:400-401),
@@ -23,16 +29,18 @@ __device__ __forceinline__ bool topk_better(float a, int ia, float b, int ib) {
 // T0), so only elements not worse than T0 are ranked.  With distinct values
 // that is typically k to 2k candidates; a run of ties larger than the
 // candidate buffer falls back to k rounds of warp arg-max.
-static __device__ __noinline__ float warp_topk(const float* __restrict__ logits, int E, int k, float* cv, int* ci,
-                           float* sv, int* si) {
+// `load(j)` gives this lane's logit lane + 32 j (j < E / 32 <= NPL); the
+// per-lane values stay in registers.
+template <int NPL, class Load>
+__device__ __forceinline__ float warp_topk_fn(Load load, int E, int k, float* cv, int* ci, float* sv, int* si) {
     const int lane = threadIdx.x & 31;
     const int npl = E >> 5;
-    float v[32];
+    float v[NPL];
     float lmax = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < NPL; ++j) {
         if (j < npl) {
-            float t = __ldcg(logits + lane + 32 * j);
+            float t = load(j);
             if (t != t) t = -INFINITY;  // NaN ranks last
             v[j] = t;
             lmax = fmaxf(lmax, t);
@@ -43,7 +51,7 @@ static __device__ __noinline__ float warp_topk(const float* __restrict__ logits,
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < NPL; ++j) {
         if (j < npl) {
             v[j] = expf(v[j] - lmax);
             if (topk_better(v[j], lane + 32 * j, bv, bi)) {
@@ -66,7 +74,7 @@ static __device__ __noinline__ float warp_topk(const float* __restrict__ logits,
 
     int c = 0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
+    for (int j = 0; j < NPL; ++j)
         if (j < npl && !topk_better(tv, ti, v[j], lane + 32 * j)) ++c;
     int incl = c;
 #pragma unroll
@@ -79,7 +87,7 @@ static __device__ __noinline__ float warp_topk(const float* __restrict__ logits,
     if (total <= kCandCap) {
         int pos = incl - c;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < NPL; ++j) {
             if (j < npl && !topk_better(tv, ti, v[j], lane + 32 * j)) {
                 cv[pos] = v[j];
                 ci[pos] = lane + 32 * j;
@@ -107,7 +115,7 @@ static __device__ __noinline__ float warp_topk(const float* __restrict__ logits,
         float lv = -INFINITY;
         int li = 0x7fffffff;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < NPL; ++j) {
             if (j < npl && !((taken >> j) & 1u) && topk_better(v[j], lane + 32 * j, lv, li)) {
                 lv = v[j];
                 li = lane + 32 * j;
@@ -134,112 +142,118 @@ static __device__ __noinline__ float warp_topk(const float* __restrict__ logits,
     return lmax;
 }
 
-}  // namespace qmoe
-
-namespace qmoe {
-
-struct NoStamp {
-    __device__ void operator()(int, unsigned long long = 0) const {}
-};
-
-// Order-preserving map of a float to an unsigned integer (for redux.sync max).
-__device__ __forceinline__ unsigned topk_ord(float f) {
-    const unsigned b = __float_as_uint(f);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+// The warp top-k of E fp32 logits in global memory (read through L2).
+static __device__ __noinline__ float warp_topk(const float* __restrict__ logits, int E, int k, float* cv, int* ci,
+                                               float* sv, int* si) {
+    return warp_topk_fn<32>([&](int j) { return __ldcg(logits + (threadIdx.x & 31) + 32 * j); }, E, k, cv, ci, sv,
+                            si);
 }
 
-// Top-k of E logits (E <= blockDim.x, E a multiple of the warp count, k <= 16)
-// by the whole CTA in a fixed number of steps.  Same selection rule as
-// warp_topk: unique keys (p bits << 32 | ~id) on p = exp(l - l_max).  Thread
-// (warp w, lane l) holds expert l * nw + w, so every warp sees experts spread
-// over the whole id range:
-//   1. the block maximum of the logits;
-//   2. each warp's largest key; T0 = the k-th largest of the nw warp maxima.
-//      Every member of the top k is >= T0 (k distinct keys reach it);
-//   3. keys >= T0 are the candidates: about k for distinct probabilities, and
-//      still about k when many tie (each warp's maximum is then its lowest
-//      tied id, so T0 is the k-th lowest tied id); each candidate is ranked
-//      against all, up to 256 of them; beyond that (adversarial ties), k
-//      rounds of block arg-max.
-// `logit(i)` loads logit i (from L2: it is read once); `between()` runs while
-// the loads are in flight.  Shared scratch: cand[256] u64, wmax[nw + 1] u64,
-// red[nw] u32, cnt (int).  Writes tkv (p values, not normalised) and tki
-// (ids), descending; returns l_max.  Every thread of the CTA must call it.
-template <class LogitAt, class Between, class Stamp = NoStamp>
-__device__ __forceinline__ float block_topk_threshold(LogitAt logit, int E, int k, unsigned long long* cand,
-                                                      unsigned long long* wmax, unsigned* red, int* cnt, float* tkv,
-                                                      int* tki, Between between, Stamp stamp = Stamp()) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int e = lane * nw + warp;
-    float l = -INFINITY;
-    if (e < E) l = logit(e);
-    stamp(0, (unsigned long long)__float_as_uint(l));
-    between();  // caller's work that overlaps the logit loads
-    stamp(1, 0ull);
-    if (l != l) l = -INFINITY;  // NaN ranks last
-    const unsigned m = __reduce_max_sync(0xffffffffu, topk_ord(l));
-    if (lane == 0) red[warp] = m;
-    if (tid == 0) *cnt = 0;
-    __syncthreads();
-    unsigned mm = 0;
-    for (int w = 0; w < nw; ++w) mm = max(mm, red[w]);
-    const float lmax = __uint_as_float((mm & 0x80000000u) ? (mm & 0x7FFFFFFFu) : ~mm);
-    const unsigned long long key =
-        e < E ? ((unsigned long long)__float_as_uint(expf(l - lmax)) << 32) | (0xFFFFFFFFu - (unsigned)e) : 0ull;
-    const unsigned kh = (unsigned)(key >> 32), kl = (unsigned)key;
-    const unsigned mh = __reduce_max_sync(0xffffffffu, kh);
-    const unsigned ml = __reduce_max_sync(0xffffffffu, kh == mh ? kl : 0u);
-    if (lane == 0) wmax[warp] = ((unsigned long long)mh << 32) | ml;
-    __syncthreads();
-    if (tid < nw) {
-        const unsigned long long v = wmax[tid];
-        int r = 0;
-        for (int w = 0; w < nw; ++w) r += wmax[w] > v ? 1 : 0;
-        if (r == k - 1) wmax[nw] = v;
+
+// Tie-admitting threshold routing for one token by one warp: the reference's
+// device select in its non-exact mode (scripts/kernels/router_select.cpp:
+// 223-255, the ttnn chain of tt/moe.py:308-327).  The softmax probabilities
+// p_e (numerators exp(l_e - l_max) over their sum; each lane sums its ids in
+// order, then a butterfly over the lanes), rounded to bf16 when probs_bf16;
+// the threshold t is the k-th largest p counting equal values separately;
+// total = the sum of every p_e >= t; then the k_sel largest positive p_e >= t
+// with ids in [e_lo, e_hi), ties to the lower id, written as (id, p_e / total
+// via the reciprocal) to ids/weights, the remaining slots as (e_lo, 0).
+// E % 32 == 0, E <= 1024, k <= 16, k_sel <= 16.  Returns l_max.
+static __device__ __noinline__ float warp_select_threshold(const float* __restrict__ lg, int E, int k, int k_sel,
+                                                           int e_lo, int e_hi, int probs_bf16, int32_t* ids,
+                                                           float* weights) {
+    const int lane = threadIdx.x & 31;
+    const int npl = E >> 5;
+    float v[32];
+    float lmax = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (j < npl) {
+            float t = __ldcg(lg + lane + 32 * j);
+            if (t != t) t = -INFINITY;  // NaN ranks last
+            v[j] = t;
+            lmax = fmaxf(lmax, t);
+        }
     }
-    __syncthreads();
-    const unsigned long long T0 = wmax[nw];
-    stamp(2, T0);
-    const bool is_c = e < E && key >= T0;
-    const unsigned bal = __ballot_sync(0xffffffffu, is_c);
-    int base = 0;
-    if (lane == 0 && bal) base = atomicAdd(cnt, __popc(bal));
-    base = __shfl_sync(0xffffffffu, base, 0);
-    const int pos = base + __popc(bal & ((1u << lane) - 1u));
-    if (is_c && pos < 256) cand[pos] = key;
-    __syncthreads();
-    const int C = *cnt;
-    if (C <= 256) {
-        for (int i = tid; i < C; i += blockDim.x) {
-            const unsigned long long ci = cand[i];
-            int r = 0;
-            for (int j = 0; j < C; ++j) r += cand[j] > ci ? 1 : 0;
-            if (r < k) {
-                tkv[r] = __uint_as_float((unsigned)(ci >> 32));
-                tki[r] = (int)(0xFFFFFFFFu - (unsigned)ci);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (j < npl) {
+            v[j] = expf(v[j] - lmax);
+            s += v[j];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (j < npl) {
+            float pj = v[j] / s;
+            if (probs_bf16) pj = __bfloat162float(__float2bfloat16_rn(pj));
+            v[j] = pj;
+        }
+    }
+    // One round of warp arg-max (value, lowest id) over this lane's values
+    // that `ok` admits and `taken` has not marked; marks the winner.
+    auto argmax = [&](uint32_t& taken, auto ok, float& wv, int& wi) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (j < npl && !((taken >> j) & 1u) && ok(j) && topk_better(v[j], lane + 32 * j, bv, bi)) {
+                bv = v[j];
+                bi = lane + 32 * j;
             }
         }
-        __syncthreads();
-        stamp(3, 0ull);
-        return lmax;
-    }
-    // Adversarial ties: k rounds of block arg-max over the keys.
-    unsigned long long mine = key;
-    for (int r = 0; r < k; ++r) {
-        const unsigned h = (unsigned)(mine >> 32), lo = (unsigned)mine;
-        const unsigned wh = __reduce_max_sync(0xffffffffu, h);
-        const unsigned wl = __reduce_max_sync(0xffffffffu, h == wh ? lo : 0u);
-        if (lane == 0) cand[warp] = ((unsigned long long)wh << 32) | wl;
-        __syncthreads();
-        unsigned long long best = 0ull;
-        for (int w = 0; w < nw; ++w) best = cand[w] > best ? cand[w] : best;
-        if (tid == 0) {
-            tkv[r] = __uint_as_float((unsigned)(best >> 32));
-            tki[r] = (int)(0xFFFFFFFFu - (unsigned)best);
+        wv = bv;
+        wi = bi;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
+            if (topk_better(ov, oi, wv, wi)) {
+                wv = ov;
+                wi = oi;
+            }
         }
-        if (mine == best) mine = 0ull;
-        __syncthreads();
+        if (bi == wi && bi != 0x7fffffff) taken |= 1u << ((wi - lane) >> 5);
+    };
+    uint32_t taken = 0;
+    float thr = 0.0f;
+    for (int r = 0; r < k; ++r) {
+        float wv;
+        int wi;
+        argmax(taken, [&](int) { return true; }, wv, wi);
+        thr = wi != 0x7fffffff ? wv : 0.0f;
     }
+    float tot = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        if (j < npl && v[j] >= thr) tot += v[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    const float inv = tot > 0.0f ? 1.0f / tot : 0.0f;
+    taken = 0;
+    for (int r = 0; r < k_sel; ++r) {
+        float wv;
+        int wi;
+        argmax(
+            taken,
+            [&](int j) {
+                const int id = lane + 32 * j;
+                return id >= e_lo && id < e_hi && v[j] > 0.0f && v[j] >= thr;
+            },
+            wv, wi);
+        if (lane == 0) {
+            const bool got = wi != 0x7fffffff;
+            ids[r] = got ? wi : e_lo;
+            weights[r] = got ? wv * inv : 0.0f;
+        }
+    }
+    __syncwarp();
     return lmax;
 }
 

@@ -24,9 +24,9 @@ from .weights import DeviceLayer
 
 # The single-launch kernel's phase stamps per layer (qmoe_read_stack_trace).
 TRACE_SLOTS = 24
-TRACE_POINTS = ("layer start", "logit round complete", "ranked, copies issued", "x ready", "shared pairs done",
+TRACE_POINTS = ("layer start", "x gathered", "x checked", "ranked, gate|up copies issued", "shared pairs done",
                 "gate|up pairs done", "h words written", "h round complete", "h converted", "down rows landed",
-                "down done", "output rows written", "logit partials added", "", "", "",
+                "down done", "output rows written", "arrived", "", "", "",
                 "gate|up chunk 0 landed", "chunk 1 landed", "chunk 2 landed", "chunk 3 landed", "chunk 4 landed",
                 "chunk 5 landed", "exchange: partial rows sent", "exchange: peers' rows summed")
 
