@@ -365,6 +365,41 @@ int qmoe_prefill(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weig
                  const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* ---- the hyper-connection mixer around the block ------------------------ */
+/* The reference's gated residual (reference/model.py:53-81; device ops
+ * tt/ops.py:2627 gated_residual_mix and :2825 reinject): the MoE block reads
+ * `mixed` and its output (the branch) goes back into every residual stream
+ * weighted by `inject`.  hyper [M, hc * hidden] holds hc residual streams. */
+typedef struct qmoe_hc_weights {
+    const float* norm_w;    /* [hc * hidden] RMS-norm weights, stream-major          */
+    const float* down_w;    /* [rank, hc * hidden]                                    */
+    const float* up_w;      /* [hc * hidden, rank]                                    */
+    const float* inject_w;  /* [hc, hc * hidden]                                      */
+} qmoe_hc_weights;
+
+typedef struct qmoe_hc_dims {
+    int hidden;  /* per-stream width: multiple of 32                                  */
+    int hc;      /* streams: 1..16                                                   */
+    int rank;    /* width of the low-rank gate: 1..4096                              */
+    float eps;   /* RMS-norm epsilon (the config's rms_norm_eps)                      */
+} qmoe_hc_dims;
+
+/* Workspace bytes of qmoe_hc_mix for n_tokens tokens (256-byte aligned base). */
+size_t qmoe_hc_workspace_bytes(const qmoe_hc_dims* dims, int n_tokens);
+/* normed = rms_norm(hyper, norm_w, eps) per stream of `hidden` values
+ * (reference/layers.py:31-43); mixed [M, hidden] fp32 = mean over the streams
+ * of sigmoid(up_w . silu(down_w . normed / hc)) * normed; inject [M, hc] fp32
+ * = 2 sigmoid(inject_w . normed / hc) (model.py:62-77).  hyper: device, bf16 or
+ * fp32 (hyper_dtype); weights fp32; all 16-byte aligned.  fp32 arithmetic. */
+int qmoe_hc_mix(const void* hyper, int hyper_dtype, int n_tokens, const qmoe_hc_weights* w,
+                const qmoe_hc_dims* dims, float* mixed, float* inject, void* workspace,
+                size_t workspace_bytes, void* stream);
+/* out [M, hc * hidden] fp32 = hyper + branch (outer) inject, stream s of token m
+ * adding branch[m] * inject[m][s] (model.py:80-81).  branch [M, hidden] bf16 or
+ * fp32 (branch_dtype); out may be hyper itself when that is fp32. */
+int qmoe_hc_reinject(const void* hyper, int hyper_dtype, const void* branch, int branch_dtype,
+                     const float* inject, int n_tokens, const qmoe_hc_dims* dims, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -143,6 +143,73 @@ def route(x: np.ndarray, router: np.ndarray, k: int) -> dict:
     return {"logits": logits, "probs": probs, "ids": ids, "weights": w}
 
 
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 -> fp32, round to nearest even (finite values)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
+def _lane_sum(v: np.ndarray) -> np.float32:
+    """Sum of E values (E % 32 == 0) in the device warp's order: lane t adds
+    ids t, t + 32, ... in turn, then a butterfly over the 32 lanes."""
+    lanes = np.zeros(32, np.float32)
+    for j in range(v.shape[0] // 32):
+        lanes = (lanes + v[32 * j:32 * (j + 1)]).astype(np.float32)
+    for o in (16, 8, 4, 2, 1):
+        lanes = (lanes + lanes[np.arange(32) ^ o]).astype(np.float32)
+    return lanes[0]
+
+
+def route_threshold(logits: np.ndarray, k: int, k_sel: int, e_lo: int = 0, e_hi: int | None = None,
+                    probs_bf16: bool = False) -> tuple[np.ndarray, np.ndarray]:
+    """The reference device select's tie-admitting mode, EXACT_TOPK off
+    (scripts/kernels/router_select.cpp:223-255): on the softmax probabilities
+    (rounded to bf16 when probs_bf16, as the ttnn chain compares them,
+    tt/moe.py:318-327) the threshold is the k-th largest counting equal values
+    separately (:176-193); `total` sums every probability >= the threshold
+    (:226-235); the k_sel largest positive ones >= the threshold inside
+    [e_lo, e_hi) are selected, ties to the lower id (:237-254), with weight
+    p * (1 / total) (:256-260); empty slots are (e_lo, 0).  The softmax sum and
+    `total` are taken in the device warp's order (_lane_sum) -- the reference
+    sums in id order -- so the oracle matches the kernel to the last bit of
+    its own arithmetic.  logits [M, E] fp32 -> ids [M, k_sel] int32, weights
+    [M, k_sel] fp32."""
+    logits = np.asarray(logits, dtype=np.float32)
+    M, E = logits.shape
+    e_hi = E if e_hi is None else e_hi
+    ids = np.full((M, k_sel), e_lo, dtype=np.int32)
+    wts = np.zeros((M, k_sel), dtype=np.float32)
+    for m in range(M):
+        l = logits[m].copy()
+        l[np.isnan(l)] = -np.inf
+        p = np.exp((l - l.max()).astype(np.float32)).astype(np.float32)
+        probs = (p / _lane_sum(p)).astype(np.float32)
+        if probs_bf16:
+            probs = bf16_round(probs)
+        thr = np.sort(probs)[::-1][k - 1]
+        total = _lane_sum(np.where(probs >= thr, probs, np.float32(0.0)).astype(np.float32))
+        inv = np.float32(1.0) / total if total > 0 else np.float32(0.0)
+        cand = [e for e in range(e_lo, e_hi) if probs[e] > 0 and probs[e] >= thr]
+        cand.sort(key=lambda e: (-probs[e], e))
+        for i, e in enumerate(cand[:k_sel]):
+            ids[m, i] = e
+            wts[m, i] = np.float32(probs[e] * inv)
+    return ids, wts
+
+
+def route_threshold_dense(logits: np.ndarray, k: int, probs_bf16: bool = True) -> np.ndarray:
+    """The ttnn chain of tt/moe.py:318-327 on CPU: probabilities, their k-th
+    largest as the threshold, keep = probs >= threshold, the kept ones
+    renormalised -> dense weights [M, E] (every kept expert, no slot cap)."""
+    probs = softmax(np.asarray(logits, dtype=np.float32))
+    if probs_bf16:
+        probs = bf16_round(probs)
+    thr = -np.sort(-probs, axis=-1)[:, k - 1:k]
+    kept = np.where(probs >= thr, probs, np.float32(0.0)).astype(np.float32)
+    return (kept / kept.sum(axis=-1, keepdims=True)).astype(np.float32)
+
+
 def raw_topk_differs(probs: np.ndarray, ids: np.ndarray, k: int) -> np.ndarray:
     """Rows whose `torch.topk` selection differs as a set from the canonical one."""
     import torch
@@ -174,7 +241,8 @@ class ExpertSource:
 
 def moe_forward(x: np.ndarray, src: ExpertSource, k: int, with_shared: bool = True,
                 expert_window: tuple[int, int] | None = None,
-                inter_window: tuple[int, int] | None = None, cache: dict | None = None) -> dict:
+                inter_window: tuple[int, int] | None = None, cache: dict | None = None,
+                routing: tuple[np.ndarray, np.ndarray] | None = None) -> dict:
     """Qwen4ExpModel._moe (model.py:387-417) on flat fp32 x [M, D].
 
     expert_window / inter_window restrict the routed experts to a variant-A
@@ -183,6 +251,8 @@ def moe_forward(x: np.ndarray, src: ExpertSource, k: int, with_shared: bool = Tr
     cache: dequantised experts kept across calls (keys: expert id, "shared"),
     the role of WeightStore's row cache (reference/weights.py:48-53) when it
     is warm; None decodes every expert on each use (cold).
+    routing: (ids [M, n], weights [M, n]) to use instead of the top-k of
+    model.py:399-403 (e.g. route_threshold's selection; weight-0 slots add 0).
     """
 
     def dq(key, gu_b, dn_b):
@@ -208,6 +278,8 @@ def moe_forward(x: np.ndarray, src: ExpertSource, k: int, with_shared: bool = Tr
         shared = (s * gate).astype(np.float32)
 
     r = route(x, src.router, k)                                                      # :399-403
+    if routing is not None:
+        r["ids"], r["weights"] = routing
     ids, weights = r["ids"], r["weights"]
     out = np.zeros_like(x)
     for e in np.unique(ids):                                                          # :407

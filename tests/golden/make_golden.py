@@ -24,6 +24,10 @@ What it records (all small, committed as .npz):
     c1_m1               BASELINE config 1: hidden 2048, inter 512, 512 experts
     c1_m4, c1_m8        the config-3 token counts through one config-1 layer
     tie_m2              a router whose 64 rows are identical: every logit ties.
+    hc_small, hc_c1     the hyper-connection mixer around the block
+                        (reference/model.py:53-81; `make_golden.py hc` makes
+                        these alone): 4 streams of hidden 512 / 2048, low rank
+                        64 / 32, seeded by oracle/hc_ref.py.
                         torch.topk's CPU tie order is not lower-index, so this
                         case runs the reference with torch.topk replaced by a
                         stable lower-index selection (the rule of the
@@ -188,7 +192,35 @@ def dequant_fixture() -> None:
     print("iq4xs_dequant: random", int(finite.sum()), "finite of", finite.size, "| quantiser blocks 32")
 
 
+def hc_fixture(name: str, hidden: int, hc: int, rank: int, m: int, seed: int) -> None:
+    """The reference's hyper-connection mixer (reference/model.py:53-81) on seeded weights and
+    inputs: the fixture keeps the seeds and the reference's outputs (the weights regenerate from
+    oracle/hc_ref.synth_weights)."""
+    from oracle import hc_ref
+
+    w = hc_ref.synth_weights(seed, hidden, hc, rank)
+    hyper, branch = hc_ref.synth_inputs(seed, hidden, hc, m)
+    g = FakeGGUF()
+    n = hc * hidden
+    for tag, shape in (("norm", (n,)), ("down", (rank, n)), ("up", (n, rank)), ("inject", (hc, n))):
+        g.add(f"blk.0.hc_ffn_{tag}.weight", shape, GGMLType.F32, w[f"{tag}_w"])
+    cfg = make_config(pkg.MoEConfig(hidden=hidden))
+    cfg.hc_count, cfg.hc_lowrank = hc, rank
+    model = Qwen4ExpModel(cfg, WeightStore(g))
+    h = torch.from_numpy(hyper).reshape(1, m, n)
+    mixed, _, inject = model._gated_residual(h, 0, "ffn")
+    out = model._reinject(h, torch.from_numpy(branch).reshape(1, m, hidden), inject)
+    np.savez_compressed(HERE / f"hc_{name}.npz", hidden=hidden, hc=hc, rank=rank, n_tokens=m, seed=seed,
+                        eps=cfg.rms_norm_eps, mixed=mixed.reshape(m, hidden).numpy(),
+                        inject=inject.reshape(m, hc).numpy(), reinjected=out.reshape(m, n).numpy())
+    print(f"hc_{name}: mixed[0,:3] {mixed.reshape(m, hidden)[0, :3].tolist()} inject[0] {inject.reshape(m, hc)[0].tolist()}")
+
+
 def main() -> None:
+    if len(sys.argv) > 1 and sys.argv[1] == "hc":
+        hc_fixture("small", 512, 4, 64, 2, 21)
+        hc_fixture("c1", 2048, 4, 32, 1, 22)
+        return
     dequant_fixture()
     small = pkg.MoEConfig(hidden=512, inter=256, n_experts=64, top_k=10, shared_inter=256)
     hl = pkg.synth_host_layer(small, layer=0, seed=7, all_experts=True)

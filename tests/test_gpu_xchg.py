@@ -3,8 +3,8 @@
 On one GPU: the single launch on one rank's variant-B slice (I / R local
 rows; down rows cut inside super-blocks at 4 and 8 ranks) against the
 per-layer launches on the same slice.  On two GPUs (skipped with fewer): two
-processes exchange partial rows over NVLink inside `qmoe_stack_decode_xchg`;
-both end with bitwise the same output, equal to the unsharded stack within
+processes (and 4 and 8 where the box has them) exchange partial rows over
+NVLink inside `qmoe_stack_decode_xchg`; all end with bitwise the same output, equal to the unsharded stack within
 the block tolerance, and a rank that never launches makes the other's
 bounded wait end with QMOE_ERR_TIMEOUT (no hang, no fault).
 """
@@ -119,15 +119,18 @@ def _spawn(world: int, n_layers: int, mode: str, out_dir: str) -> None:
 
 
 @pytest.mark.timeout(900)
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("n_layers", [1, 2])
-def test_two_ranks_exchange_inside_the_kernel(pkg, n_layers):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def test_ranks_exchange_inside_the_kernel(pkg, n_layers, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
-        _spawn(2, n_layers, "ok", d)
-        r0, r1 = np.load(Path(d) / "rank0.npz"), np.load(Path(d) / "rank1.npz")
-        assert (r0["status"] == 0).all() and (r1["status"] == 0).all()
-        assert np.array_equal(r0["out"], r1["out"]), "ranks must hold the same bits"
+        _spawn(world, n_layers, "ok", d)
+        rs = [np.load(Path(d) / f"rank{r}.npz") for r in range(world)]
+        for r in rs:
+            assert (r["status"] == 0).all()
+            assert np.array_equal(r["out"], rs[0]["out"]), "ranks must hold the same bits"
+        r0 = rs[0]
         assert np.array_equal(r0["out"][0], r0["out"][1]) and np.array_equal(r0["out"][1], r0["out"][2])
         got = torch.from_numpy(r0["out"][0])
     cfg = pkg.MoEConfig(n_layers=n_layers)

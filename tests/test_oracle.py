@@ -155,3 +155,48 @@ def test_row_cache_is_lru_by_bytes():
     v1[2] = row                              # over the limit: evicts the least recent, (1, 1)
     assert v1.get(1) is None and v0.get(1) is row and v1.get(2) is row
     assert c.hits == 3 and c.misses == 1
+
+
+def test_threshold_oracle_is_the_dense_chain_and_exact_without_ties(oracle):
+    """route_threshold (the device select's tie-admitting mode) keeps what the ttnn chain keeps
+    (tt/moe.py:318-327) and, with no tie at the k-th place, selects the exact top-k."""
+    rng = np.random.default_rng(3)
+    lg = rng.standard_normal((6, 512)).astype(np.float32)
+    tenth = int(np.argsort(-lg[2], kind="stable")[9])
+    others = [e for e in (40, 41, 42) if e != tenth]
+    lg[2, others] = lg[2, tenth]  # a tie at the 10th place
+    for bf16 in (False, True):
+        ids, w = oracle.route_threshold(lg, 10, 16, probs_bf16=bf16)
+        dense = oracle.route_threshold_dense(lg, 10, probs_bf16=bf16)
+        for m in range(lg.shape[0]):
+            kept = np.nonzero(dense[m] > 0)[0]
+            assert set(ids[m][w[m] > 0].tolist()) == set(kept.tolist())
+            np.testing.assert_allclose(w[m][w[m] > 0], dense[m][ids[m][w[m] > 0]], rtol=1e-6)
+    ids, w = oracle.route_threshold(lg, 10, 16)
+    assert (w[2] > 0).sum() == 10 + len(others)  # the tie admitted
+    for m in (0, 1, 3):
+        probs = oracle.softmax(lg[m:m + 1])
+        _, top = oracle.topk_canonical(probs, 10)
+        assert np.array_equal(ids[m][:10], top[0])
+        assert np.all(w[m][10:] == 0) and np.all(ids[m][10:] == 0)
+    # a window keeps only its experts, normalised over all that pass
+    wi, ww = oracle.route_threshold(lg, 10, 16, e_lo=256, e_hi=512)
+    for m in range(lg.shape[0]):
+        sel = wi[m][ww[m] > 0]
+        assert np.all((sel >= 256) & (sel < 512))
+        assert set(sel.tolist()) == set(e for e in ids[m][w[m] > 0].tolist() if e >= 256)
+
+
+@pytest.mark.parametrize("name", ["small", "c1"])
+def test_hc_oracle_matches_reference_fixture(name):
+    """oracle/hc_ref.py against the reference's own _gated_residual / _reinject outputs."""
+    from oracle import hc_ref
+
+    g = load_golden(f"hc_{name}.npz")
+    D, hc, r, m, seed = (int(g[k]) for k in ("hidden", "hc", "rank", "n_tokens", "seed"))
+    w = hc_ref.synth_weights(seed, D, hc, r)
+    hyper, branch = hc_ref.synth_inputs(seed, D, hc, m)
+    o = hc_ref.gated_residual(hyper, w, float(g["eps"]), hc, D)
+    for got, ref in ((o["mixed"], g["mixed"]), (o["inject"], g["inject"]),
+                     (hc_ref.reinject(hyper, branch, o["inject"]), g["reinjected"])):
+        assert float(np.abs(got - ref).max() / np.abs(ref).max()) < 1e-6

@@ -17,9 +17,11 @@ from .moe import (
     apply_experts,
     moe_block,
     route,
+    route_threshold,
     route_topk,
     shared_expert,
 )
+from .hc import gated_residual_mix, reinject
 from .stack import MoEStack
 from .weights import (
     DeviceLayer,
@@ -34,4 +36,7 @@ __all__ = [
     "C1", "C2", "MoEConfig", "Shard", "QMoEError", "MoELayer", "MoEStack", "Workspace", "PrefillWorkspace",
     "DeviceLayer", "HostLayer", "apply_experts", "moe_block", "route", "route_topk", "shared_expert",
     "synth_device_layer", "synth_host_layer", "synth_x", "upload_host_layer",
+    "route_threshold",
+    "gated_residual_mix",
+    "reinject",
 ]

@@ -74,6 +74,18 @@ class Xchg(ctypes.Structure):
     ]
 
 
+class HcWeights(ctypes.Structure):
+    """qmoe_hc_weights: the hyper-connection mixer's fp32 weights."""
+
+    _fields_ = [("norm_w", c_void_p), ("down_w", c_void_p), ("up_w", c_void_p), ("inject_w", c_void_p)]
+
+
+class HcDims(ctypes.Structure):
+    """qmoe_hc_dims."""
+
+    _fields_ = [("hidden", c_int), ("hc", c_int), ("rank", c_int), ("eps", c_float)]
+
+
 XCHG_HANDLE_BYTES = 64
 
 
@@ -132,6 +144,9 @@ _SIGS = {
                                        _P, c_size_t, _P]),
     "qmoe_moe_block_noalloc": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P]),
     "qmoe_noalloc_read_status": (c_int, [POINTER(c_int), _P]),
+    "qmoe_hc_workspace_bytes": (c_size_t, [POINTER(HcDims), c_int]),
+    "qmoe_hc_mix": (c_int, [_P, c_int, c_int, POINTER(HcWeights), POINTER(HcDims), _P, _P, _P, c_size_t, _P]),
+    "qmoe_hc_reinject": (c_int, [_P, c_int, _P, c_int, _P, c_int, POINTER(HcDims), _P, _P]),
     "qmoe_prefill_max_tokens": (c_int, []),
     "qmoe_prefill_small_group_max": (c_int, [c_int]),
     "qmoe_prefill_workspace_bytes": (c_size_t, [POINTER(Dims), c_int]),

@@ -186,6 +186,8 @@ int run_block(const void* x, int x_dtype, int M, const qmoe_layer_weights* w, co
     QMOE_TRY(run_route(x, x_dtype, M, w, d, ws.ids(), ws.weights(), ws.shared(), ws, s));
     ExpertArgs a = expert_args(x, x_dtype, M, ws.ids(), ws.weights(), ws.shared(), w, d, ws.h(),
                                ws.L.h_stride, out, ws.status());
+    a.hconv = ws.h();
+    a.hconv_stride = ws.L.h_stride;
     QMOE_TRY(cuda_status(launch_gateup(a, s)));
     return cuda_status(launch_down(a, s));
 }
@@ -372,6 +374,8 @@ int qmoe_down_combine(const float* h, int h_stride, int n_tokens, const int32_t*
     QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
     ExpertArgs a = expert_args(nullptr, QMOE_ACT_F32, n_tokens, ids, weights, shared_logit, w, dims,
                                (float*)h, h_stride, out, ws.status());
+    a.hconv = ws.h();  // the caller's h stays as given
+    a.hconv_stride = ws.L.h_stride;
     QMOE_TRY(check_smem(a));
     return cuda_status(launch_down(a, (cudaStream_t)stream));
 }
@@ -671,6 +675,53 @@ static int get_prefill_ws(void* workspace, size_t bytes, const qmoe_dims* d, int
     if (!aligned(workspace, 256)) return QMOE_ERR_ALIGNMENT;
     if (bytes < prefill_workspace_bytes(*d, T)) return QMOE_ERR_WORKSPACE;
     return QMOE_OK;
+}
+
+namespace {
+int check_hc(const qmoe_hc_dims* d, int M) {
+    if (!d) return QMOE_ERR_INVALID_ARG;
+    if (d->hidden < 32 || d->hidden % 32 || d->hc < 1 || d->hc > 16 || d->rank < 1 || d->rank > 4096 ||
+        !(d->eps >= 0.0f))
+        return QMOE_ERR_INVALID_ARG;
+    if (M < 1 || M > 1024) return QMOE_ERR_INVALID_ARG;
+    if (hc_down_smem(1, d->hc, d->hidden) > kSmemLimit || hc_up_smem(M, d->rank) > kSmemLimit)
+        return QMOE_ERR_UNSUPPORTED;
+    return QMOE_OK;
+}
+}  // namespace
+
+size_t qmoe_hc_workspace_bytes(const qmoe_hc_dims* dims, int n_tokens) {
+    if (check_hc(dims, n_tokens) != QMOE_OK) return 0;
+    return hc_workspace_bytes(n_tokens, dims->hc, dims->rank);
+}
+
+int qmoe_hc_mix(const void* hyper, int hyper_dtype, int n_tokens, const qmoe_hc_weights* w,
+                const qmoe_hc_dims* dims, float* mixed, float* inject, void* workspace,
+                size_t workspace_bytes, void* stream) {
+    QMOE_TRY(check_hc(dims, n_tokens));
+    QMOE_TRY(check_act(hyper, hyper_dtype));
+    if (!w || !w->norm_w || !w->down_w || !w->up_w || !w->inject_w || !mixed || !inject)
+        return QMOE_ERR_INVALID_ARG;
+    if (!aligned(w->norm_w, 16) || !aligned(w->down_w, 16) || !aligned(w->up_w, 16) ||
+        !aligned(w->inject_w, 16))
+        return QMOE_ERR_ALIGNMENT;
+    if (!workspace) return QMOE_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return QMOE_ERR_ALIGNMENT;
+    if (workspace_bytes < hc_workspace_bytes(n_tokens, dims->hc, dims->rank)) return QMOE_ERR_WORKSPACE;
+    return cuda_status(launch_hc_mix(hyper, hyper_dtype == QMOE_ACT_F32, n_tokens, dims->hidden, dims->hc,
+                                     dims->rank, dims->eps, w->norm_w, w->down_w, w->up_w, w->inject_w, mixed,
+                                     inject, (unsigned char*)workspace, (cudaStream_t)stream));
+}
+
+int qmoe_hc_reinject(const void* hyper, int hyper_dtype, const void* branch, int branch_dtype,
+                     const float* inject, int n_tokens, const qmoe_hc_dims* dims, float* out, void* stream) {
+    QMOE_TRY(check_hc(dims, n_tokens));
+    QMOE_TRY(check_act(hyper, hyper_dtype));
+    QMOE_TRY(check_act(branch, branch_dtype));
+    if (!inject || !out) return QMOE_ERR_INVALID_ARG;
+    if (out == hyper && hyper_dtype != QMOE_ACT_F32) return QMOE_ERR_INVALID_ARG;
+    return cuda_status(launch_hc_reinject(hyper, hyper_dtype == QMOE_ACT_F32, branch, branch_dtype == QMOE_ACT_F32,
+                                          inject, n_tokens, dims->hidden, dims->hc, out, (cudaStream_t)stream));
 }
 
 int qmoe_prefill_max_tokens(void) { return prefill_max_tokens(); }

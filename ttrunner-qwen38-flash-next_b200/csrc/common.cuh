@@ -140,6 +140,11 @@ struct ExpertArgs {
     int sh_I_loc;           // 0: no shared expert
     float* h;               // [M][k+1][h_stride]
     int h_stride;
+    // the h blocks in block floating point for M > 1: block b of (token m,
+    // slot s) at float (m * (k+1) + s) * h_stride + 32 b, 16 pair words then
+    // the step (the workspace's h region; may be h itself)
+    float* hconv;           // null: the down kernel converts h itself
+    int hconv_stride;
     // down
     const uint8_t* down;
     size_t dn_expert_bytes;
@@ -177,6 +182,16 @@ bool stack_kernel_supported(const qmoe_dims& d, int M, int n_layers, int R);
 cudaError_t launch_stack_kernel(const void* x, float* out, unsigned char* sync, unsigned long long* trace,
                                 int* status, const qmoe_layer_weights* layers, int n_layers, const qmoe_dims& d,
                                 const XchgDesc* xc, const StackTraceBufs& tb, cudaStream_t stream);
+
+// The hyper-connection mixer (hc.cu).
+size_t hc_workspace_bytes(int M, int hc, int rank);
+size_t hc_down_smem(int M, int hc, int D);
+size_t hc_up_smem(int M, int rank);
+cudaError_t launch_hc_mix(const void* hyper, int f32, int M, int D, int hc, int rank, float eps,
+                          const float* norm_w, const float* down_w, const float* up_w, const float* inject_w,
+                          float* mixed, float* inject, unsigned char* ws, cudaStream_t s);
+cudaError_t launch_hc_reinject(const void* hyper, int h_f32, const void* branch, int b_f32, const float* inject,
+                               int M, int D, int hc, float* out, cudaStream_t s);
 
 // Prefill / large verify chunks (prefill.cu).
 int prefill_max_tokens();
@@ -244,7 +259,10 @@ __device__ __forceinline__ int warp_block_fp(float v, float* step) {
         const int k1 = k >> 1, k2 = k - k1;
         const float s1 = __uint_as_float((unsigned)(127 + k1) << 23);
         const float s2 = __uint_as_float((unsigned)(127 + k2) << 23);
-        q = __float2int_rn((v * s1) * s2);
+        // rint((v * s1) * s2) on the FMA pipe: the product is exact (powers of
+        // two) and below 2^15 in magnitude, so adding 1.5 * 2^23 rounds it to
+        // an integer in the low mantissa bits (round to nearest even).
+        q = __float_as_int(fmaf(v * s1, s2, 12582912.0f)) - 0x4B400000;
         st = E >= 14 ? __uint_as_float((unsigned)(E - 13) << 23) : __uint_as_float(1u << (E + 9));
     }
     const int hi = __shfl_down_sync(0xffffffffu, q, 16);

@@ -267,6 +267,35 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// The h rows of every (token, slot) to block floating point once, for the
+// down kernel's CTAs to copy (M > 1; with M = 1 each CTA converts its own).
+// A warp per 32-value block reads all of it before writing, so hconv may be
+// h itself.
+__global__ void __launch_bounds__(kWarps * 32) convert_h_kernel(ExpertArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int K1 = a.k + 1;
+    const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
+    const int nsbh = I_max >> 5;
+    const int i = blockIdx.x * kWarps + (threadIdx.x >> 5);
+    if (i >= a.M * K1 * nsbh) return;
+    const int b = i % nsbh, ms = i / nsbh, m = ms / K1, s = ms % K1;
+    int nv;
+    if (s < a.k) {
+        const int id = a.ids[m * a.k + s];
+        nv = (id >= a.e_lo && id < a.e_hi) ? (a.I_loc >> 5) : 0;
+    } else {
+        nv = (a.sh_down != nullptr && a.sh_I_loc > 0) ? (a.sh_I_loc >> 5) : 0;
+    }
+    const float v = b < nv ? a.h[(size_t)ms * a.h_stride + b * 32 + lane] : 0.0f;
+    float st;
+    const int pw = warp_block_fp(v, &st);
+    __syncwarp();
+    float* dst = a.hconv + (size_t)ms * a.hconv_stride + b * 32;
+    if (lane < 16) dst[lane] = __int_as_float(pw);
+    if (lane == 16) dst[16] = st;
+}
+
+// ---------------------------------------------------------------------------
 // down + weighted combine + gated shared expert.
 template <int MAXM>
 __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
@@ -305,16 +334,27 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
         s_nvalid[m][s] = nv;
     }
     __syncthreads();
-    convert_blocks<8>(
-        M * K1 * nsbh,
-        [&](int i, int ln) {
+    if (a.hconv) {
+        // converted once by convert_h_kernel: 16 pair words and the step per
+        // block; blocks past a slot's valid count were written as zeros
+        for (int i = warp; i < M * K1 * nsbh; i += kWarps) {
             const int b = i % nsbh, ms = i / nsbh;
-            return b < s_nvalid[ms / K1][ms % K1] ? a.h[(size_t)ms * a.h_stride + b * 32 + ln] : 0.0f;
-        },
-        [&](int i, int ln, int pw, float st) {
-            if (ln < 16) hq[(size_t)i * 16 + ln] = pw;
-            if (ln == 0) hs[i] = st;
-        });
+            const float* src = a.hconv + (size_t)ms * a.hconv_stride + b * 32;
+            if (lane < 16) hq[(size_t)i * 16 + lane] = __float_as_int(__ldcg(src + lane));
+            if (lane == 16) hs[i] = __ldcg(src + 16);
+        }
+    } else {
+        convert_blocks<8>(
+            M * K1 * nsbh,
+            [&](int i, int ln) {
+                const int b = i % nsbh, ms = i / nsbh;
+                return b < s_nvalid[ms / K1][ms % K1] ? a.h[(size_t)ms * a.h_stride + b * 32 + ln] : 0.0f;
+            },
+            [&](int i, int ln, int pw, float st) {
+                if (ln < 16) hq[(size_t)i * 16 + ln] = pw;
+                if (ln == 0) hs[i] = st;
+            });
+    }
     __syncthreads();
 
     const int nsb_r = a.dn_nseg * a.dn_nsub;
@@ -423,7 +463,10 @@ cudaError_t launch_gateup_m(const ExpertArgs& a, cudaStream_t s) {
     const size_t smem = (size_t)a.M * nsb * (16 * 4 + 4) + (size_t)(a.e_hi - a.e_lo) * 4;
     const int n_units = a.M * a.k + 1;
     const long tasks = (long)n_units * (a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc);
-    const unsigned grid = (unsigned)((tasks + kWarps - 1) / kWarps);
+    unsigned grid = (unsigned)((tasks + kWarps - 1) / kWarps);
+    // Several tokens: every CTA converts all of x and plans all the experts
+    // first, so a grid of a few CTAs per SM takes the row pairs in strides.
+    if (a.M > 1) grid = min(grid, (unsigned)device_sm_count() * 4u);
     const int sbl = (nsb + 31) / 32;
     switch (sbl) {
         case 1: return launch_with_smem(gateup_kernel<MAXM, 1>, grid, smem, a, s);
@@ -439,7 +482,16 @@ cudaError_t launch_down_m(const ExpertArgs& a, cudaStream_t s) {
     const size_t smem = (size_t)a.M * (a.k + 1) * (I_max >> 5) * (16 * 4 + 4) +
                         (size_t)(a.e_hi - a.e_lo) * 4;
     const unsigned grid = (unsigned)((a.D + kWarps - 1) / kWarps);
-    return launch_with_smem(down_kernel<MAXM>, grid, smem, a, s);
+    if (a.M > 1 && a.hconv) {
+        const int nb = a.M * (a.k + 1) * (I_max >> 5);
+        convert_h_kernel<<<(unsigned)((nb + kWarps - 1) / kWarps), kWarps * 32, 0, s>>>(a);
+        cudaError_t err = cudaGetLastError();
+        if (err != cudaSuccess) return err;
+        return launch_with_smem(down_kernel<MAXM>, grid, smem, a, s);
+    }
+    ExpertArgs b = a;
+    b.hconv = nullptr;
+    return launch_with_smem(down_kernel<MAXM>, grid, smem, b, s);
 }
 
 }  // namespace

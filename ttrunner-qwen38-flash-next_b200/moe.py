@@ -10,11 +10,13 @@ caller all-reduces).  Its stages are exposed as the reference's operators:
   moe_block(x, router_w, gate_w, up_w, ...) tt/moe.py:159   -> routed output
   shared_expert(x, gate_w, up_w, down_w, g) tt/moe.py:983   -> shared output
 
-Differences from the reference, by design: routing is exact top-k with ties
-to the lower expert id (the reference's device kernel in EXACT_TOPK mode,
-scripts/kernels/router_select.cpp:198-222; its ttnn threshold chain admits
-ties), and errors raise `QMoEError` instead of warning and falling back
-(tt/moe.py:264-271) -- there is no fallback path.
+Routing is exact top-k with ties to the lower expert id by default (the
+reference's device kernel in EXACT_TOPK mode, scripts/kernels/router_select.cpp
+:198-222, and its CPU model); `route_mode="threshold"` / `"threshold_bf16"`
+selects the tie-admitting mode of the same kernel (:223-255) and of the ttnn
+chain (tt/moe.py:308-327), with up to 16 experts per token.  Errors raise
+`QMoEError` instead of warning and falling back (tt/moe.py:264-271) -- there is
+no fallback path.
 
 IQ4_XS operands are uint8 tensors of GGUF bytes: gate_w [E, I, D/256*136]
 (or the fused gate|up [E, 2I, D/256*136] with up_w None, as
@@ -132,14 +134,31 @@ def _act(x: torch.Tensor) -> tuple[torch.Tensor, int]:
 class MoELayer:
     """One MoE block resident in HBM (one shard of it)."""
 
-    def __init__(self, layer: DeviceLayer, max_tokens: int | None = None):
+    ROUTE_MODES = ("exact", "threshold", "threshold_bf16")
+
+    def __init__(self, layer: DeviceLayer, max_tokens: int | None = None, route_mode: str = "exact",
+                 k_sel: int = 16):
+        """route_mode: "exact" top-k, or the tie-admitting threshold select at the top_k-th
+        probability in fp32 ("threshold") or bf16 ("threshold_bf16") with k_sel slots."""
+        if route_mode not in self.ROUTE_MODES:
+            raise ValueError(f"route_mode {route_mode!r} not in {self.ROUTE_MODES}")
         self.layer = layer
         self.cfg: MoEConfig = layer.cfg
         self.shard: Shard = layer.shard
+        self.route_mode = route_mode
         self.dims = layer.shard.dims(layer.cfg)
+        if route_mode != "exact":
+            if not layer.cfg.top_k <= k_sel <= 16:
+                raise ValueError(f"k_sel {k_sel} outside [top_k, 16]")
+            self.dims.top_k = k_sel  # the slots the experts see
         self.max_tokens = max_tokens or lib.qmoe_max_tokens()
         self.weights = layer.c_struct()
         self.ws = workspace_for(self.dims, self.max_tokens, layer.router.device)
+
+    @property
+    def slots(self) -> int:
+        """Routed slots per token: top_k, or k_sel in a threshold mode."""
+        return self.dims.top_k
 
     def _m(self, x: torch.Tensor) -> int:
         m = x.shape[0]
@@ -154,6 +173,13 @@ class MoELayer:
         x2, dt = _act(x)
         m = self._m(x2)
         given = out is not None
+        if self.route_mode != "exact":
+            ids, w, sl = self.route(x2)
+            y = self.down(self.gate_up(x2, ids), ids, w, sl)
+            if given:
+                out.view(m, self.cfg.hidden).copy_(y)
+                return out
+            return _shaped(y, x, out_dtype)
         if out is None:
             out = torch.empty(m, self.cfg.hidden, dtype=torch.float32, device=x2.device)
         check(lib.qmoe_moe_block(x2.data_ptr(), dt, m, ctypes.byref(self.weights), ctypes.byref(self.dims),
@@ -204,16 +230,22 @@ class MoELayer:
         return out
 
     def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        """(ids [M, k] int32, weights [M, k] fp32, shared_logit [M] fp32)."""
+        """(ids [M, slots] int32, weights [M, slots] fp32, shared_logit [M] fp32)."""
         x2, dt = _act(x)
         m = self._m(x2)
-        k = self.cfg.top_k
+        k = self.slots
         ids = torch.empty(m, k, dtype=torch.int32, device=x2.device)
         w = torch.empty(m, k, dtype=torch.float32, device=x2.device)
         sl = torch.empty(m, dtype=torch.float32, device=x2.device)
-        check(lib.qmoe_route(x2.data_ptr(), dt, m, ctypes.byref(self.weights), ctypes.byref(self.dims),
-                             ids.data_ptr(), w.data_ptr(), sl.data_ptr(), self.ws.ptr, self.ws.nbytes,
-                             _stream()), "qmoe_route")
+        if self.route_mode == "exact":
+            check(lib.qmoe_route(x2.data_ptr(), dt, m, ctypes.byref(self.weights), ctypes.byref(self.dims),
+                                 ids.data_ptr(), w.data_ptr(), sl.data_ptr(), self.ws.ptr, self.ws.nbytes,
+                                 _stream()), "qmoe_route")
+        else:
+            check(lib.qmoe_route_threshold(x2.data_ptr(), dt, m, ctypes.byref(self.weights), ctypes.byref(self.dims),
+                                           self.cfg.top_k, int(self.route_mode == "threshold_bf16"), ids.data_ptr(),
+                                           w.data_ptr(), sl.data_ptr(), self.ws.ptr, self.ws.nbytes, _stream()),
+                  "qmoe_route_threshold")
         return ids, w, sl
 
     def gate_up(self, x: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
@@ -221,7 +253,7 @@ class MoELayer:
         x2, dt = _act(x)
         m = self._m(x2)
         hs = max(self.dims.inter_local, self.dims.sh_inter_local)
-        h = torch.zeros(m, self.cfg.top_k + 1, hs, dtype=torch.float32, device=x2.device)
+        h = torch.zeros(m, self.slots + 1, hs, dtype=torch.float32, device=x2.device)
         ids = ids.to(torch.int32).contiguous()
         check(lib.qmoe_gateup_swiglu(x2.data_ptr(), dt, m, ids.data_ptr(), ctypes.byref(self.weights),
                                      ctypes.byref(self.dims), h.data_ptr(), hs, self.ws.ptr,
@@ -339,14 +371,52 @@ def route_topk(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[tor
     return ids, wt
 
 
-def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]:
+def route_threshold(x: torch.Tensor, router_w: torch.Tensor, top_k: int, k_sel: int = 16,
+                    probs_bf16: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """The tie-admitting select (router_select.cpp:223-255, TT_ROUTER_EXACT_TOPK=0): (ids [M, k_sel]
+    int32, weights [M, k_sel] fp32), every expert at or above the top_k-th probability (bf16 when
+    probs_bf16, as the ttnn chain compares them), largest first, ties to the lower id, renormalised
+    over all of them; unused slots are (0, 0)."""
+    x2, dt = _act(x)
+    m = x2.shape[0]
+    E, D = router_w.shape
+    dims = _raw_dims(D, 256, E, k_sel)
+    r_w = router_w.float().contiguous()
+    w = LayerWeights(router=r_w.data_ptr())
+    ids = torch.empty(m, k_sel, dtype=torch.int32, device=x2.device)
+    wt = torch.empty(m, k_sel, dtype=torch.float32, device=x2.device)
+    if m > lib.qmoe_max_tokens():  # a prefill chunk
+        pws = prefill_workspace_for(dims, m, x2.device)
+        check(lib.qmoe_prefill_route_threshold(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), top_k,
+                                               int(probs_bf16), ids.data_ptr(), wt.data_ptr(), None, pws.ptr,
+                                               pws.nbytes, _stream()), "route_threshold")
+        return ids, wt
+    ws = workspace_for(dims, max(m, 1), x2.device)
+    check(lib.qmoe_route_threshold(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), top_k,
+                                   int(probs_bf16), ids.data_ptr(), wt.data_ptr(), None, ws.ptr, ws.nbytes,
+                                   _stream()), "route_threshold")
+    return ids, wt
+
+
+def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int,
+          mode: str = "exact") -> tuple[torch.Tensor, torch.Tensor]:
     """Dense routing as tt/moe.py:308-327 returns it: (weights, keep), both with x's leading shape
-    and E last ([1, 1, M, E] for the reference's [1, 1, M, K] activations)."""
-    ids, wt = route_topk(x, router_w, top_k)
+    and E last ([1, 1, M, E] for the reference's [1, 1, M, K] activations).  mode "exact": the top_k
+    (the reference's default device select); "threshold_bf16": the ttnn chain's own rule, every
+    probability >= the top_k-th in bf16 kept (up to 16); "threshold": the same on fp32 probabilities."""
+    if mode == "exact":
+        ids, wt = route_topk(x, router_w, top_k)
+    elif mode in ("threshold", "threshold_bf16"):
+        ids, wt = route_threshold(x, router_w, top_k, 16, mode == "threshold_bf16")
+    else:
+        raise ValueError(f"route mode {mode!r}")
     E = router_w.shape[0]
     dense = torch.zeros(ids.shape[0], E, dtype=torch.float32, device=ids.device)
-    dense.scatter_(1, ids.long(), wt)
-    keep = torch.zeros_like(dense).scatter_(1, ids.long(), 1.0)
+    dense.scatter_add_(1, ids.long(), wt)
+    if mode == "exact":
+        keep = torch.zeros_like(dense).scatter_(1, ids.long(), 1.0)
+    else:  # the padding slots (id 0, weight 0) keep nothing
+        keep = (dense > 0).float()
     lead = x.shape[:-1]
     return dense.view(*lead, E), keep.view(*lead, E)
 
