@@ -46,7 +46,7 @@ FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per layer of the single-launch stack
 # kernel, from one ncu capture of a 2-layer stack of the same shape; traffic grows with the layer
 # count, so a launch of n layers moves n times this.
-STACK_TRAFFIC_PER_LAYER_B = (45_320_192 + 189_184) // 2
+STACK_TRAFFIC_PER_LAYER_B = (45_254_656 + 178_688) // 2
 
 
 def peaks() -> tuple[float, str]:
