@@ -189,6 +189,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill timings")
     ap.add_argument("--no-verify", action="store_true", help="skip the config-3 verify-chunk timings")
+    ap.add_argument("--no-formats", action="store_true", help="skip the checkpoint-format block timings")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -285,6 +286,7 @@ def main() -> None:
     stage = stage_timings(pkg, layers, xs[0], M, dev, reps=2)
     prefill = prefill_timings(pkg, layers[0], cfg, dev) if world == 1 and not args.no_prefill else None
     verify = verify_timings(pkg, layers, cfg, dev) if world == 1 and M == 1 and not args.no_verify else None
+    formats = formats_timings(pkg, cfg, dev) if world == 1 and M == 1 and not args.no_formats else None
 
     if world > 1:
         t = torch.tensor([ms, ms_e2e, float(device_status != 0)], dtype=torch.float64, device=dev)
@@ -345,6 +347,7 @@ def main() -> None:
             "per_layer_path_stage_us": {k: round(v, 3) for k, v in stage.items()},
             "prefill_config4": prefill,
             "verify_config3": verify,
+            "formats_block": formats,
             "clocks": clocks,
             "device_status": device_status,
         }
@@ -456,6 +459,72 @@ def prefill_timings(pkg, layer, cfg, dev, chunks=(128, 2048), steps: int = 10, w
             "frac_of_measured_bf16": round(flops / (us * 1e-6) / 1e12 / tflops_peak, 4),
         })
         del xs
+    return out
+
+
+def formats_timings(pkg, cfg, dev, tokens=(1, 4), n_layers: int = 4, steps: int = 24, warmup: int = 4) -> list:
+    """The MoE block on the real checkpoint's format mix (IQ3_S gate|up, IQ4_NL down, IQ3_S gate|up
+    and Q8_0 down of the shared expert; tt/plan.py:90-103) at the config's dimensions, through the C
+    ABI (`qmoe_moe_block_formats`).  Weights are random block bytes with a fixed fp16 scale, made on
+    the device (4 layers, 3 GB, rotated per step so each step reads its experts from HBM); bytes =
+    the rows of the k routed experts and the shared expert + the router."""
+    import torch
+
+    bb = {8: 34, 20: 18, 21: 110}
+    bv = {8: 32, 20: 32, 21: 256}
+    E, D, I, Ish = cfg.n_experts, cfg.hidden, cfg.inter, cfg.shared_inter
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+
+    def blocks(fmt, rows, vals):
+        nb = rows * vals // bv[fmt]
+        t = torch.randint(0, 256, (nb, bb[fmt]), dtype=torch.uint8, device=dev, generator=gen)
+        t[:, 0:2] = torch.full((nb, 1), 2e-4, dtype=torch.float16, device=dev).view(torch.uint8)
+        return t.view(rows, vals // bv[fmt] * bb[fmt])
+
+    lays = []
+    for _ in range(n_layers):
+        lays.append(dict(
+            router=torch.randn(E, D, device=dev, generator=gen) * 0.02,
+            gate_vec=torch.randn(D, device=dev, generator=gen) * 0.02,
+            gate_up=blocks(21, E * 2 * I, D).view(E, 2 * I, -1), down=blocks(20, E * D, I).view(E, D, -1),
+            sh_gate_up=blocks(21, 2 * Ish, D), sh_down=blocks(8, D, Ish)))
+    fmts = (21, 20, 21, 8)
+    row_b = 2 * I * (D // 256 * 110) + D * (I // 32 * 18)
+    sh_b = 2 * Ish * (D // 256 * 110) + D * (Ish // 32 * 34)
+    hbm = peaks()[0]
+    out = []
+    for M in tokens:
+        xs = [(torch.randn(M, D, device=dev, generator=gen)).to(torch.bfloat16) for _ in range(warmup + steps)]
+
+        def run(i):
+            L = lays[i % n_layers]
+            return pkg.moe_block_formats(xs[i], L["router"], L["gate_vec"], L["gate_up"], L["down"],
+                                         L["sh_gate_up"], L["sh_down"], fmts, cfg.top_k)
+
+        for i in range(warmup):
+            run(i)
+        touched = 0
+        for i in range(steps):
+            L = lays[(warmup + i) % n_layers]
+            logits = xs[warmup + i].float() @ L["router"].t()
+            touched += int(torch.unique(logits.topk(cfg.top_k, dim=-1).indices).numel())
+        torch.cuda.synchronize(dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record()
+        for i in range(steps):
+            run(warmup + i)
+        ev[1].record()
+        torch.cuda.synchronize(dev)
+        us = ev[0].elapsed_time(ev[1]) * 1000.0 / steps
+        nbytes = touched / steps * row_b + sh_b + E * D * 4
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out.append({"tokens": M, "us_per_layer": round(us, 2), "bytes_per_layer": int(nbytes),
+                    "achieved_gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm, 4),
+                    "launches_per_layer": 3})
+        del xs
+    del lays
+    torch.cuda.empty_cache()
     return out
 
 

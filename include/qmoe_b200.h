@@ -365,6 +365,44 @@ int qmoe_prefill(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weig
                  const qmoe_dims* dims, float* out, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* ---- the real checkpoint's other expert formats ---------------------------- */
+/* GGML block formats by their GGML type ids (the reference's gguf/reader.py:53-74):
+ * Q8_0 (32 values, 34 bytes), IQ4_NL (32, 18), IQ3_S (256, 110), IQ4_XS (256, 136).
+ * The reference's checkpoint stores gate|up as IQ3_S and down as IQ4_NL, or
+ * Q8_0 in its first layers (tt/plan.py:90-103). */
+enum qmoe_format {
+    QMOE_FMT_Q8_0 = 8,
+    QMOE_FMT_IQ4_NL = 20,
+    QMOE_FMT_IQ3_S = 21,
+    QMOE_FMT_IQ4_XS = 23
+};
+
+/* The format of each expert tensor of a layer. */
+typedef struct qmoe_formats {
+    int gate_up;     /* routed experts' fused gate|up rows  */
+    int down;        /* routed experts' down rows           */
+    int sh_gate_up;  /* shared expert's gate|up rows        */
+    int sh_down;     /* shared expert's down rows           */
+} qmoe_formats;
+
+/* Bytes of a row of n_values values in `format`; 0 when n_values is not a
+ * whole number of its blocks or the format is unknown. */
+size_t qmoe_format_row_bytes(int format, int64_t n_values);
+/* Decode n_values values of `format` to fp32, bitwise the reference's
+ * gguf.quants.dequantize (quants.py:33-37 Q8_0, :100-108 IQ4_NL, :112-129
+ * IQ4_XS, :132-165 IQ3_S).  blocks 16-byte aligned; out fp32 16-byte aligned. */
+int qmoe_dequant_f32(int format, const void* blocks, int64_t n_values, float* out, void* stream);
+/* The MoE block (as qmoe_moe_block: routed experts + gated shared expert,
+ * reference/model.py:387-417) on expert tensors of the given formats, laid
+ * out as the IQ4_XS ones are (gate_up [E][2I rows], down [E][D rows], rows of
+ * qmoe_format_row_bytes bytes).  Unsharded dims only (the whole expert range
+ * and intermediate width); shared expert optional (sh_inter_local = 0).
+ * Routing is the exact top-k; each 32-value block is decoded with the
+ * reference's arithmetic and dotted in fp32.  out [M, hidden] fp32. */
+int qmoe_moe_block_formats(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                           const qmoe_dims* dims, const qmoe_formats* formats, float* out,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- the hyper-connection mixer around the block ------------------------ */
 /* The reference's gated residual (reference/model.py:53-81; device ops
  * tt/ops.py:2627 gated_residual_mix and :2825 reinject): the MoE block reads

@@ -36,7 +36,8 @@ _SO = HERE / "liboracle_iq4xs.so"
 
 def build() -> Path:
     """Compile the C restatements (make in this directory)."""
-    srcs = [HERE / "iq4xs_ref.c", HERE / "synth_ref.c", HERE / "Makefile"]
+    srcs = [HERE / "iq4xs_ref.c", HERE / "synth_ref.c", HERE / "formats_ref.c", HERE / "iq3s_grid.inc",
+            HERE / "Makefile"]
     if not _SO.exists() or any(_SO.stat().st_mtime < s.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return _SO
@@ -57,6 +58,8 @@ def _c() -> ctypes.CDLL:
             fn.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p]
         _lib.oracle_quantize_iq4xs.restype = None
         _lib.oracle_quantize_iq4xs.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+        _lib.oracle_dequant.restype = ctypes.c_int
+        _lib.oracle_dequant.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
     return _lib
 
 
@@ -93,6 +96,63 @@ def dequant_iq4xs(raw: np.ndarray) -> np.ndarray:
     out = np.empty(raw.shape[:-1] + (raw.shape[-1] // 136 * 256,), dtype=np.float32)
     _c().oracle_dequant_iq4xs(raw.ctypes.data, nb, out.ctypes.data)
     return out
+
+
+# GGML type ids and block traits (gguf/reader.py:53-74, 85-108): (values, bytes) per block.
+Q8_0, IQ4_NL, IQ3_S, IQ4_XS = 8, 20, 21, 23
+BLOCK = {Q8_0: (32, 34), IQ4_NL: (32, 18), IQ3_S: (256, 110), IQ4_XS: (256, 136)}
+
+
+def row_bytes(fmt: int, n_values: int) -> int:
+    bv, bb = BLOCK[fmt]
+    if n_values % bv:
+        raise ValueError(f"{n_values} values is not a whole number of blocks of format {fmt}")
+    return n_values // bv * bb
+
+
+def dequant(fmt: int, raw: np.ndarray) -> np.ndarray:
+    """Bytes [..., row bytes] of `fmt` -> fp32 [..., values] (quants.py; formats_ref.c)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    bv, bb = BLOCK[fmt]
+    if raw.shape[-1] % bb:
+        raise ValueError("last dimension is not a whole number of blocks")
+    n = raw.size // bb * bv
+    out = np.empty(raw.shape[:-1] + (raw.shape[-1] // bb * bv,), dtype=np.float32)
+    if _c().oracle_dequant(fmt, raw.ctypes.data, ctypes.c_int64(n), out.ctypes.data) != 0:
+        raise ValueError(f"format {fmt}")
+    return out
+
+
+def synth_format_bytes(fmt: int, seed: int, sid: int, n_rows: int, row_values: int,
+                       d_scale: float) -> np.ndarray:
+    """Seeded bytes of `fmt` [n_rows, row bytes]: every byte from the exact-arithmetic generator's
+    stream, then each block's fp16 scale set to d_scale * (1 + |z| / 2) so the decoded weights have
+    the magnitude of N(0, 0.02) weights (no quantiser exists here for these formats; the
+    reference decodes whatever bytes it is given)."""
+    rb = row_bytes(fmt, row_values)
+    n = n_rows * rb
+    u = np.abs(synth_f32(seed, sid, n, 1.0)).astype(np.float64)
+    raw = (np.floor(u * 1e6).astype(np.int64) % 256).astype(np.uint8).reshape(n_rows, rb)
+    bv, bb = BLOCK[fmt]
+    z = np.abs(synth_f32(seed, sid + 1000, n_rows * (rb // bb), 1.0)).reshape(n_rows, rb // bb)
+    d = (np.float32(d_scale) * (np.float32(1.0) + z / np.float32(2.0))).astype(np.float16)
+    blocks = raw.reshape(n_rows, rb // bb, bb)
+    blocks[:, :, 0:2] = d.view(np.uint8).reshape(n_rows, rb // bb, 2)
+    return blocks.reshape(n_rows, rb)
+
+
+def synth_formats_layer(seed: int, E: int, D: int, I: int, Ish: int) -> dict:
+    """A seeded layer in the real checkpoint's format mix: IQ3_S gate|up [E, 2I, ...], IQ4_NL down
+    [E, D, ...], IQ3_S shared gate|up, Q8_0 shared down, fp32 router and gate vector."""
+    return {
+        "formats": (IQ3_S, IQ4_NL, IQ3_S, Q8_0),
+        "gate_up": synth_format_bytes(IQ3_S, seed, 1, E * 2 * I, D, 2e-4).reshape(E, 2 * I, -1),
+        "down": synth_format_bytes(IQ4_NL, seed, 2, E * D, I, 2e-4).reshape(E, D, -1),
+        "sh_gate_up": synth_format_bytes(IQ3_S, seed, 3, 2 * Ish, D, 2e-4),
+        "sh_down": synth_format_bytes(Q8_0, seed, 4, D, Ish, 2e-4),
+        "router": synth_f32(seed, 5, E * D, 0.02).reshape(E, D),
+        "gate_vec": synth_f32(seed, 6, D, 0.02),
+    }
 
 
 def dequant_iq4xs_numpy(raw: np.ndarray) -> np.ndarray:
@@ -224,7 +284,10 @@ class ExpertSource:
     bytes (gate|up [2I, rb], down [D, rb_dn]) and are decoded on each use."""
 
     def __init__(self, expert, sh_gate_up: np.ndarray | None, sh_down: np.ndarray | None,
-                 router: np.ndarray, gate_vec: np.ndarray | None, inter: int, shared_inter: int):
+                 router: np.ndarray, gate_vec: np.ndarray | None, inter: int, shared_inter: int,
+                 formats: tuple[int, int, int, int] = (23, 23, 23, 23)):
+        """formats: GGML types of (gate|up, down, shared gate|up, shared down); IQ4_XS by default."""
+        self.formats = formats
         self.expert = expert
         self.sh_gate_up = sh_gate_up
         self.sh_down = sh_down
@@ -256,11 +319,12 @@ def moe_forward(x: np.ndarray, src: ExpertSource, k: int, with_shared: bool = Tr
     """
 
     def dq(key, gu_b, dn_b):
+        fg, fd = src.formats[2:4] if key == "shared" else src.formats[0:2]
         if cache is None:
-            return dequant_iq4xs(gu_b), dequant_iq4xs(dn_b)
+            return dequant(fg, gu_b), dequant(fd, dn_b)
         got = cache.get(key)
         if got is None:
-            got = cache[key] = (dequant_iq4xs(gu_b), dequant_iq4xs(dn_b))
+            got = cache[key] = (dequant(fg, gu_b), dequant(fd, dn_b))
         return got
 
     x = np.ascontiguousarray(x, dtype=np.float32)

@@ -24,6 +24,10 @@ What it records (all small, committed as .npz):
     c1_m1               BASELINE config 1: hidden 2048, inter 512, 512 experts
     c1_m4, c1_m8        the config-3 token counts through one config-1 layer
     tie_m2              a router whose 64 rows are identical: every logit ties.
+    formats_*           the real checkpoint's other expert formats (`make_golden.py
+                        formats`): the reference's dequantize of Q8_0, IQ4_NL
+                        and IQ3_S bytes, and its _moe on a layer of IQ3_S
+                        gate|up, IQ4_NL down and a Q8_0 shared down.
     hc_small, hc_c1     the hyper-connection mixer around the block
                         (reference/model.py:53-81; `make_golden.py hc` makes
                         these alone): 4 streams of hidden 512 / 2048, low rank
@@ -216,7 +220,66 @@ def hc_fixture(name: str, hidden: int, hc: int, rank: int, m: int, seed: int) ->
     print(f"hc_{name}: mixed[0,:3] {mixed.reshape(m, hidden)[0, :3].tolist()} inject[0] {inject.reshape(m, hc)[0].tolist()}")
 
 
+# The real checkpoint's other expert formats (gguf/quants.py): GGML type ids.
+FORMATS = {"Q8_0": GGMLType.Q8_0, "IQ4_NL": GGMLType.IQ4_NL, "IQ3_S": GGMLType.IQ3_S}
+# The formats' MoE fixture: IQ3_S gate|up, IQ4_NL down (tt/plan.py:90-103), Q8_0 shared down.
+FMT_SEED = 41
+
+
+def formats_dequant_fixture() -> None:
+    """The reference's dequantize on seeded bytes of Q8_0, IQ4_NL and IQ3_S (a few blocks with
+    non-finite or zero scales)."""
+    from oracle import moe_ref
+
+    out = {}
+    for i, (name, t) in enumerate(FORMATS.items()):
+        bv, bb = moe_ref.BLOCK[int(t)]
+        nblk = 48
+        raw = moe_ref.synth_format_bytes(int(t), 90 + i, 1, 1, nblk * bv, 0.01)[0].copy()
+        for b, h in ((3, 0x7C00), (7, 0xFE00), (11, 0x0000), (13, 0x8001)):  # inf, nan, zero, -subnormal
+            raw[b * bb:b * bb + 2] = np.array([h & 0xFF, h >> 8], dtype=np.uint8)
+        ref = dequantize(memoryview(raw.tobytes()), t, nblk * bv)
+        out[f"{name}_raw"], out[f"{name}_out"] = raw, ref
+    np.savez_compressed(HERE / "formats_dequant.npz", **out)
+    print("formats_dequant:", {k: v.shape for k, v in out.items()})
+
+
+def formats_moe_fixture() -> None:
+    """One small layer with the real checkpoint's format mix through the reference's _moe."""
+    from oracle import moe_ref
+
+    small = pkg.MoEConfig(hidden=512, inter=256, n_experts=64, top_k=10, shared_inter=256)
+    E, D, I, Ish = small.n_experts, small.hidden, small.inter, small.shared_inter
+    lay = moe_ref.synth_formats_layer(FMT_SEED, E, D, I, Ish)
+    gu, dn, sgu, sdn = lay["gate_up"], lay["down"], lay["sh_gate_up"], lay["sh_down"]
+    router, gate_vec = lay["router"], lay["gate_vec"]
+    g = FakeGGUF()
+    p = "blk.0."
+    for name, shape, t, raw in (
+        ("ffn_gate_inp.weight", (E, D), GGMLType.F32, router),
+        ("ffn_gate_inp_shexp.weight", (D,), GGMLType.F32, gate_vec),
+        ("ffn_gate_shexp.weight", (Ish, D), GGMLType.IQ3_S, sgu[:Ish]),
+        ("ffn_up_shexp.weight", (Ish, D), GGMLType.IQ3_S, sgu[Ish:]),
+        ("ffn_down_shexp.weight", (D, Ish), GGMLType.Q8_0, sdn),
+        ("ffn_gate_exps.weight", (E, I, D), GGMLType.IQ3_S, gu[:, :I]),
+        ("ffn_up_exps.weight", (E, I, D), GGMLType.IQ3_S, gu[:, I:]),
+        ("ffn_down_exps.weight", (E, D, I), GGMLType.IQ4_NL, dn),
+    ):
+        g.add(p + name, shape, t, raw)
+    model = Qwen4ExpModel(make_config(small), WeightStore(g))
+    for m in (1, 4):
+        x = pkg.synth_x(small, m, seed=FMT_SEED)
+        out = model._moe(x.float().reshape(1, m, D), 0).reshape(m, D).numpy()
+        np.savez_compressed(HERE / f"formats_moe_m{m}.npz", seed=FMT_SEED, n_tokens=m,
+                            x_bf16=x.view(torch.int16).numpy(), out=out)
+        print(f"formats_moe_m{m}: out[0,:3] {out[0, :3]}")
+
+
 def main() -> None:
+    if len(sys.argv) > 1 and sys.argv[1] == "formats":
+        formats_dequant_fixture()
+        formats_moe_fixture()
+        return
     if len(sys.argv) > 1 and sys.argv[1] == "hc":
         hc_fixture("small", 512, 4, 64, 2, 21)
         hc_fixture("c1", 2048, 4, 32, 1, 22)

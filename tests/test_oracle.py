@@ -200,3 +200,29 @@ def test_hc_oracle_matches_reference_fixture(name):
     for got, ref in ((o["mixed"], g["mixed"]), (o["inject"], g["inject"]),
                      (hc_ref.reinject(hyper, branch, o["inject"]), g["reinjected"])):
         assert float(np.abs(got - ref).max() / np.abs(ref).max()) < 1e-6
+
+
+def test_format_oracles_match_reference_dequant(oracle):
+    """oracle/formats_ref.c (Q8_0, IQ4_NL, IQ3_S) bit for bit against the reference's dequantize,
+    non-finite and zero scales included."""
+    g = load_golden("formats_dequant.npz")
+    for name, fmt in (("Q8_0", oracle.Q8_0), ("IQ4_NL", oracle.IQ4_NL), ("IQ3_S", oracle.IQ3_S)):
+        got = oracle.dequant(fmt, g[f"{name}_raw"].reshape(1, -1))[0]
+        ref = g[f"{name}_out"]
+        assert np.array_equal(got.view(np.uint32)[np.isfinite(ref)], ref.view(np.uint32)[np.isfinite(ref)]), name
+        assert np.array_equal(np.isnan(got), np.isnan(ref)) and np.array_equal(np.isinf(got), np.isinf(ref)), name
+
+
+@pytest.mark.parametrize("m", [1, 4])
+def test_format_moe_oracle_matches_reference(oracle, m):
+    """The oracle's _moe on a layer of IQ3_S gate|up, IQ4_NL down and a Q8_0 shared down against
+    the reference's own _moe on the same bytes."""
+    import torch
+
+    g = load_golden(f"formats_moe_m{m}.npz")
+    lay = oracle.synth_formats_layer(int(g["seed"]), 64, 512, 256, 256)
+    src = oracle.ExpertSource(lambda e: (lay["gate_up"][e], lay["down"][e]), lay["sh_gate_up"], lay["sh_down"],
+                              lay["router"], lay["gate_vec"], 256, 256, formats=lay["formats"])
+    x = torch.from_numpy(g["x_bf16"]).view(torch.bfloat16).float().numpy()
+    got = oracle.moe_forward(x, src, 10)["out"]
+    assert oracle.max_rel_err(got, g["out"]) < 1e-5

@@ -17,6 +17,8 @@ from .moe import (
     apply_experts,
     moe_block,
     route,
+    dequant,
+    moe_block_formats,
     route_threshold,
     route_topk,
     shared_expert,
@@ -39,4 +41,6 @@ __all__ = [
     "route_threshold",
     "gated_residual_mix",
     "reinject",
+    "dequant",
+    "moe_block_formats",
 ]

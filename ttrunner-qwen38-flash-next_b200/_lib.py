@@ -74,6 +74,15 @@ class Xchg(ctypes.Structure):
     ]
 
 
+class Formats(ctypes.Structure):
+    """qmoe_formats: GGML type ids of a layer's expert tensors."""
+
+    _fields_ = [("gate_up", c_int), ("down", c_int), ("sh_gate_up", c_int), ("sh_down", c_int)]
+
+
+QMOE_FMT_Q8_0, QMOE_FMT_IQ4_NL, QMOE_FMT_IQ3_S, QMOE_FMT_IQ4_XS = 8, 20, 21, 23
+
+
 class HcWeights(ctypes.Structure):
     """qmoe_hc_weights: the hyper-connection mixer's fp32 weights."""
 
@@ -144,6 +153,10 @@ _SIGS = {
                                        _P, c_size_t, _P]),
     "qmoe_moe_block_noalloc": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P]),
     "qmoe_noalloc_read_status": (c_int, [POINTER(c_int), _P]),
+    "qmoe_format_row_bytes": (c_size_t, [c_int, c_int64]),
+    "qmoe_dequant_f32": (c_int, [c_int, _P, c_int64, _P, _P]),
+    "qmoe_moe_block_formats": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), POINTER(Formats), _P,
+                                       _P, c_size_t, _P]),
     "qmoe_hc_workspace_bytes": (c_size_t, [POINTER(HcDims), c_int]),
     "qmoe_hc_mix": (c_int, [_P, c_int, c_int, POINTER(HcWeights), POINTER(HcDims), _P, _P, _P, c_size_t, _P]),
     "qmoe_hc_reinject": (c_int, [_P, c_int, _P, c_int, _P, c_int, POINTER(HcDims), _P, _P]),

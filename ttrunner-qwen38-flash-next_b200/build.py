@@ -25,7 +25,7 @@ LIB = HERE / "libqmoe_b200.so"
 OBJ = HERE / "_build"
 
 CUDA_SOURCES = ["iq4xs_kernels.cu", "route.cu", "experts.cu", "capi.cu", "noalloc.cu", "stack_kernel.cu", "prefill.cu",
-                "hc.cu"]
+                "hc.cu", "formats.cu"]
 HOST_SOURCES = ["quant_host.cpp"]
 
 NVCC_FLAGS = [

@@ -724,6 +724,43 @@ int qmoe_hc_reinject(const void* hyper, int hyper_dtype, const void* branch, int
                                           inject, n_tokens, dims->hidden, dims->hc, out, (cudaStream_t)stream));
 }
 
+size_t qmoe_format_row_bytes(int format, int64_t n_values) {
+    return n_values > 0 ? fmt_row_bytes(format, n_values) : 0;
+}
+
+int qmoe_dequant_f32(int format, const void* blocks, int64_t n_values, float* out, void* stream) {
+    if (!blocks || !out || n_values < 0 || (n_values > 0 && fmt_row_bytes(format, n_values) == 0))
+        return QMOE_ERR_INVALID_ARG;
+    if (!aligned(blocks, 16) || !aligned(out, 16)) return QMOE_ERR_ALIGNMENT;
+    if (n_values == 0) return QMOE_OK;
+    return cuda_status(launch_fmt_dequant(format, (const uint8_t*)blocks, n_values, out, (cudaStream_t)stream));
+}
+
+int qmoe_moe_block_formats(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
+                           const qmoe_dims* dims, const qmoe_formats* f, float* out, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+    QMOE_TRY(check_dims(dims));
+    QMOE_TRY(check_tokens(n_tokens));
+    QMOE_TRY(check_act(x, x_dtype));
+    QMOE_TRY(check_weights_route(w));
+    QMOE_TRY(route_smem_ok(n_tokens, dims->hidden));
+    if (!f || !out || !w->gate_up || !w->down) return QMOE_ERR_INVALID_ARG;
+    if (dims->expert_lo != 0 || dims->expert_hi != dims->n_experts || dims->inter_local != dims->inter)
+        return QMOE_ERR_UNSUPPORTED;
+    const bool sh = dims->sh_inter_local > 0;
+    if (fmt_row_bytes(f->gate_up, dims->hidden) == 0 || fmt_row_bytes(f->down, dims->inter) == 0 ||
+        (sh && (fmt_row_bytes(f->sh_gate_up, dims->hidden) == 0 ||
+                fmt_row_bytes(f->sh_down, dims->sh_inter_local) == 0 || !w->sh_gate_up || !w->sh_down)))
+        return QMOE_ERR_INVALID_ARG;
+    if (dims->inter % 32 || (sh && dims->sh_inter_local % 32)) return QMOE_ERR_UNSUPPORTED;
+    Ws ws;
+    QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
+    cudaStream_t s = (cudaStream_t)stream;
+    QMOE_TRY(run_route(x, x_dtype, n_tokens, w, dims, ws.ids(), ws.weights(), ws.shared(), ws, s));
+    return cuda_status(launch_fmt_experts(x, x_dtype == QMOE_ACT_F32, n_tokens, *dims, *f, *w, ws.ids(),
+                                          ws.weights(), ws.shared(), ws.h(), ws.L.h_stride, out, ws.status(), s));
+}
+
 int qmoe_prefill_max_tokens(void) { return prefill_max_tokens(); }
 int qmoe_prefill_small_group_max(int n) { return prefill_small_group_max(n); }
 

@@ -183,6 +183,14 @@ cudaError_t launch_stack_kernel(const void* x, float* out, unsigned char* sync, 
                                 int* status, const qmoe_layer_weights* layers, int n_layers, const qmoe_dims& d,
                                 const XchgDesc* xc, const StackTraceBufs& tb, cudaStream_t stream);
 
+// The other expert formats (formats.cu).
+size_t fmt_row_bytes(int fmt, int64_t n);
+cudaError_t launch_fmt_dequant(int fmt, const uint8_t* raw, int64_t n_values, float* out, cudaStream_t s);
+cudaError_t launch_fmt_experts(const void* x, int x_f32, int M, const qmoe_dims& d, const qmoe_formats& f,
+                               const qmoe_layer_weights& w, const int32_t* ids, const float* weights,
+                               const float* shared_logit, float* h, int h_stride, float* out, int* status,
+                               cudaStream_t s);
+
 // The hyper-connection mixer (hc.cu).
 size_t hc_workspace_bytes(int M, int hc, int rank);
 size_t hc_down_smem(int M, int hc, int D);
@@ -233,6 +241,60 @@ __device__ __forceinline__ float load_act(const void* x, int x_f32, size_t i) {
         return __bfloat162float(__float2bfloat16_rn(v));
     }
     return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
+}
+
+// x[0, n) as load_act returns it, into shared memory (16-byte aligned): every
+// load of a thread's batch is issued before any store, 16-byte loads when x is
+// 16-byte aligned and n a multiple of 8.
+__device__ __forceinline__ void stage_act(float* dst, const void* x, int x_f32, int n) {
+    constexpr int U = 8;
+    const int nt = blockDim.x;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (n & 7) == 0) {
+        const int n8 = n >> 3;
+        const uint4* src = reinterpret_cast<const uint4*>(x);
+        for (int g0 = threadIdx.x; g0 < n8; g0 += nt * U) {
+            uint4 lo[U], hi[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int g = g0 + u * nt;
+                if (g < n8) {
+                    if (x_f32) {
+                        lo[u] = __ldcg(src + 2 * g);
+                        hi[u] = __ldcg(src + 2 * g + 1);
+                    } else {
+                        lo[u] = __ldcg(src + g);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int g = g0 + u * nt;
+                if (g >= n8) break;
+                float4 a, b;
+                if (x_f32) {
+                    auto r = [](uint32_t w) { return __bfloat162float(__float2bfloat16_rn(__uint_as_float(w))); };
+                    a = make_float4(r(lo[u].x), r(lo[u].y), r(lo[u].z), r(lo[u].w));
+                    b = make_float4(r(hi[u].x), r(hi[u].y), r(hi[u].z), r(hi[u].w));
+                } else {
+                    auto l = [](uint32_t w) { return __uint_as_float(w << 16); };
+                    auto h = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };
+                    a = make_float4(l(lo[u].x), h(lo[u].x), l(lo[u].y), h(lo[u].y));
+                    b = make_float4(l(lo[u].z), h(lo[u].z), l(lo[u].w), h(lo[u].w));
+                }
+                reinterpret_cast<float4*>(dst)[2 * g] = a;
+                reinterpret_cast<float4*>(dst)[2 * g + 1] = b;
+            }
+        }
+        return;
+    }
+    for (int i0 = threadIdx.x; i0 < n; i0 += nt * U) {
+        float v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = i0 + u * nt < n ? load_act(x, x_f32, (size_t)(i0 + u * nt)) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * nt < n) dst[i0 + u * nt] = v[u];
+    }
 }
 
 __device__ __forceinline__ void record_status(int* status, int code) {

@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
     int* owner = reinterpret_cast<int*>(xs + (size_t)M * nsb);     // [E_loc]
 
     build_plan(a, plan, owner);
-    convert_blocks<8>(
+    convert_blocks<16>(
         M * nsb, [&](int b, int ln) { return load_act(a.x, a.x_f32, (size_t)b * 32 + ln); },
         [&](int b, int ln, int pw, float st) {
             if (ln < 16) xq[(size_t)b * 16 + ln] = pw;
@@ -337,11 +337,33 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
     if (a.hconv) {
         // converted once by convert_h_kernel: 16 pair words and the step per
         // block; blocks past a slot's valid count were written as zeros
-        for (int i = warp; i < M * K1 * nsbh; i += kWarps) {
-            const int b = i % nsbh, ms = i / nsbh;
-            const float* src = a.hconv + (size_t)ms * a.hconv_stride + b * 32;
-            if (lane < 16) hq[(size_t)i * 16 + lane] = __float_as_int(__ldcg(src + lane));
-            if (lane == 16) hs[i] = __ldcg(src + 16);
+        // a thread per block, four blocks' loads in flight before any store
+        constexpr int U = 4;
+        const int nblk = M * K1 * nsbh;
+        for (int i0 = tid; i0 < nblk; i0 += blockDim.x * U) {
+            float4 q[U][4];
+            float st[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * blockDim.x;
+                if (i < nblk) {
+                    const int b = i % nsbh, ms = i / nsbh;
+                    const float* src = a.hconv + (size_t)ms * a.hconv_stride + b * 32;
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) q[u][v] = __ldcg(reinterpret_cast<const float4*>(src) + v);
+                    st[u] = __ldcg(src + 16);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * blockDim.x;
+                if (i < nblk) {
+                    float4* d = reinterpret_cast<float4*>(hq + (size_t)i * 16);
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) d[v] = q[u][v];
+                    hs[i] = st[u];
+                }
+            }
         }
     } else {
         convert_blocks<8>(
@@ -458,16 +480,30 @@ cudaError_t launch_with_smem(K kernel, unsigned grid, size_t smem, const ExpertA
 }
 
 template <int MAXM>
+int gateup_resident(int sbl, size_t smem) {
+    int n = 0;
+    const void* k = sbl == 1   ? reinterpret_cast<const void*>(gateup_kernel<MAXM, 1>)
+                    : sbl == 2 ? reinterpret_cast<const void*>(gateup_kernel<MAXM, 2>)
+                    : sbl == 3 ? reinterpret_cast<const void*>(gateup_kernel<MAXM, 3>)
+                               : reinterpret_cast<const void*>(gateup_kernel<MAXM, 4>);
+    if (smem_opt_in(k, (int)smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kWarps * 32, smem) != cudaSuccess || n < 1)
+        n = 1;
+    return n;
+}
+
+template <int MAXM>
 cudaError_t launch_gateup_m(const ExpertArgs& a, cudaStream_t s) {
     const int nsb = a.D >> 5;
     const size_t smem = (size_t)a.M * nsb * (16 * 4 + 4) + (size_t)(a.e_hi - a.e_lo) * 4;
     const int n_units = a.M * a.k + 1;
     const long tasks = (long)n_units * (a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc);
     unsigned grid = (unsigned)((tasks + kWarps - 1) / kWarps);
-    // Several tokens: every CTA converts all of x and plans all the experts
-    // first, so a grid of a few CTAs per SM takes the row pairs in strides.
-    if (a.M > 1) grid = min(grid, (unsigned)device_sm_count() * 4u);
     const int sbl = (nsb + 31) / 32;
+    // Several tokens: every CTA converts all of x and plans all the experts
+    // first, so one wave of resident CTAs takes the row pairs in strides (a
+    // second, partial wave would repeat that work for a few row pairs).
+    if (a.M > 1) grid = min(grid, (unsigned)(device_sm_count() * gateup_resident<MAXM>(sbl, smem)));
     switch (sbl) {
         case 1: return launch_with_smem(gateup_kernel<MAXM, 1>, grid, smem, a, s);
         case 2: return launch_with_smem(gateup_kernel<MAXM, 2>, grid, smem, a, s);

@@ -20,8 +20,9 @@
 namespace qmoe {
 namespace {
 
-constexpr int kRouteWarps = 4;
-template <int MAXM>
+// kRouteWarps warps per CTA: one router row each, then one token each in the
+// selecting CTA (4 for up to 4 tokens, else one per token).
+template <int MAXM, int kRouteWarps>
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
     extern __shared__ __align__(16) float xs[];  // [M][D]
     __shared__ float s_cv[kRouteWarps][kCandCap];
@@ -32,7 +33,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int M = a.M, D = a.D, E = a.E;
-    for (int i = tid; i < M * D; i += blockDim.x) xs[i] = load_act(a.x, a.x_f32, (size_t)i);
+    stage_act(xs, a.x, a.x_f32, M * D);
     __syncthreads();
 
     const int rows = E + (a.gate_vec ? 1 : 0);
@@ -121,12 +122,13 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
 
 template <int MAXM>
 cudaError_t launch_route_t(const RouteArgs& a, cudaStream_t s) {
+    constexpr int kRouteWarps = MAXM < 4 ? 4 : MAXM;
     const int rows = a.E + (a.gate_vec ? 1 : 0);
     const unsigned grid = (unsigned)((rows + kRouteWarps - 1) / kRouteWarps);
     const size_t smem = (size_t)a.M * a.D * sizeof(float);
-    cudaError_t err = smem_opt_in(reinterpret_cast<const void*>(route_kernel<MAXM>), (int)smem);
+    cudaError_t err = smem_opt_in(reinterpret_cast<const void*>(route_kernel<MAXM, kRouteWarps>), (int)smem);
     if (err != cudaSuccess) return err;
-    route_kernel<MAXM><<<grid, kRouteWarps * 32, smem, s>>>(a);
+    route_kernel<MAXM, kRouteWarps><<<grid, kRouteWarps * 32, smem, s>>>(a);
     return cudaGetLastError();
 }
 

@@ -37,10 +37,14 @@ __device__ __forceinline__ float warp_topk_fn(Load load, int E, int k, float* cv
     const int npl = E >> 5;
     float v[NPL];
     float lmax = -INFINITY;
+    // Every load issued before any use (a load past npl re-reads the last
+    // valid one and is never used).
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) v[j] = load(j < npl ? j : npl - 1);
 #pragma unroll
     for (int j = 0; j < NPL; ++j) {
         if (j < npl) {
-            float t = load(j);
+            float t = v[j];
             if (t != t) t = -INFINITY;  // NaN ranks last
             v[j] = t;
             lmax = fmaxf(lmax, t);
@@ -143,10 +147,12 @@ __device__ __forceinline__ float warp_topk_fn(Load load, int E, int k, float* cv
 }
 
 // The warp top-k of E fp32 logits in global memory (read through L2).
+// (E <= 512: 16 per lane, the register arrays sized to fit.)
 static __device__ __noinline__ float warp_topk(const float* __restrict__ logits, int E, int k, float* cv, int* ci,
                                                float* sv, int* si) {
-    return warp_topk_fn<32>([&](int j) { return __ldcg(logits + (threadIdx.x & 31) + 32 * j); }, E, k, cv, ci, sv,
-                            si);
+    auto load = [&](int j) { return __ldcg(logits + (threadIdx.x & 31) + 32 * j); };
+    if (E <= 512) return warp_topk_fn<16>(load, E, k, cv, ci, sv, si);
+    return warp_topk_fn<32>(load, E, k, cv, ci, sv, si);
 }
 
 

@@ -371,6 +371,58 @@ def route_topk(x: torch.Tensor, router_w: torch.Tensor, top_k: int) -> tuple[tor
     return ids, wt
 
 
+def dequant(fmt: int, raw: torch.Tensor) -> torch.Tensor:
+    """GGML blocks of `fmt` (Q8_0, IQ4_NL, IQ3_S, IQ4_XS; uint8 CUDA tensor [..., row bytes]) -> fp32
+    [..., values], bitwise the reference's `gguf.quants.dequantize`."""
+    if raw.dtype != torch.uint8 or not raw.is_cuda:
+        raise TypeError("raw must be a CUDA uint8 tensor of GGML blocks")
+    blk = {8: (32, 34), 20: (32, 18), 21: (256, 110), 23: (256, 136)}.get(fmt)
+    if blk is None:
+        raise ValueError(f"unsupported GGML type {fmt}")
+    bv, bb = blk
+    raw = raw.contiguous()
+    n = raw.numel() // bb * bv
+    out = torch.empty(*raw.shape[:-1], raw.shape[-1] // bb * bv, dtype=torch.float32, device=raw.device)
+    check(lib.qmoe_dequant_f32(fmt, raw.data_ptr(), n, out.data_ptr(), _stream()), "qmoe_dequant_f32")
+    return out
+
+
+def moe_block_formats(x: torch.Tensor, router_w: torch.Tensor, gate_vec: torch.Tensor | None,
+                      gate_up: torch.Tensor, down: torch.Tensor, sh_gate_up: torch.Tensor | None,
+                      sh_down: torch.Tensor | None, formats: tuple[int, int, int, int], top_k: int,
+                      out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """The MoE block (routed experts + sigmoid-gated shared expert, reference/model.py:387-417) on the
+    real checkpoint's formats: `formats` = GGML types of (gate|up, down, shared gate|up, shared down),
+    e.g. (IQ3_S, IQ4_NL, IQ3_S, Q8_0) as tt/plan.py:90-103 loads them.  gate_up [E, 2I, row bytes],
+    down [E, D, row bytes] uint8 CUDA tensors; x [.., M, D] -> the same leading shape."""
+    x2, dt = _act(x)
+    m = x2.shape[0]
+    E, D = router_w.shape
+    I = gate_up.shape[1] // 2
+    Ish = sh_gate_up.shape[0] // 2 if sh_gate_up is not None else 0
+    def segs(n):  # the IQ4_XS row-slice fields, consistent with a whole row (unused by other formats)
+        return (n // 256, 8) if n % 256 == 0 else (n // 32, 1)
+
+    (dseg, dsub), (sseg, ssub) = segs(I), segs(max(Ish, 32))
+    dims = Dims(hidden=D, inter=I, n_experts=E, top_k=top_k, expert_lo=0, expert_hi=E, inter_local=I,
+                down_nseg=dseg, down_nsub=dsub, down_ib0=0, sh_inter_local=Ish, sh_down_nseg=sseg,
+                sh_down_nsub=ssub, sh_down_ib0=0)
+    r_w = router_w.float().contiguous()
+    g_v = gate_vec.float().contiguous() if gate_vec is not None else None
+    gu, dn = gate_up.contiguous(), down.contiguous()
+    sgu = sh_gate_up.contiguous() if sh_gate_up is not None else None
+    sdn = sh_down.contiguous() if sh_down is not None else None
+    w = LayerWeights(router=r_w.data_ptr(), gate_vec=None if g_v is None else g_v.data_ptr(),
+                     gate_up=gu.data_ptr(), down=dn.data_ptr(),
+                     sh_gate_up=None if sgu is None else sgu.data_ptr(), sh_down=None if sdn is None else sdn.data_ptr())
+    f = _lib.Formats(*formats)
+    ws = workspace_for(dims, max(m, 1), x2.device)
+    out = torch.empty(m, D, dtype=torch.float32, device=x2.device)
+    check(lib.qmoe_moe_block_formats(x2.data_ptr(), dt, m, ctypes.byref(w), ctypes.byref(dims), ctypes.byref(f),
+                                     out.data_ptr(), ws.ptr, ws.nbytes, _stream()), "qmoe_moe_block_formats")
+    return _shaped(out, x, out_dtype)
+
+
 def route_threshold(x: torch.Tensor, router_w: torch.Tensor, top_k: int, k_sel: int = 16,
                     probs_bf16: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
     """The tie-admitting select (router_select.cpp:223-255, TT_ROUTER_EXACT_TOPK=0): (ids [M, k_sel]
