@@ -158,7 +158,7 @@ int get_ws(void* workspace, size_t bytes, const qmoe_dims* d, int M, Ws* ws) {
 
 int run_route(const void* x, int x_dtype, int M, const qmoe_layer_weights* w, const qmoe_dims* d,
               int32_t* ids, float* weights, float* shared_logit, const Ws& ws, cudaStream_t s, int thr_mode = 0,
-              int thr_k = 0) {
+              int thr_k = 0, int* xconv = nullptr) {
     RouteArgs r{};
     r.x = x;
     r.x_f32 = x_dtype == QMOE_ACT_F32;
@@ -178,14 +178,19 @@ int run_route(const void* x, int x_dtype, int M, const qmoe_layer_weights* w, co
     r.thr_k = thr_k;
     r.e_lo = d->expert_lo;
     r.e_hi = d->expert_hi;
+    r.xconv = xconv;
     return cuda_status(launch_route(r, s));
 }
 
 int run_block(const void* x, int x_dtype, int M, const qmoe_layer_weights* w, const qmoe_dims* d,
               float* out, const Ws& ws, cudaStream_t s) {
-    QMOE_TRY(run_route(x, x_dtype, M, w, d, ws.ids(), ws.weights(), ws.shared(), ws, s));
+    // The route launch also leaves x in block floating point (the workspace's
+    // act region) for every gate|up CTA to copy.
+    int* xconv = (int*)ws.act();
+    QMOE_TRY(run_route(x, x_dtype, M, w, d, ws.ids(), ws.weights(), ws.shared(), ws, s, 0, 0, xconv));
     ExpertArgs a = expert_args(x, x_dtype, M, ws.ids(), ws.weights(), ws.shared(), w, d, ws.h(),
                                ws.L.h_stride, out, ws.status());
+    a.xconv = xconv;
     a.hconv = ws.h();
     a.hconv_stride = ws.L.h_stride;
     QMOE_TRY(cuda_status(launch_gateup(a, s)));

@@ -121,6 +121,9 @@ struct RouteArgs {
     // thr_k-th probability (fp32, bf16 probabilities), the k slots filled from
     // experts [e_lo, e_hi).
     int thr_mode, thr_k, e_lo, e_hi;
+    // Non-null: the launch also writes x in block floating point for the
+    // gate|up kernel, [M][D/32][16] pair words then [M][D/32] steps.
+    int* xconv;
 };
 
 // Arguments shared by the two expert kernels.
@@ -145,6 +148,9 @@ struct ExpertArgs {
     // the step (the workspace's h region; may be h itself)
     float* hconv;           // null: the down kernel converts h itself
     int hconv_stride;
+    // x in block floating point as the route launch wrote it (RouteArgs::xconv);
+    // null: the gate|up kernel converts x itself
+    const int* xconv;
     // down
     const uint8_t* down;
     size_t dn_expert_bytes;

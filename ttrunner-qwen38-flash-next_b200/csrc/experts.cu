@@ -137,6 +137,28 @@ __device__ __forceinline__ void convert_blocks(int n, LoadF load, StoreF store) 
     }
 }
 
+// qmoe_subblock_dot on codes already through the codebook look-up (lo/hi
+// of the four qs words), for a sub-block dotted with several tokens.
+__device__ __forceinline__ int subblock_dot_lut(const uint32_t (&lo)[4], const uint32_t (&hi)[4], const int* xp) {
+    int a0 = __dp2a_lo(xp[0], (int)lo[0], 0);
+    int a1 = __dp2a_lo(xp[4], (int)lo[1], 0);
+    int a2 = __dp2a_lo(xp[8], (int)lo[2], 0);
+    int a3 = __dp2a_lo(xp[12], (int)lo[3], 0);
+    a0 = __dp2a_hi(xp[1], (int)lo[0], a0);
+    a1 = __dp2a_hi(xp[5], (int)lo[1], a1);
+    a2 = __dp2a_hi(xp[9], (int)lo[2], a2);
+    a3 = __dp2a_hi(xp[13], (int)lo[3], a3);
+    a0 = __dp2a_lo(xp[2], (int)hi[0], a0);
+    a1 = __dp2a_lo(xp[6], (int)hi[1], a1);
+    a2 = __dp2a_lo(xp[10], (int)hi[2], a2);
+    a3 = __dp2a_lo(xp[14], (int)hi[3], a3);
+    a0 = __dp2a_hi(xp[3], (int)hi[0], a0);
+    a1 = __dp2a_hi(xp[7], (int)hi[1], a1);
+    a2 = __dp2a_hi(xp[11], (int)hi[2], a2);
+    a3 = __dp2a_hi(xp[15], (int)hi[3], a3);
+    return (a0 + a1) + (a2 + a3);
+}
+
 // ---------------------------------------------------------------------------
 // gate|up + SwiGLU.  SBL = 32-value sub-blocks per lane along D (D / 1024).
 template <int MAXM, int SBL>
@@ -151,12 +173,30 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
     int* owner = reinterpret_cast<int*>(xs + (size_t)M * nsb);     // [E_loc]
 
     build_plan(a, plan, owner);
-    convert_blocks<16>(
-        M * nsb, [&](int b, int ln) { return load_act(a.x, a.x_f32, (size_t)b * 32 + ln); },
-        [&](int b, int ln, int pw, float st) {
-            if (ln < 16) xq[(size_t)b * 16 + ln] = pw;
-            if (ln == 0) xs[b] = st;
-        });
+    if (a.xconv) {
+        // converted once by the route launch; the same layout as xq then xs,
+        // copied with 16-byte loads, eight in flight per thread
+        const int n16 = M * nsb * 68 / 16;
+        const uint4* src = reinterpret_cast<const uint4*>(a.xconv);
+        uint4* dst = reinterpret_cast<uint4*>(smem);
+        constexpr int U = 8;
+        for (int i0 = tid; i0 < n16; i0 += blockDim.x * U) {
+            uint4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (i0 + u * (int)blockDim.x < n16) v[u] = __ldcg(src + i0 + u * blockDim.x);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (i0 + u * (int)blockDim.x < n16) dst[i0 + u * blockDim.x] = v[u];
+        }
+    } else {
+        convert_blocks<16>(
+            M * nsb, [&](int b, int ln) { return load_act(a.x, a.x_f32, (size_t)b * 32 + ln); },
+            [&](int b, int ln, int pw, float st) {
+                if (ln < 16) xq[(size_t)b * 16 + ln] = pw;
+                if (ln == 0) xs[b] = st;
+            });
+    }
     __syncthreads();
 
     // M == 1: the lane's activation blocks stay in registers for every row.
@@ -212,55 +252,80 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
         }
 
         const uint32_t tmask = (u < n_routed) ? plan.mask[u] : ((M >= 32) ? 0xffffffffu : ((1u << M) - 1u));
-        float accg[MAXM], accu[MAXM];
-#pragma unroll
-        for (int m = 0; m < MAXM; ++m) accg[m] = accu[m] = 0.0f;
+        const int slot_sh = a.k;
+        float dg[SBL], du[SBL];
 #pragma unroll
         for (int i = 0; i < SBL; ++i) {
-            const int b = lane + 32 * i;
-            if (b >= nsb) continue;
-            const int ib = b & 7;
-            const float dg = qmoe_half_bits_to_float((uint16_t)(hg[i].x & 0xFFFFu)) *
-                             (float)(qmoe_iq4xs_ls(hg[i].x, hg[i].y, ib) - 32);
-            const float du = qmoe_half_bits_to_float((uint16_t)(hu[i].x & 0xFFFFu)) *
-                             (float)(qmoe_iq4xs_ls(hu[i].x, hu[i].y, ib) - 32);
-            if (MAXM == 1) {
+            const int ib = (lane + 32 * i) & 7;
+            if (lane + 32 * i >= nsb) {
+                dg[i] = du[i] = 0.0f;
+                continue;
+            }
+            dg[i] = qmoe_half_bits_to_float((uint16_t)(hg[i].x & 0xFFFFu)) *
+                    (float)(qmoe_iq4xs_ls(hg[i].x, hg[i].y, ib) - 32);
+            du[i] = qmoe_half_bits_to_float((uint16_t)(hu[i].x & 0xFFFFu)) *
+                    (float)(qmoe_iq4xs_ls(hu[i].x, hu[i].y, ib) - 32);
+        }
+        if (MAXM == 1) {
+            float accg = 0.0f, accu = 0.0f;
+#pragma unroll
+            for (int i = 0; i < SBL; ++i) {
+                if (lane + 32 * i >= nsb) continue;
                 const int sg = qmoe_subblock_dot(qg[i][0].x, qg[i][0].y, qg[i][1].x, qg[i][1].y, xr[i], 0);
                 const int su = qmoe_subblock_dot(qu[i][0].x, qu[i][0].y, qu[i][1].x, qu[i][1].y, xr[i], 0);
-                accg[0] = fmaf(dg * xsr[i], (float)sg, accg[0]);
-                accu[0] = fmaf(du * xsr[i], (float)su, accu[0]);
-            } else {
-#pragma unroll
-                for (int m = 0; m < MAXM; ++m) {
-                    if (m < M && ((tmask >> m) & 1u)) {
-                        int xp[16];
-                        const int4* src = reinterpret_cast<const int4*>(xq + ((size_t)m * nsb + b) * 16);
-#pragma unroll
-                        for (int v = 0; v < 4; ++v) {
-                            const int4 w4 = src[v];
-                            xp[4 * v] = w4.x;
-                            xp[4 * v + 1] = w4.y;
-                            xp[4 * v + 2] = w4.z;
-                            xp[4 * v + 3] = w4.w;
-                        }
-                        const float st = xs[m * nsb + b];
-                        const int sg = qmoe_subblock_dot(qg[i][0].x, qg[i][0].y, qg[i][1].x, qg[i][1].y, xp, 0);
-                        const int su = qmoe_subblock_dot(qu[i][0].x, qu[i][0].y, qu[i][1].x, qu[i][1].y, xp, 0);
-                        accg[m] = fmaf(dg * st, (float)sg, accg[m]);
-                        accu[m] = fmaf(du * st, (float)su, accu[m]);
-                    }
-                }
+                accg = fmaf(dg[i] * xsr[i], (float)sg, accg);
+                accu = fmaf(du[i] * xsr[i], (float)su, accu);
             }
+            const float g = warp_sum(accg);
+            const float uu = warp_sum(accu);
+            if (lane == 0 && (tmask & 1u)) {
+                const int slot = (u < n_routed) ? plan.slot[u][0] : slot_sh;
+                a.h[(size_t)slot * a.h_stride + r] = silu(g) * uu;
+            }
+            continue;
         }
+        // Several tokens: the codes go through the codebook once, then each
+        // token that uses the unit (warp-uniform, usually one) takes one pass.
+        uint32_t glo[SBL][4], ghi[SBL][4], ulo[SBL][4], uhi[SBL][4];
 #pragma unroll
-        for (int m = 0; m < MAXM; ++m) {
-            if (m < M && ((tmask >> m) & 1u)) {
-                const float g = warp_sum(accg[m]);
-                const float uu = warp_sum(accu[m]);
-                if (lane == 0) {
-                    const int slot = (u < n_routed) ? plan.slot[u][m] : a.k;
-                    a.h[((size_t)m * (a.k + 1) + slot) * a.h_stride + r] = silu(g) * uu;
+        for (int i = 0; i < SBL; ++i) {
+            qmoe_lut8(qg[i][0].x, glo[i][0], ghi[i][0]);
+            qmoe_lut8(qg[i][0].y, glo[i][1], ghi[i][1]);
+            qmoe_lut8(qg[i][1].x, glo[i][2], ghi[i][2]);
+            qmoe_lut8(qg[i][1].y, glo[i][3], ghi[i][3]);
+            qmoe_lut8(qu[i][0].x, ulo[i][0], uhi[i][0]);
+            qmoe_lut8(qu[i][0].y, ulo[i][1], uhi[i][1]);
+            qmoe_lut8(qu[i][1].x, ulo[i][2], uhi[i][2]);
+            qmoe_lut8(qu[i][1].y, ulo[i][3], uhi[i][3]);
+        }
+        for (uint32_t mm = tmask; mm; mm &= mm - 1u) {
+            const int m = __ffs(mm) - 1;
+            float accg = 0.0f, accu = 0.0f;
+#pragma unroll
+            for (int i = 0; i < SBL; ++i) {
+                const int b = lane + 32 * i;
+                if (b >= nsb) continue;
+                int xp[16];
+                const int4* src = reinterpret_cast<const int4*>(xq + ((size_t)m * nsb + b) * 16);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const int4 w4 = src[v];
+                    xp[4 * v] = w4.x;
+                    xp[4 * v + 1] = w4.y;
+                    xp[4 * v + 2] = w4.z;
+                    xp[4 * v + 3] = w4.w;
                 }
+                const float st = xs[m * nsb + b];
+                const int sg = subblock_dot_lut(glo[i], ghi[i], xp);
+                const int su = subblock_dot_lut(ulo[i], uhi[i], xp);
+                accg = fmaf(dg[i] * st, (float)sg, accg);
+                accu = fmaf(du[i] * st, (float)su, accu);
+            }
+            const float g = warp_sum(accg);
+            const float uu = warp_sum(accu);
+            if (lane == 0) {
+                const int slot = (u < n_routed) ? plan.slot[u][m] : slot_sh;
+                a.h[((size_t)m * (a.k + 1) + slot) * a.h_stride + r] = silu(g) * uu;
             }
         }
     }
@@ -297,28 +362,29 @@ __global__ void __launch_bounds__(kWarps * 32) convert_h_kernel(ExpertArgs a) {
 
 // ---------------------------------------------------------------------------
 // down + weighted combine + gated shared expert.
-template <int MAXM>
-__global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ Plan plan;
-    __shared__ float s_w[kMaxTokens][kMaxTopK + 1];
-    __shared__ int s_nvalid[kMaxTokens][kMaxTopK + 1];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// The down kernels' common start: the expert plan, the per-(token, slot)
+// combine weights and valid h block counts, and every h block in block
+// floating point in shared memory (hq pair words, hs steps).
+struct DownShared {
+    Plan plan;
+    float w[kMaxTokens][kMaxTopK + 1];
+    int nvalid[kMaxTokens][kMaxTopK + 1];
+};
+
+__device__ __forceinline__ void down_prologue(const ExpertArgs& a, DownShared& sh, int* hq, float* hs, int* owner,
+                                              bool stage_h = true) {
+    const int tid = threadIdx.x;
     const int M = a.M, K1 = a.k + 1;
     const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
-    const int nsbh = I_max >> 5;                                     // h blocks per slot
-    int* hq = reinterpret_cast<int*>(smem);                          // [M][k+1][nsbh][16]
-    float* hs = reinterpret_cast<float*>(hq + (size_t)M * K1 * nsbh * 16);  // [M][k+1][nsbh]
-    int* owner = reinterpret_cast<int*>(hs + (size_t)M * K1 * nsbh);
-
-    build_plan(a, plan, owner);
+    const int nsbh = I_max >> 5;
+    build_plan(a, sh.plan, owner);
     const int has_sh = (a.sh_down != nullptr && a.sh_I_loc > 0) ? 1 : 0;
     for (int i = tid; i < M * K1; i += blockDim.x) {
         const int m = i / K1, s = i % K1;
         float w;
         if (s < a.k) w = a.weights[m * a.k + s];
         else w = (has_sh && a.shared_logit) ? sigmoid(a.shared_logit[m]) : (has_sh ? 1.0f : 0.0f);
-        s_w[m][s] = w;
+        sh.w[m][s] = w;
     }
     // Which (token, slot) h rows are in use, then convert them to block
     // floating point.
@@ -331,13 +397,14 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
         } else {
             nv = has_sh ? (a.sh_I_loc >> 5) : 0;
         }
-        s_nvalid[m][s] = nv;
+        sh.nvalid[m][s] = nv;
     }
     __syncthreads();
+    if (!stage_h) return;
     if (a.hconv) {
         // converted once by convert_h_kernel: 16 pair words and the step per
-        // block; blocks past a slot's valid count were written as zeros
-        // a thread per block, four blocks' loads in flight before any store
+        // block; blocks past a slot's valid count were written as zeros.  A
+        // thread per block, four blocks' loads in flight before any store.
         constexpr int U = 4;
         const int nblk = M * K1 * nsbh;
         for (int i0 = tid; i0 < nblk; i0 += blockDim.x * U) {
@@ -370,7 +437,7 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
             M * K1 * nsbh,
             [&](int i, int ln) {
                 const int b = i % nsbh, ms = i / nsbh;
-                return b < s_nvalid[ms / K1][ms % K1] ? a.h[(size_t)ms * a.h_stride + b * 32 + ln] : 0.0f;
+                return b < sh.nvalid[ms / K1][ms % K1] ? a.h[(size_t)ms * a.h_stride + b * 32 + ln] : 0.0f;
             },
             [&](int i, int ln, int pw, float st) {
                 if (ln < 16) hq[(size_t)i * 16 + ln] = pw;
@@ -378,6 +445,22 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
             });
     }
     __syncthreads();
+}
+
+template <int MAXM>
+__global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ DownShared sh;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int M = a.M, K1 = a.k + 1;
+    const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
+    const int nsbh = I_max >> 5;                                     // h blocks per slot
+    int* hq = reinterpret_cast<int*>(smem);                          // [M][k+1][nsbh][16]
+    float* hs = reinterpret_cast<float*>(hq + (size_t)M * K1 * nsbh * 16);  // [M][k+1][nsbh]
+    int* owner = reinterpret_cast<int*>(hs + (size_t)M * K1 * nsbh);
+    down_prologue(a, sh, hq, hs, owner);
+    const Plan& plan = sh.plan;
+    const int has_sh = (a.sh_down != nullptr && a.sh_I_loc > 0) ? 1 : 0;
 
     const int nsb_r = a.dn_nseg * a.dn_nsub;
     const int nsb_s = a.sh_nseg * a.sh_nsub;
@@ -455,7 +538,7 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
                             xp[4 * v + 3] = w4.w;
                         }
                         const int S = qmoe_subblock_dot(q0[i].x, q0[i].y, q1[i].x, q1[i].y, xp, 0);
-                        acc[m] = fmaf(s_w[m][s] * dl * hs[hb], (float)S, acc[m]);
+                        acc[m] = fmaf(sh.w[m][s] * dl * hs[hb], (float)S, acc[m]);
                     }
                 }
             }
@@ -465,6 +548,135 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
             if (m < M) {
                 const float v = warp_sum(acc[m]);
                 if (lane == 0) a.out[(size_t)m * a.D + j] = v;
+            }
+        }
+    }
+}
+
+// down + combine for several tokens with R = 32 / NSB output rows per warp
+// (NSB = the sub-blocks of a down row, routed and shared alike): lane
+// (rr, t) takes sub-block t of row j0 + rr of every unit (a routed expert or
+// the shared one), so the tokens that use a unit are the same for the whole
+// warp and the token loop does not diverge; each sub-block is looked up in
+// the codebook once for all its tokens.  US warps split a row group's units
+// and add their sums in a fixed order.  Grid: exactly D / (R * kWarps / US)
+// CTAs.
+template <int MAXM, int NSB, int US>
+__global__ void __launch_bounds__(kWarps * 32) down_rows_kernel(ExpertArgs a) {
+    constexpr int R = 32 / NSB, G = kWarps / US;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ DownShared sh;
+    __shared__ float part[kWarps][R][MAXM];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int M = a.M, K1 = a.k + 1;
+    const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
+    const int nsbh = I_max >> 5;
+    int* hq = reinterpret_cast<int*>(smem);                          // [M][k+1][nsbh][16]
+    float* hs = reinterpret_cast<float*>(hq + (size_t)M * K1 * nsbh * 16);  // [M][k+1][nsbh]
+    int* owner = reinterpret_cast<int*>(hs + (size_t)M * K1 * nsbh);
+    down_prologue(a, sh, hq, hs, owner);
+    const Plan& plan = sh.plan;
+    const int has_sh = (a.sh_down != nullptr && a.sh_I_loc > 0) ? 1 : 0;
+
+    const int rr = lane / NSB, t = lane % NSB;
+    const int g = warp % G, sp = warp / G;
+    const int n_units = plan.n + has_sh;
+    const int u_lo = sp * n_units / US, u_hi = (sp + 1) * n_units / US;
+    const int rb_r = a.dn_nseg * (8 + 16 * a.dn_nsub);
+    const int rb_s = a.sh_nseg * (8 + 16 * a.sh_nsub);
+    const int seg_r = t / a.dn_nsub, ibl_r = t - seg_r * a.dn_nsub;
+    const int seg_s = t / a.sh_nsub, ibl_s = t - seg_s * a.sh_nsub;
+    const int off_r = seg_r * (8 + 16 * a.dn_nsub), off_s = seg_s * (8 + 16 * a.sh_nsub);
+    const uint32_t all = (M >= 32) ? 0xffffffffu : ((1u << M) - 1u);
+    const int j = (blockIdx.x * G + g) * R + rr;
+
+    float acc[MAXM];
+#pragma unroll
+    for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
+    constexpr int kUB = 6;
+    for (int u0 = u_lo; u0 < u_hi; u0 += kUB) {
+        uint2 hdr[kUB], q0[kUB], q1[kUB];
+#pragma unroll
+        for (int i = 0; i < kUB; ++i) {
+            const int u = u0 + i;
+            if (u < u_hi) {
+                const uint8_t* sp_;
+                int ibl;
+                if (u < plan.n) {
+                    sp_ = a.down + (size_t)plan.expert[u] * a.dn_expert_bytes + (size_t)j * rb_r + off_r;
+                    ibl = ibl_r;
+                } else {
+                    sp_ = a.sh_down + (size_t)j * rb_s + off_s;
+                    ibl = ibl_s;
+                }
+                hdr[i] = ldg2(sp_);
+                q0[i] = ldg2(sp_ + 8 + 16 * ibl);
+                q1[i] = ldg2(sp_ + 16 + 16 * ibl);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kUB; ++i) {
+            const int u = u0 + i;
+            if (u >= u_hi) break;
+            const bool routed = u < plan.n;
+            const int ib = routed ? a.dn_ib0 + ibl_r : a.sh_ib0 + ibl_s;
+            const float dl = qmoe_half_bits_to_float((uint16_t)(hdr[i].x & 0xFFFFu)) *
+                             (float)(qmoe_iq4xs_ls(hdr[i].x, hdr[i].y, ib) - 32);
+            uint32_t lo[4], hi[4];
+            qmoe_lut8(q0[i].x, lo[0], hi[0]);
+            qmoe_lut8(q0[i].y, lo[1], hi[1]);
+            qmoe_lut8(q1[i].x, lo[2], hi[2]);
+            qmoe_lut8(q1[i].y, lo[3], hi[3]);
+            // the unit's tokens (warp-uniform), one pass each; the sum goes to
+            // its accumulator by a predicated select, so acc stays in registers
+            for (uint32_t mm = routed ? plan.mask[u] : all; mm; mm &= mm - 1u) {
+                const int m = __ffs(mm) - 1;
+                const int s = routed ? plan.slot[u][m] : a.k;
+                const size_t hb = ((size_t)m * K1 + s) * nsbh + t;
+                int xp[16];
+                const int4* src = reinterpret_cast<const int4*>(hq + hb * 16);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const int4 w4 = src[v];
+                    xp[4 * v] = w4.x;
+                    xp[4 * v + 1] = w4.y;
+                    xp[4 * v + 2] = w4.z;
+                    xp[4 * v + 3] = w4.w;
+                }
+                const float f = sh.w[m][s] * dl * hs[hb];
+                const float S = (float)subblock_dot_lut(lo, hi, xp);
+#pragma unroll
+                for (int q = 0; q < MAXM; ++q)
+                    if (q == m) acc[q] = fmaf(f, S, acc[q]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MAXM; ++m) {
+#pragma unroll
+        for (int o = NSB / 2; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+    }
+    if (US == 1) {
+        if (t == 0) {
+#pragma unroll
+            for (int m = 0; m < MAXM; ++m)
+                if (m < M) a.out[(size_t)m * a.D + j] = acc[m];
+        }
+        return;
+    }
+    if (t == 0) {
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) part[warp][rr][m] = acc[m];
+    }
+    __syncthreads();
+    if (sp == 0 && t == 0) {
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+            if (m < M) {
+                float v = part[g][rr][m];
+#pragma unroll
+                for (int q = 1; q < US; ++q) v += part[q * G + g][rr][m];
+                a.out[(size_t)m * a.D + j] = v;
             }
         }
     }
@@ -523,6 +735,18 @@ cudaError_t launch_down_m(const ExpertArgs& a, cudaStream_t s) {
         convert_h_kernel<<<(unsigned)((nb + kWarps - 1) / kWarps), kWarps * 32, 0, s>>>(a);
         cudaError_t err = cudaGetLastError();
         if (err != cudaSuccess) return err;
+        // Rows-per-warp layout when the routed and shared down rows have 8 or
+        // 16 sub-blocks (and D fills the exact grid); else a row per warp.
+        const int nsb_r = a.dn_nseg * a.dn_nsub;
+        const bool sh_ok = a.sh_down == nullptr || a.sh_I_loc == 0 || a.sh_nseg * a.sh_nsub == nsb_r;
+        if (sh_ok && (nsb_r == 16 || nsb_r == 8)) {
+            const int R = 32 / nsb_r;
+            if (a.D % (R * kWarps / 2) == 0) {
+                const unsigned g2 = (unsigned)(a.D / (R * kWarps / 2));
+                return nsb_r == 16 ? launch_with_smem(down_rows_kernel<MAXM, 16, 2>, g2, smem, a, s)
+                                   : launch_with_smem(down_rows_kernel<MAXM, 8, 2>, g2, smem, a, s);
+            }
+        }
         return launch_with_smem(down_kernel<MAXM>, grid, smem, a, s);
     }
     ExpertArgs b = a;

@@ -22,11 +22,25 @@
 namespace qmoe {
 namespace {
 
-#define QMOE_IQ3S_GRID_DEF __constant__ uint32_t c_iq3s_grid[512]
+#define QMOE_IQ3S_GRID_DEF __device__ uint32_t g_iq3s_grid[512]
 #include "iq3s_grid.inc"
 #undef QMOE_IQ3S_GRID_DEF
 
-__constant__ int8_t c_kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+__device__ float g_kvf[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f,
+                              1.f, 13.f, 25.f, 38.f, 53.f, 69.f, 89.f, 113.f};
+
+// The two code tables in shared memory, where lanes with different codes read
+// them in one pass (a constant-bank read serialises on distinct addresses).
+struct FmtTables {
+    uint32_t grid[512];
+    float kv[16];
+};
+
+__device__ __forceinline__ void load_tables(FmtTables& t) {
+    for (int i = threadIdx.x; i < 512; i += blockDim.x) t.grid[i] = g_iq3s_grid[i];
+    if (threadIdx.x < 16) t.kv[threadIdx.x] = g_kvf[threadIdx.x];
+    __syncthreads();
+}
 
 constexpr int kFmtWarps = 8;
 
@@ -34,8 +48,42 @@ __device__ __forceinline__ float f16_at(const uint8_t* p) {
     return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
 }
 
+// Activation values off .. off + 31 as load_act returns them; 16-byte loads
+// when x is 16-byte aligned (off is a multiple of 32).
+__device__ __forceinline__ void load_act32(const void* x, int x_f32, bool vec, size_t off, float (&xv)[32]) {
+    if (!vec) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) xv[j] = load_act(x, x_f32, off + j);
+        return;
+    }
+    if (x_f32) {
+        const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + off);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 v = __ldg(p + i);
+            xv[4 * i] = __bfloat162float(__float2bfloat16_rn(v.x));
+            xv[4 * i + 1] = __bfloat162float(__float2bfloat16_rn(v.y));
+            xv[4 * i + 2] = __bfloat162float(__float2bfloat16_rn(v.z));
+            xv[4 * i + 3] = __bfloat162float(__float2bfloat16_rn(v.w));
+        }
+        return;
+    }
+    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 v = __ldg(p + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            xv[8 * i + 2 * q] = __uint_as_float(w[q] << 16);
+            xv[8 * i + 2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
+        }
+    }
+}
+
 // Values 0..31 of 32-value sub-block sb of a row in format fmt.
-__device__ void decode32(int fmt, const uint8_t* row, int64_t sb, float (&v)[32]) {
+__device__ __forceinline__ void decode32(int fmt, const uint8_t* row, int64_t sb, float (&v)[32],
+                                         const FmtTables& tb) {
     if (fmt == QMOE_FMT_Q8_0) {
         const uint8_t* blk = row + (size_t)sb * 34;
         const float d = f16_at(blk);
@@ -47,8 +95,8 @@ __device__ void decode32(int fmt, const uint8_t* row, int64_t sb, float (&v)[32]
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             const uint8_t q = blk[2 + j];
-            v[j] = (float)c_kv[q & 0xF] * d;
-            v[16 + j] = (float)c_kv[q >> 4] * d;
+            v[j] = tb.kv[q & 0xF] * d;
+            v[16 + j] = tb.kv[q >> 4] * d;
         }
     } else if (fmt == QMOE_FMT_IQ4_XS) {
         const uint8_t* blk = row + (size_t)(sb >> 3) * 136;
@@ -60,8 +108,8 @@ __device__ void decode32(int fmt, const uint8_t* row, int64_t sb, float (&v)[32]
         const uint8_t* q = blk + 8 + ib * 16;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            v[j] = (float)c_kv[q[j] & 0xF] * dl;
-            v[16 + j] = (float)c_kv[q[j] >> 4] * dl;
+            v[j] = tb.kv[q[j] & 0xF] * dl;
+            v[16 + j] = tb.kv[q[j] >> 4] * dl;
         }
     } else {  // QMOE_FMT_IQ3_S
         const uint8_t* blk = row + (size_t)(sb >> 3) * 110;
@@ -74,8 +122,8 @@ __device__ void decode32(int fmt, const uint8_t* row, int64_t sb, float (&v)[32]
         const uint8_t* sg = blk + 74 + ib32 * 4;
 #pragma unroll
         for (int l = 0; l < 4; ++l) {
-            const uint32_t g1 = c_iq3s_grid[qs[2 * l] | ((h << (8 - 2 * l)) & 256)];
-            const uint32_t g2 = c_iq3s_grid[qs[2 * l + 1] | ((h << (7 - 2 * l)) & 256)];
+            const uint32_t g1 = tb.grid[qs[2 * l] | ((h << (8 - 2 * l)) & 256)];
+            const uint32_t g2 = tb.grid[qs[2 * l + 1] | ((h << (7 - 2 * l)) & 256)];
             const int s = sg[l];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -89,9 +137,11 @@ __device__ void decode32(int fmt, const uint8_t* row, int64_t sb, float (&v)[32]
 }
 
 __global__ void fmt_dequant_kernel(int fmt, const uint8_t* __restrict__ raw, int64_t n_sub, float* __restrict__ out) {
+    __shared__ FmtTables tb;
+    load_tables(tb);
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_sub; i += (int64_t)gridDim.x * blockDim.x) {
         float v[32];
-        decode32(fmt, raw, i, v);
+        decode32(fmt, raw, i, v, tb);
         float4* o = reinterpret_cast<float4*>(out + i * 32);
 #pragma unroll
         for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
@@ -120,7 +170,10 @@ struct FmtArgs {
 
 // h[m][s][r] = silu(G_e[r] . x_m) * (U_e[r] . x_m); slot k: the shared expert.
 __global__ void __launch_bounds__(kFmtWarps * 32) fmt_gateup_kernel(FmtArgs a) {
+    __shared__ FmtTables tb;
+    load_tables(tb);
     const int lane = threadIdx.x & 31;
+    const bool xvec = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
     const int K1 = a.k + 1, Imax = max(a.I, a.Ish);
     const long tasks = (long)a.M * K1 * Imax;
     const int nsb = a.D >> 5;
@@ -147,15 +200,15 @@ __global__ void __launch_bounds__(kFmtWarps * 32) fmt_gateup_kernel(FmtArgs a) {
         }
         float g = 0.0f, u = 0.0f;
         for (int sb = lane; sb < nsb; sb += 32) {
-            float wg[32], wu[32];
-            decode32(fmt, grow, sb, wg);
-            decode32(fmt, urow, sb, wu);
+            float xv[32];
+            load_act32(a.x, a.x_f32, xvec, (size_t)m * a.D + sb * 32, xv);
+            float w[32];
+            decode32(fmt, grow, sb, w, tb);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float xv = load_act(a.x, a.x_f32, (size_t)m * a.D + sb * 32 + j);
-                g = fmaf(wg[j], xv, g);
-                u = fmaf(wu[j], xv, u);
-            }
+            for (int j = 0; j < 32; ++j) g = fmaf(w[j], xv[j], g);
+            decode32(fmt, urow, sb, w, tb);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) u = fmaf(w[j], xv[j], u);
         }
         g = warp_sum(g);
         u = warp_sum(u);
@@ -165,6 +218,8 @@ __global__ void __launch_bounds__(kFmtWarps * 32) fmt_gateup_kernel(FmtArgs a) {
 
 // out[m][j] = sum_s w[m][s] D_e[j] . h[m][s] + sigmoid(shared logit) Dsh[j] . h[m][k]
 __global__ void __launch_bounds__(kFmtWarps * 32) fmt_down_kernel(FmtArgs a) {
+    __shared__ FmtTables tb;
+    load_tables(tb);
     const int lane = threadIdx.x & 31;
     const int K1 = a.k + 1;
     const int nr = a.I >> 5, ns = a.Ish >> 5;
@@ -193,11 +248,17 @@ __global__ void __launch_bounds__(kFmtWarps * 32) fmt_down_kernel(FmtArgs a) {
                 w = a.shared_logit ? sigmoid(a.shared_logit[m]) : 1.0f;
             }
             float v[32];
-            decode32(fmt, row, sb, v);
-            const float* hh = a.h + ((size_t)m * K1 + s) * a.h_stride + sb * 32;
+            decode32(fmt, row, sb, v, tb);
+            const float4* hh = reinterpret_cast<const float4*>(a.h + ((size_t)m * K1 + s) * a.h_stride + sb * 32);
             float d = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) d = fmaf(v[i], hh[i], d);
+            for (int i = 0; i < 8; ++i) {
+                const float4 h4 = hh[i];
+                d = fmaf(v[4 * i], h4.x, d);
+                d = fmaf(v[4 * i + 1], h4.y, d);
+                d = fmaf(v[4 * i + 2], h4.z, d);
+                d = fmaf(v[4 * i + 3], h4.w, d);
+            }
             acc = fmaf(w, d, acc);
         }
         acc = warp_sum(acc);

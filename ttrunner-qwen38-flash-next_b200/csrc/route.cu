@@ -35,6 +35,18 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
     const int M = a.M, D = a.D, E = a.E;
     stage_act(xs, a.x, a.x_f32, M * D);
     __syncthreads();
+    if (a.xconv) {
+        // x in block floating point for the gate|up kernel, a warp per
+        // 32-value block over the grid (block b = token b / (D/32)).
+        const int nb = M * (D >> 5);
+        float* xsf = reinterpret_cast<float*>(a.xconv + (size_t)nb * 16);
+        for (int b = blockIdx.x * kRouteWarps + warp; b < nb; b += gridDim.x * kRouteWarps) {
+            float st;
+            const int pw = warp_block_fp(xs[b * 32 + lane], &st);
+            if (lane < 16) a.xconv[b * 16 + lane] = pw;
+            if (lane == 0) xsf[b] = st;
+        }
+    }
 
     const int rows = E + (a.gate_vec ? 1 : 0);
     const int row = blockIdx.x * kRouteWarps + warp;
