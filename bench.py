@@ -283,7 +283,7 @@ def main() -> None:
     device_status = stack.ws.read_status()
 
     # ---- per-kernel durations for the roofline (eager, events per stage) ----
-    stage = stage_timings(pkg, layers, xs[0], M, dev, reps=2)
+    stage = stage_timings(pkg, layers, xs[0], M, dev)
     prefill = prefill_timings(pkg, layers[0], cfg, dev) if world == 1 and not args.no_prefill else None
     verify = verify_timings(pkg, layers, cfg, dev) if world == 1 and M == 1 and not args.no_verify else None
     formats = formats_timings(pkg, cfg, dev) if world == 1 and M == 1 and not args.no_formats else None
@@ -528,30 +528,39 @@ def formats_timings(pkg, cfg, dev, tokens=(1, 4), n_layers: int = 4, steps: int 
     return out
 
 
-def stage_timings(pkg, layers, x, M: int, dev, reps: int = 2) -> dict:
-    """Average duration of each stage launch over all layers, CUDA events on the
-    launching stream (eager calls through the stage entry points)."""
+def stage_timings(pkg, layers, x, M: int, dev, reps: int = 10) -> dict:
+    """Average device time of each stage launch of the per-layer path (route, gate|up, down through
+    their C entry points), every layer's call of a stage captured in one CUDA graph and replayed
+    `reps` times; CUDA events around the replays on the launching stream."""
     import torch
 
     mls = [pkg.MoELayer(l, max_tokens=max(M, 1)) for l in layers]
     x = x.contiguous()
-    acc = {"route_us": [], "gateup_us": [], "down_us": []}
-    for _ in range(reps + 1):
-        for ml in mls:
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-            ev[0].record()
-            ids, w, sl = ml.route(x)
-            ev[1].record()
-            h = ml.gate_up(x, ids)
-            ev[2].record()
-            ml.down(h, ids, w, sl)
-            ev[3].record()
-            torch.cuda.synchronize(dev)
-            acc["route_us"].append(ev[0].elapsed_time(ev[1]) * 1000)
-            acc["gateup_us"].append(ev[1].elapsed_time(ev[2]) * 1000)
-            acc["down_us"].append(ev[2].elapsed_time(ev[3]) * 1000)
-    n = len(mls)
-    return {k: statistics.mean(v[n:]) for k, v in acc.items()}  # first pass is warm-up
+    routed = [ml.route(x) for ml in mls]
+    hs = [ml.gate_up(x, r[0]) for ml, r in zip(mls, routed)]
+    stages = {
+        "route_us": lambda: [ml.route(x) for ml in mls],
+        "gateup_us": lambda: [ml.gate_up(x, r[0]) for ml, r in zip(mls, routed)],
+        "down_us": lambda: [ml.down(h, r[0], r[1], r[2]) for ml, r, h in zip(mls, routed, hs)],
+    }
+    out = {}
+    for name, fn in stages.items():
+        fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        out[name] = e0.elapsed_time(e1) * 1000.0 / reps / len(mls)
+        del g
+    return out
 
 
 def run_reference_arm(args, rank: int, world: int) -> None:
