@@ -162,7 +162,7 @@ __device__ __forceinline__ int subblock_dot_lut(const uint32_t (&lo)[4], const u
 // ---------------------------------------------------------------------------
 // gate|up + SwiGLU.  SBL = 32-value sub-blocks per lane along D (D / 1024).
 template <int MAXM, int SBL>
-__global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, (MAXM == 1 || SBL > 2) ? 1 : 3) gateup_kernel(ExpertArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ Plan plan;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
 // and add their sums in a fixed order.  Grid: exactly D / (R * kWarps / US)
 // CTAs.
 template <int MAXM, int NSB, int US>
-__global__ void __launch_bounds__(kWarps * 32) down_rows_kernel(ExpertArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, 3) down_rows_kernel(ExpertArgs a) {
     constexpr int R = 32 / NSB, G = kWarps / US;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ DownShared sh;
