@@ -341,6 +341,15 @@ int qmoe_prefill_max_tokens(void);
  * reference has no counterpart (its prefill runs every group through the
  * same matmul, tt/moe.py:330-368). */
 int qmoe_prefill_small_group_max(int n);
+/* Diagnostics: enable != 0 makes the grouped GEMM's CTA 0 stamp its pipeline
+ * clock (%clock64) per A slot into the prefill workspace (bytes 256 .. 4351:
+ * [64 slots][8 events] u64: B copy issued, MMA thread past the A and B waits,
+ * MMAs issued, expansion past its slot wait and done, stage issued, expansion
+ * past the stage wait); 0 turns it off (the default: the stamps slow CTA 0);
+ * < 0 only queries.  Returns the previous value.  Process-wide, like
+ * qmoe_prefill_small_group_max.  The reference's counterpart is its section
+ * profiler (tt/bench.py:33-78). */
+int qmoe_prefill_trace(int enable);
 size_t qmoe_prefill_workspace_bytes(const qmoe_dims* dims, int n_tokens);
 /* ids [T, top_k] int32 and weights [T, top_k] fp32 (renormalised, descending,
  * ties to the lower id); shared_logit [T] (x . gate_vec) or NULL. */

@@ -162,6 +162,7 @@ _SIGS = {
     "qmoe_hc_reinject": (c_int, [_P, c_int, _P, c_int, _P, c_int, POINTER(HcDims), _P, _P]),
     "qmoe_prefill_max_tokens": (c_int, []),
     "qmoe_prefill_small_group_max": (c_int, [c_int]),
+    "qmoe_prefill_trace": (c_int, [c_int]),
     "qmoe_prefill_workspace_bytes": (c_size_t, [POINTER(Dims), c_int]),
     "qmoe_prefill_route": (c_int, [_P, c_int, c_int, POINTER(LayerWeights), POINTER(Dims), _P, _P, _P, _P,
                                    c_size_t, _P]),

@@ -768,6 +768,7 @@ int qmoe_moe_block_formats(const void* x, int x_dtype, int n_tokens, const qmoe_
 
 int qmoe_prefill_max_tokens(void) { return prefill_max_tokens(); }
 int qmoe_prefill_small_group_max(int n) { return prefill_small_group_max(n); }
+int qmoe_prefill_trace(int enable) { return prefill_trace(enable); }
 
 size_t qmoe_prefill_workspace_bytes(const qmoe_dims* dims, int n_tokens) {
     if (check_dims(dims) != QMOE_OK || n_tokens < 1 || n_tokens > prefill_max_tokens()) return 0;

@@ -210,6 +210,7 @@ cudaError_t launch_hc_reinject(const void* hyper, int h_f32, const void* branch,
 // Prefill / large verify chunks (prefill.cu).
 int prefill_max_tokens();
 int prefill_small_group_max(int n);
+int prefill_trace(int enable);
 bool prefill_supported(const qmoe_dims& d);
 struct PfLayout;
 size_t prefill_workspace_bytes(const qmoe_dims& d, int T);

@@ -54,10 +54,19 @@ constexpr int kGTmemCols = 2 * kGNMax;  // two accumulator buffers
 // warp roles
 // Dequant: two groups of kNDqG warps; group g expands the slots whose running
 // index is g mod 2, so two slots are expanded at once.
+// A warp issues on scheduler (warp mod 4).  The single MMA-issuing thread
+// shares its scheduler only with the light roles (stage loads, B copies, one
+// epilogue warp), so the expansion warps do not take its issue slots: with
+// four expansion warps beside it, each step of its per-slot loop waited
+// several hundred cycles.  Warps 20-23 are the epilogue (TMEM lane quarter =
+// warp mod 4), warp 18 has no role, the other 16 expand.
 constexpr int kNDqG = 8, kNDqGroups = 2;
-constexpr int kWLoad = 0, kWGather = 1, kWMma = 2, kWDq0 = 3, kNDq = kNDqG * kNDqGroups, kWEp0 = kWDq0 + kNDq, kNEp = 4;
-constexpr int kGWarps = kWEp0 + kNEp;  // 23
+constexpr int kWLoad = 6, kWGather = 10, kWMma = 2, kWIdle = 18, kNDq = kNDqG * kNDqGroups, kWEp0 = 20, kNEp = 4;
+constexpr int kGWarps = 24;
 constexpr int kGThreads = kGWarps * 32;
+// Expansion index 0..15 of a warp that is none of the above.
+__host__ __device__ constexpr int dq_index(int w) { return w - (w > 2) - (w > 6) - (w > 10) - (w > 18); }
+static_assert(dq_index(19) == kNDq - 1 && dq_index(0) == 0, "16 expansion warps");
 
 // shared-memory carve-up from a 1024-aligned base
 constexpr int kOffA = 0;
@@ -122,7 +131,7 @@ struct PfSmem {
 // false: the drains before exit wait for in-flight work regardless).
 __device__ bool pf_wait(uint64_t* bar, uint32_t par, volatile int* abort_flag, int* status,
                         bool honour_abort = true) {
-    if (ptx::mbar_test(bar, par)) return true;
+    if (ptx::mbar_probe(bar, par)) return true;
     const unsigned long long t0 = ptx::now_ns();
     for (unsigned it = 0;; ++it) {
         if (ptx::mbar_test_sleep(bar, par, 20000u)) return true;
@@ -330,6 +339,11 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
         if (lane == 0) {
             int it = 0, tc = 0;
             bool ok = true, issued = false;
+            // Slot s's descriptor is slot 0's plus s * slot bytes / 16 in the
+            // start-address field (the rings lie below 256 KB of shared
+            // memory, so the 14-bit field does not overflow).
+            const uint64_t desc_a0 = ptx::desc_sw128(ptx::smem_addr(S.a_slot(0)));
+            const uint64_t desc_b0 = ptx::desc_sw128(ptx::smem_addr(S.b_slot(0)));
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
                 const TileInfo ti = tile_info(a, t, MT);
                 const uint32_t idesc = ptx::idesc_bf16(kGM, ti.N);
@@ -340,6 +354,7 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                 }
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * kGNMax);
+                const uint32_t idesc_t = idesc;
                 for (int ks = 0; ks < nslots; ++ks) {
                     const int slot = it % kGSlots, bslot = it % kGBSlots;
                     if (!pf_wait(S.s_full(slot), (it / kGSlots) & 1, abort_flag, a.status)) {
@@ -353,11 +368,13 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                     }
                     pf_stamp(a, it, 2);
                     ptx::tc_fence_after();
-                    const uint32_t a0 = ptx::smem_addr(S.a_slot(slot)), b0 = ptx::smem_addr(S.b_slot(bslot));
+                    // descriptors of the slots, advanced 32 bytes (2 in the
+                    // start-address field) per K = 16 step
+                    const uint64_t da = desc_a0 + (uint64_t)(slot * (kGSlotBytes >> 4));
+                    const uint64_t db = desc_b0 + (uint64_t)(bslot * (kGBSlotBytes >> 4));
 #pragma unroll
                     for (int k = 0; k < kGSlotK / 16; ++k)
-                        ptx::mma_bf16(d_tmem, ptx::desc_sw128(a0 + k * 32), ptx::desc_sw128(b0 + k * 32), idesc,
-                                      (ks | k) != 0 ? 1u : 0u);
+                        ptx::mma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc_t, (ks | k) != 0 ? 1u : 0u);
                     ptx::mma_commit(S.s_empty(slot));
                     ptx::mma_commit(S.b_empty(bslot));
                     pf_stamp(a, it, 3);
@@ -375,9 +392,10 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
             }
         }
         __syncwarp();
+    } else if (warp == kWIdle) {
     } else if (warp < kWEp0) {
         // ---- dequant: IQ4_XS stage -> bf16 A slot -----------------------
-        const int dq = warp - kWDq0, grp = dq / kNDqG;
+        const int dq = dq_index(warp), grp = dq / kNDqG;
         const int d = (dq % kNDqG) * 32 + lane;  // 0..255 within the group
         const int m = d & (kGM - 1), sub = d >> 7;
         int it = 0, st_it = 0;
@@ -433,6 +451,20 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
             const TileInfo ti = tile_info(a, t, MT);
             const int ab = tc & 1;
+            // this tile's token ids and weights (down), one per lane and column
+            // half, loaded before the accumulator wait and broadcast per column
+            int tok_r[2] = {0, 0};
+            float w_r[2] = {0.0f, 0.0f};
+            if (a.mode == 1) {
+#pragma unroll
+                for (int hlf = 0; hlf < 2; ++hlf) {
+                    const int n = hlf * 32 + lane;
+                    if (n < ti.cnt) {
+                        tok_r[hlf] = __ldg(a.slot_tok + ti.row0 + n);
+                        w_r[hlf] = __ldg(a.slot_w + ti.row0 + n);
+                    }
+                }
+            }
             if (!pf_wait_warp(S.acc_full(ab), (tc >> 1) & 1, abort_flag, a.status)) break;
             ptx::tc_fence_after();
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * kGNMax);
@@ -450,14 +482,14 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                     }
                 } else {
                     const int row = ti.mt * kGM + m;
+                    const int hlf = c0 >> 5;  // c0 + j < 64 stays in one half: c0 is a multiple of 16
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = c0 + j;
-                        if (n < ti.cnt) {
-                            const int tok = __ldg(a.slot_tok + ti.row0 + n);
-                            const float w = __ldg(a.slot_w + ti.row0 + n);
-                            if ((unsigned)tok < (unsigned)a.T) atomicAdd(a.out + (size_t)tok * a.D + row, w * v[j]);
-                        }
+                        const int tok = __shfl_sync(0xffffffffu, tok_r[hlf], n & 31);
+                        const float w = __shfl_sync(0xffffffffu, w_r[hlf], n & 31);
+                        if (n < ti.cnt && (unsigned)tok < (unsigned)a.T)
+                            atomicAdd(a.out + (size_t)tok * a.D + row, w * v[j]);
                     }
                 }
             }
@@ -1075,6 +1107,15 @@ int prefill_small_group_max(int n) {
     return g_small_group_max.exchange(n < kGvMax ? n : kGvMax);
 }
 
+// Whether the grouped GEMM's CTA 0 stamps its pipeline clocks into the
+// workspace (off by default: the stamps cost CTA 0, and with it the launch,
+// tens of cycles per slot).  Process-wide, atomic like the setting above.
+static std::atomic<int> g_pf_trace{0};
+int prefill_trace(int enable) {
+    if (enable < 0) return g_pf_trace.load();
+    return g_pf_trace.exchange(enable ? 1 : 0);
+}
+
 size_t prefill_workspace_bytes(const qmoe_dims& d, int T) { return pf_layout(d, T).total; }
 
 void prefill_route_buffers(const qmoe_dims& d, int T, unsigned char* ws, int32_t** ids, float** weights,
@@ -1179,7 +1220,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     a.meta = meta;
     a.out = out;
     a.status = status;
-    a.trace = reinterpret_cast<unsigned long long*>(ws + L.trace);
+    a.trace = g_pf_trace.load() ? reinterpret_cast<unsigned long long*>(ws + L.trace) : nullptr;
     err = smem_opt_in(reinterpret_cast<const void*>(grouped_gemm_kernel), kGSmemBytes);
     if (err != cudaSuccess) return err;
     const int n_sm = device_sm_count();

@@ -23,6 +23,17 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
 }
+// The same question without the potentially blocking try_wait: one
+// non-blocking test (for the common case of a phase that has completed).
+__device__ __forceinline__ bool mbar_probe(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // True once the phase with parity `parity` has completed (a fresh barrier
 // counts the phase before its first as completed with parity 1).
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
