@@ -41,14 +41,17 @@ constexpr unsigned long long kPfTimeoutNs = 1000ull * 1000 * 1000;
 // ---- grouped GEMM geometry --------------------------------------------------
 constexpr int kGM = 128;            // MMA M: weight rows per tile
 constexpr int kGNMax = 64;          // tokens per n-tile (MMA N, padded to 16)
-constexpr int kGSlotK = 64;         // K per operand slot: one 128-byte swizzle row of bf16
-constexpr int kGSlots = 4;          // A (expanded weights) ring depth
-constexpr int kGBSlots = 8;         // B (token rows) ring depth: its copies run further ahead
+constexpr int kGAtomK = 64;         // K of one 128-byte swizzle atom row of bf16
+constexpr int kGSlotK = 128;        // K per operand slot: two atoms, one handshake
+constexpr int kGSlots = 3;          // slot ring depth (A expanded weights and B token rows together)
 constexpr int kGStageK = 512;       // K per IQ4_XS stage: two super-blocks of every row
 constexpr int kGStageRowB = 2 * QMOE_SB_BYTES;  // 272 bytes of one row per stage
 constexpr int kGStages = 2;
-constexpr int kGSlotBytes = kGM * kGSlotK * 2;      // 16 KB A slot
-constexpr int kGBSlotBytes = kGNMax * kGSlotK * 2;  // 8 KB B slot
+constexpr int kGAtomBytes = kGM * kGAtomK * 2;      // 16 KB: 128 rows x 64 K of A
+constexpr int kGSlotBytes = 2 * kGAtomBytes;        // 32 KB A slot
+constexpr int kGBAtomBytes = kGNMax * kGAtomK * 2;  // 8 KB: 64 token rows x 64 K of B
+constexpr int kGBSlotBytes = 2 * kGBAtomBytes;      // 16 KB B slot
+constexpr int kGSlotsPerStage = kGStageK / kGSlotK; // 4
 constexpr int kGStageBytes = kGM * kGStageRowB;  // 34,816
 constexpr int kGTmemCols = 2 * kGNMax;  // two accumulator buffers
 // warp roles
@@ -71,12 +74,13 @@ static_assert(dq_index(19) == kNDq - 1 && dq_index(0) == 0, "16 expansion warps"
 // shared-memory carve-up from a 1024-aligned base
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kGSlots * kGSlotBytes;
-constexpr int kOffStage = kOffB + kGBSlots * kGBSlotBytes;
+constexpr int kOffStage = kOffB + kGSlots * kGBSlotBytes;
 constexpr int kOffBars = kOffStage + kGStages * kGStageBytes;
-constexpr int kNBars = 2 * kGStages + 2 * kGSlots + 2 * kGBSlots + 2 * 2 + 1;
+constexpr int kNBars = 2 * kGStages + 2 * kGSlots + 2 * 2 + 1;
 constexpr int kOffMisc = kOffBars + kNBars * 8;
 constexpr int kGSmemBytes = kOffMisc + 64 + 1024;  // + slack to align the base
 static_assert(kOffStage % 1024 == 0 && kOffB % 1024 == 0, "operand tiles must be 1024-aligned");
+static_assert(kGSmemBytes <= 232448, "dynamic shared memory above the 227 KB opt-in limit");
 
 struct GemmArgs {
     int mode;  // 0: gate|up + SwiGLU -> h; 1: down + weighted scatter-add -> out
@@ -117,11 +121,9 @@ struct PfSmem {
     __device__ uint64_t* iq_empty(int s) const { return bars + kGStages + s; }
     __device__ uint64_t* s_full(int s) const { return bars + 2 * kGStages + s; }
     __device__ uint64_t* s_empty(int s) const { return bars + 2 * kGStages + kGSlots + s; }
-    __device__ uint64_t* b_full(int s) const { return bars + 2 * kGStages + 2 * kGSlots + s; }
-    __device__ uint64_t* b_empty(int s) const { return bars + 2 * kGStages + 2 * kGSlots + kGBSlots + s; }
-    __device__ uint64_t* acc_full(int b) const { return bars + 2 * kGStages + 2 * kGSlots + 2 * kGBSlots + b; }
-    __device__ uint64_t* acc_empty(int b) const { return bars + 2 * kGStages + 2 * kGSlots + 2 * kGBSlots + 2 + b; }
-    __device__ uint64_t* fin() const { return bars + 2 * kGStages + 2 * kGSlots + 2 * kGBSlots + 4; }
+    __device__ uint64_t* acc_full(int b) const { return bars + 2 * kGStages + 2 * kGSlots + b; }
+    __device__ uint64_t* acc_empty(int b) const { return bars + 2 * kGStages + 2 * kGSlots + 2 + b; }
+    __device__ uint64_t* fin() const { return bars + 2 * kGStages + 2 * kGSlots + 4; }
     __device__ uint32_t* tmem_holder() const { return reinterpret_cast<uint32_t*>(base + kOffMisc); }
     __device__ volatile int* abort_flag() const { return reinterpret_cast<volatile int*>(base + kOffMisc + 16); }
 };
@@ -236,13 +238,11 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
             ptx::mbar_init(S.iq_full(s), 1);
             ptx::mbar_init(S.iq_empty(s), kNDq);
         }
+        // A slot full: the 8 expansion warps of its group and the B copy (one
+        // arrival with the copy's bytes); empty: the MMAs that read it.
         for (int s = 0; s < kGSlots; ++s) {
-            ptx::mbar_init(S.s_full(s), kNDqG);
+            ptx::mbar_init(S.s_full(s), kNDqG + 1);
             ptx::mbar_init(S.s_empty(s), 1);
-        }
-        for (int s = 0; s < kGBSlots; ++s) {
-            ptx::mbar_init(S.b_full(s), 1);
-            ptx::mbar_init(S.b_empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
             ptx::mbar_init(S.acc_full(b), 1);
@@ -308,29 +308,33 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                     (void)pf_wait(S.iq_full(s), (last_issue[s] / kGStages) & 1, abort_flag, a.status, false);
         }
     } else if (warp == kWGather) {
-        // ---- B operand: one 2-D tensor copy per slot (64 K x 64 rows), on its
-        // own ring of kGBSlots so the copies run ahead of the A ring ---------
+        // ---- B operand: two 2-D tensor copies per slot (2 x 64 K x 64 rows)
+        // into the slot's B half, counted on the slot's full barrier --------
         if (lane == 0) {
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
                 const TileInfo ti = tile_info(a, t, MT);
                 for (int ks = 0; ks < nslots; ++ks) {
-                    const int slot = it % kGBSlots;
-                    if (!pf_wait(S.b_empty(slot), ((it / kGBSlots) & 1) ^ 1, abort_flag, a.status)) {
+                    const int slot = it % kGSlots;
+                    if (!pf_wait(S.s_empty(slot), ((it / kGSlots) & 1) ^ 1, abort_flag, a.status)) {
                         ok = false;
                         break;
                     }
-                    ptx::mbar_expect_tx(S.b_full(slot), kGBSlotBytes);
-                    ptx::tma_load_2d(S.b_slot(slot), &a.bmap, ks * kGSlotK, ti.row0, S.b_full(slot));
+                    ptx::mbar_expect_tx(S.s_full(slot), kGBSlotBytes);
+                    ptx::tma_load_2d(S.b_slot(slot), &a.bmap, ks * kGSlotK, ti.row0, S.s_full(slot));
+                    ptx::tma_load_2d(S.b_slot(slot) + kGBAtomBytes, &a.bmap, ks * kGSlotK + kGAtomK, ti.row0,
+                                     S.s_full(slot));
                     pf_stamp(a, it, 0);
                     ++it;
                 }
             }
-            // the last copies land before the CTA leaves (bounded)
+            // The last copies land before the CTA leaves (bounded: after an
+            // abort the expansion arrivals on those slots may never come, and
+            // each wait then ends at the time limit).
             if (!ok)
-                for (int j = 1; j <= kGBSlots && it - j >= 0; ++j)
-                    (void)pf_wait(S.b_full((it - j) % kGBSlots), ((it - j) / kGBSlots) & 1, abort_flag, a.status,
+                for (int j = 1; j <= kGSlots && it - j >= 0; ++j)
+                    (void)pf_wait(S.s_full((it - j) % kGSlots), ((it - j) / kGSlots) & 1, abort_flag, a.status,
                                   false);
         }
         __syncwarp();
@@ -356,27 +360,26 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * kGNMax);
                 const uint32_t idesc_t = idesc;
                 for (int ks = 0; ks < nslots; ++ks) {
-                    const int slot = it % kGSlots, bslot = it % kGBSlots;
+                    const int slot = it % kGSlots;
                     if (!pf_wait(S.s_full(slot), (it / kGSlots) & 1, abort_flag, a.status)) {
                         ok = false;
                         break;
                     }
                     pf_stamp(a, it, 1);
-                    if (!pf_wait(S.b_full(bslot), (it / kGBSlots) & 1, abort_flag, a.status)) {
-                        ok = false;
-                        break;
-                    }
                     pf_stamp(a, it, 2);
                     ptx::tc_fence_after();
-                    // descriptors of the slots, advanced 32 bytes (2 in the
-                    // start-address field) per K = 16 step
+                    // descriptors of the slot's atoms, advanced 32 bytes (2 in
+                    // the start-address field) per K = 16 step
                     const uint64_t da = desc_a0 + (uint64_t)(slot * (kGSlotBytes >> 4));
-                    const uint64_t db = desc_b0 + (uint64_t)(bslot * (kGBSlotBytes >> 4));
+                    const uint64_t db = desc_b0 + (uint64_t)(slot * (kGBSlotBytes >> 4));
 #pragma unroll
-                    for (int k = 0; k < kGSlotK / 16; ++k)
-                        ptx::mma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc_t, (ks | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < kGSlotK / 16; ++k) {
+                        const int atom = k >> 2, kk = k & 3;
+                        ptx::mma_bf16(d_tmem, da + (uint64_t)(atom * (kGAtomBytes >> 4) + 2 * kk),
+                                      db + (uint64_t)(atom * (kGBAtomBytes >> 4) + 2 * kk), idesc_t,
+                                      (ks | k) != 0 ? 1u : 0u);
+                    }
                     ptx::mma_commit(S.s_empty(slot));
-                    ptx::mma_commit(S.b_empty(bslot));
                     pf_stamp(a, it, 3);
                     issued = true;
                     ++it;
@@ -403,7 +406,7 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
         for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
             for (int ks = 0; ks < nslots; ++ks) {
                 const int st = st_it % kGStages;
-                if ((ks & 7) == 0) {
+                if ((ks % kGSlotsPerStage) == 0) {
                     if (!pf_wait_warp(S.iq_full(st), (st_it / kGStages) & 1, abort_flag, a.status)) {
                         ok = false;
                         break;
@@ -417,26 +420,33 @@ __global__ void __launch_bounds__(kGThreads, 1) grouped_gemm_kernel(const __grid
                         break;
                     }
                     if (dq % kNDqG == 0 && lane == 0) pf_stamp(a, it, 4);
-                    const int sbk = (ks & 7) * 2 + sub;  // sub-block of the row within the stage (0..15)
                     // stage row of M row m: gate|up stages hold the gate box then the up box
                     const int srow = a.mode == 0 ? ((m & 1) ? 64 + (m >> 1) : (m >> 1)) : m;
-                    const uint8_t* blk = S.stage(st) + srow * kGStageRowB + (sbk >> 3) * QMOE_SB_BYTES;
-                    const int ib = sbk & 7;
-                    const uint2 hd = *reinterpret_cast<const uint2*>(blk);
-                    const uint2 qa = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
-                    const uint2 qb = *reinterpret_cast<const uint2*>(blk + 16 + 16 * ib);
-                    uint4 cv[4];
-                    dequant_subblock_bf16(hd.x, hd.y, ib, qa.x, qa.y, qb.x, qb.y, cv);
                     uint8_t* dst = S.a_slot(slot);
+                    // this thread's two of the slot's four sub-blocks: sub and
+                    // sub + 2, i.e. half `sub` of each atom's 64 K
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + sw128_off(m, sub * 4 + j)) = cv[j];
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        const int sbq = sub + 2 * h2;
+                        const int sbk = (ks % kGSlotsPerStage) * 4 + sbq;  // sub-block within the stage row (0..15)
+                        const uint8_t* blk = S.stage(st) + srow * kGStageRowB + (sbk >> 3) * QMOE_SB_BYTES;
+                        const int ib = sbk & 7;
+                        const uint2 hd = *reinterpret_cast<const uint2*>(blk);
+                        const uint2 qa = *reinterpret_cast<const uint2*>(blk + 8 + 16 * ib);
+                        const uint2 qb = *reinterpret_cast<const uint2*>(blk + 16 + 16 * ib);
+                        uint4 cv[4];
+                        dequant_subblock_bf16(hd.x, hd.y, ib, qa.x, qa.y, qb.x, qb.y, cv);
+                        uint8_t* at = dst + h2 * kGAtomBytes;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(at + sw128_off(m, sub * 4 + j)) = cv[j];
+                    }
                     ptx::fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive(S.s_full(slot));
                     if (dq % kNDqG == 0 && lane == 0) pf_stamp(a, it, 5);
                 }
                 ++it;
-                if ((ks & 7) == 7 || ks == nslots - 1) {
+                if ((ks % kGSlotsPerStage) == kGSlotsPerStage - 1 || ks == nslots - 1) {
                     __syncwarp();
                     if (lane == 0) ptx::mbar_arrive(S.iq_empty(st));
                     ++st_it;
@@ -1230,7 +1240,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     pf_gather_kernel<<<(unsigned)L.rows, 256, 0, s>>>(xb, d.hidden, slot_tok, meta, T, xg);
     a.mode = 0;
     err = encode_2d(&a.bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xg, (unsigned long long)d.hidden,
-                    (unsigned long long)L.rows, (unsigned long long)d.hidden * 2, kGSlotK, kGNMax,
+                    (unsigned long long)L.rows, (unsigned long long)d.hidden * 2, kGAtomK, kGNMax,
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (err != cudaSuccess) return err;
     err = encode_2d(&a.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.gate_up, rb / 2, (unsigned long long)E * 2 * d.inter, rb,
@@ -1292,7 +1302,7 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     }
     a.mode = 1;
     err = encode_2d(&a.bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, h, (unsigned long long)d.inter, (unsigned long long)L.rows,
-                    (unsigned long long)d.inter * 2, kGSlotK, kGNMax, CU_TENSOR_MAP_SWIZZLE_128B);
+                    (unsigned long long)d.inter * 2, kGAtomK, kGNMax, CU_TENSOR_MAP_SWIZZLE_128B);
     if (err != cudaSuccess) return err;
     err = encode_2d(&a.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.down, drb / 2, (unsigned long long)E * d.hidden, drb,
                     kGStageRowB / 2, kGM);
