@@ -179,6 +179,15 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, int t, int MT) 
     return ti;
 }
 
+// (x0 - bias) * scale and (x1 - bias) * scale with sm_100's packed fp32
+// instructions: an exact subtraction of the 2^23 bias, then one rounding.
+__device__ __forceinline__ void sub_mul_f32x2(float& x0, float& x1, float bias, float scale) {
+    asm("{\n .reg .b64 v, b, s;\n mov.b64 v, {%0, %1};\n mov.b64 b, {%2, %2};\n mov.b64 s, {%3, %3};\n"
+        " add.rn.f32x2 v, v, b;\n mul.rn.f32x2 v, v, s;\n mov.b64 {%0, %1}, v;\n}"
+        : "+f"(x0), "+f"(x1)
+        : "f"(-bias), "f"(scale));
+}
+
 // One 32-value sub-block of IQ4_XS (header words h0/h1, qs words q0..q3) to
 // 32 bf16 in natural order, as four 16-byte chunks.  Each code's codebook
 // entry + 128 is placed under the exponent of 2^23 (an exact float 2^23 + b),
@@ -197,9 +206,15 @@ __device__ __forceinline__ void dequant_subblock_bf16(uint32_t h0, uint32_t h1, 
         float v[8];
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-            v[b] = (__uint_as_float(qmoe_prmt(lo, 0x4B000000u, 0x7540u + (uint32_t)b)) - 8388736.0f) * dl;
-            v[4 + b] = (__uint_as_float(qmoe_prmt(hi, 0x4B000000u, 0x7540u + (uint32_t)b)) - 8388736.0f) * dl;
+            v[b] = __uint_as_float(qmoe_prmt(lo, 0x4B000000u, 0x7540u + (uint32_t)b));
+            v[4 + b] = __uint_as_float(qmoe_prmt(hi, 0x4B000000u, 0x7540u + (uint32_t)b));
         }
+        // (v - (2^23 + 128)) * dl, two values per packed instruction (the
+        // same two roundings as the scalar form)
+        sub_mul_f32x2(v[0], v[2], 8388736.0f, dl);
+        sub_mul_f32x2(v[4], v[6], 8388736.0f, dl);
+        sub_mul_f32x2(v[1], v[3], 8388736.0f, dl);
+        sub_mul_f32x2(v[5], v[7], 8388736.0f, dl);
         const __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[2]);  // values 4w, 4w+1
         const __nv_bfloat162 p1 = __floats2bfloat162_rn(v[4], v[6]);  // 4w+2, 4w+3
         const __nv_bfloat162 p2 = __floats2bfloat162_rn(v[1], v[3]);  // 16+4w, 16+4w+1
@@ -1001,46 +1016,33 @@ __global__ void __launch_bounds__(kGvWarps * 32) pf_gv_down_kernel(const __grid_
 // Slot rows in token order: warp per routed group scans every token's ids
 // (held in shared memory) and ranks its hits with a ballot; the shared group
 // lists every token.
-constexpr int kPlaceWarps = 16;
-__global__ void __launch_bounds__(kPlaceWarps * 32) pf_place_kernel(const int32_t* __restrict__ ids,
-                                                                    const float* __restrict__ weights,
-                                                                    const float* __restrict__ shared_logit, int T,
-                                                                    int k, int E, int has_shared,
-                                                                    const int* __restrict__ offsets, int* slot_tok,
-                                                                    float* slot_w) {
-    extern __shared__ short sid[];  // [T][k]
+// Slot rows: a thread per (token, slot) entry takes the next free row of its
+// group, counting the group's size (left by the count and scan kernels)
+// down with an atomic, then a thread per token fills the shared group's rows
+// in token order.  The order within a routed group is the arrival order: a
+// token's results do not depend on its column in a tile (each accumulator
+// column sums over K in the same order), so only the rows' bookkeeping sees
+// it.
+__global__ void __launch_bounds__(256) pf_place_kernel(const int32_t* __restrict__ ids,
+                                                       const float* __restrict__ weights,
+                                                       const float* __restrict__ shared_logit, int T, int k, int E,
+                                                       int has_shared, const int* __restrict__ offsets, int* counts,
+                                                       int* slot_tok, float* slot_w) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int n = T * k;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int g = ids[i];
-        sid[i] = (short)((g >= 0 && g < E) ? g : -1);
-    }
-    __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = blockIdx.x * kPlaceWarps + warp;
-    if (g < E) {
-        const int base = offsets[g];
-        int pos = 0;
+    if (i < n) {
         // Every (token, slot) naming g is placed, so the rows match the counts even when a
         // caller's routing repeats an expert within a token.
-        for (int t0 = 0; t0 < T; t0 += 32) {
-            const int t = t0 + lane;
-            for (int s = 0; s < k; ++s) {
-                const bool hit = t < T && sid[t * k + s] == g;
-                const unsigned b = __ballot_sync(0xffffffffu, hit);
-                if (hit) {
-                    const int r = base + pos + __popc(b & ((1u << lane) - 1u));
-                    slot_tok[r] = t;
-                    slot_w[r] = weights[(size_t)t * k + s];
-                }
-                pos += __popc(b);
-            }
+        const int g = ids[i];
+        if (g >= 0 && g < E) {
+            const int r = offsets[g] + atomicSub(counts + g, 1) - 1;
+            slot_tok[r] = i / k;
+            slot_w[r] = weights[i];
         }
-    } else if (g == E && has_shared) {
-        const int base = offsets[E];
-        for (int t = lane; t < T; t += 32) {
-            slot_tok[base + t] = t;
-            slot_w[base + t] = sigmoid(shared_logit[t]);
-        }
+    } else if (has_shared && i < n + T) {
+        const int t = i - n, base = offsets[E];
+        slot_tok[base + t] = t;
+        slot_w[base + t] = sigmoid(shared_logit[t]);
     }
 }
 
@@ -1205,11 +1207,9 @@ cudaError_t launch_prefill_experts(const __nv_bfloat16* xb, int T, const int32_t
     int4* gv = reinterpret_cast<int4*>(ws + L.gv);
     pf_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, G, has_shared ? T : 0, g_small_group_max.load(), offsets, ntiles, gv,
                                               meta);
-    const size_t place_smem = (size_t)n * sizeof(short);
-    err = smem_opt_in(reinterpret_cast<const void*>(pf_place_kernel), (int)place_smem);
-    if (err != cudaSuccess) return err;
-    pf_place_kernel<<<(unsigned)((G + kPlaceWarps - 1) / kPlaceWarps), kPlaceWarps * 32, place_smem, s>>>(
-        ids, weights, shared_logit, T, k, E, has_shared ? 1 : 0, offsets, slot_tok, slot_w);
+    pf_place_kernel<<<(unsigned)((n + T + 255) / 256), 256, 0, s>>>(ids, weights, shared_logit, T, k, E,
+                                                                 has_shared ? 1 : 0, offsets, counts, slot_tok,
+                                                                 slot_w);
 
     GemmArgs a{};
     a.D = d.hidden;
