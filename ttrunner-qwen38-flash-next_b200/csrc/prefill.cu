@@ -566,42 +566,52 @@ __global__ void pf_convert_kernel(const void* x, int x_f32, size_t n, __nv_bfloa
 // alone would leave SMs idle (small chunks), grid.z splits K into equal
 // chunks whose partials go to part[z] and are summed in chunk order by
 // pf_logit_reduce_kernel: the same bits on every run.
-constexpr int kRtK = 32;
+constexpr int kRtK = 32;   // K per step
+constexpr int kRtM = 128;  // tokens per tile (8 per thread)
+constexpr int kRtN = 64;   // router rows per tile (4 per thread)
 
+// out[t][e] = x[t] . W[e] over this CTA's K chunk, fp32 (x from its bf16 copy), each thread
+// accumulating its 8 x 4 outputs over k in ascending order.
 __global__ void __launch_bounds__(256) pf_router_kernel(const __nv_bfloat16* __restrict__ xb, int T, int D,
                                                         const float* __restrict__ router,
                                                         const float* __restrict__ gate_vec, int E, int k_chunk,
                                                         float* __restrict__ out) {
-    __shared__ __align__(16) float xs[kRtK][64 + 4];
-    __shared__ __align__(16) float rs[kRtK][64 + 4];
-    const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64, tid = threadIdx.x;
+    __shared__ __align__(16) float xs[kRtK][kRtM + 4];
+    __shared__ __align__(16) float rs[kRtK][kRtN + 4];
+    const int t0 = blockIdx.x * kRtM, e0 = blockIdx.y * kRtN, tid = threadIdx.x;
     const int kb = blockIdx.z * k_chunk, nsteps = k_chunk / kRtK;
     const int tr = tid >> 4, tcol = tid & 15;
-    // loader: row lr of the tile, 8 consecutive k at lk
+    // loader: rows lr and lr + 64 of the x tile and row lr of the router tile, 8 consecutive k at lk
     const int lr = tid >> 2, lk = (tid & 3) * 8;
-    const int t = t0 + lr, e = e0 + lr;
-    const __nv_bfloat16* xrow = t < T ? xb + (size_t)t * D + kb + lk : nullptr;
+    const __nv_bfloat16* xrow0 = t0 + lr < T ? xb + (size_t)(t0 + lr) * D + kb + lk : nullptr;
+    const __nv_bfloat16* xrow1 = t0 + lr + 64 < T ? xb + (size_t)(t0 + lr + 64) * D + kb + lk : nullptr;
+    const int e = e0 + lr;
     const float* rrow = e < E ? router + (size_t)e * D + kb + lk : (e == E && gate_vec ? gate_vec + kb + lk : nullptr);
-    uint4 xv4 = make_uint4(0u, 0u, 0u, 0u);
+    uint4 xa = make_uint4(0u, 0u, 0u, 0u), xc = xa;
     float4 r0 = make_float4(0.f, 0.f, 0.f, 0.f), r1 = r0;
-    if (xrow) xv4 = __ldg(reinterpret_cast<const uint4*>(xrow));
+    if (xrow0) xa = __ldg(reinterpret_cast<const uint4*>(xrow0));
+    if (xrow1) xc = __ldg(reinterpret_cast<const uint4*>(xrow1));
     if (rrow) {
         r0 = __ldg(reinterpret_cast<const float4*>(rrow));
         r1 = __ldg(reinterpret_cast<const float4*>(rrow) + 1);
     }
-    float acc[4][4];
+    float acc[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
     for (int st = 0; st < nsteps; ++st) {
         {
-            const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv4);
+            const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xa);
+            const __nv_bfloat162* xq = reinterpret_cast<const __nv_bfloat162*>(&xc);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float2 f = __bfloat1622float2(xp[q]);
+                const float2 g = __bfloat1622float2(xq[q]);
                 xs[lk + 2 * q][lr] = f.x;
                 xs[lk + 2 * q + 1][lr] = f.y;
+                xs[lk + 2 * q][lr + 64] = g.x;
+                xs[lk + 2 * q + 1][lr + 64] = g.y;
             }
             rs[lk + 0][lr] = r0.x;
             rs[lk + 1][lr] = r0.y;
@@ -615,7 +625,8 @@ __global__ void __launch_bounds__(256) pf_router_kernel(const __nv_bfloat16* __r
         __syncthreads();
         if (st + 1 < nsteps) {  // the next step's operands, in flight during this step's arithmetic
             const int off = (st + 1) * kRtK;
-            if (xrow) xv4 = __ldg(reinterpret_cast<const uint4*>(xrow + off));
+            if (xrow0) xa = __ldg(reinterpret_cast<const uint4*>(xrow0 + off));
+            if (xrow1) xc = __ldg(reinterpret_cast<const uint4*>(xrow1 + off));
             if (rrow) {
                 r0 = __ldg(reinterpret_cast<const float4*>(rrow + off));
                 r1 = __ldg(reinterpret_cast<const float4*>(rrow + off) + 1);
@@ -623,11 +634,12 @@ __global__ void __launch_bounds__(256) pf_router_kernel(const __nv_bfloat16* __r
         }
 #pragma unroll 8
         for (int kk = 0; kk < kRtK; ++kk) {
-            const float4 xq = *reinterpret_cast<const float4*>(&xs[kk][tr * 4]);
+            const float4 x0 = *reinterpret_cast<const float4*>(&xs[kk][tr * 8]);
+            const float4 x1 = *reinterpret_cast<const float4*>(&xs[kk][tr * 8 + 4]);
             const float4 rq = *reinterpret_cast<const float4*>(&rs[kk][tcol * 4]);
-            const float xv[4] = {xq.x, xq.y, xq.z, xq.w}, rv[4] = {rq.x, rq.y, rq.z, rq.w};
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w}, rv[4] = {rq.x, rq.y, rq.z, rq.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 8; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i], rv[j], acc[i][j]);
         }
@@ -635,8 +647,8 @@ __global__ void __launch_bounds__(256) pf_router_kernel(const __nv_bfloat16* __r
     }
     float* o = out + (size_t)blockIdx.z * T * (E + 1);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int tt = t0 + tr * 4 + i;
+    for (int i = 0; i < 8; ++i) {
+        const int tt = t0 + tr * 8 + i;
         if (tt >= T) continue;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -659,7 +671,7 @@ __global__ void __launch_bounds__(256) pf_logit_reduce_kernel(const float* __res
 // K chunks of the router GEMM for a chunk of T tokens: enough CTAs to cover
 // the SMs, each chunk a multiple of 256 columns.
 int router_splits(int T, int E, int D) {
-    const int tiles = ((T + 63) / 64) * ((E + 1 + 63) / 64);
+    const int tiles = ((T + kRtM - 1) / kRtM) * ((E + 1 + kRtN - 1) / kRtN);
     int S = 1;
     while (S * 2 * tiles <= 2 * 148 && D % (S * 2 * 256) == 0) S *= 2;
     return S;
@@ -1170,7 +1182,7 @@ cudaError_t launch_prefill_route(const __nv_bfloat16* xb, int T, const qmoe_laye
     const int E = d.n_experts;
     const int S = router_splits(T, E, d.hidden);
     float* logits = reinterpret_cast<float*>(ws + L.logits);
-    dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 1 + 63) / 64), (unsigned)S);
+    dim3 grid((unsigned)((T + kRtM - 1) / kRtM), (unsigned)((E + 1 + kRtN - 1) / kRtN), (unsigned)S);
     pf_router_kernel<<<grid, 256, 0, s>>>(xb, T, d.hidden, w.router, w.gate_vec, E, d.hidden / S,
                                           S > 1 ? reinterpret_cast<float*>(ws + L.part) : logits);
     if (S > 1) {
