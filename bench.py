@@ -399,7 +399,7 @@ def verify_timings(pkg, layers, cfg, dev, tokens=(4, 8), steps: int = 10, warmup
             nbytes = cfg.n_layers * (uniq * expert_b + cfg.shared_bytes)
             gbs = nbytes / (us * 1e-6) / 1e9
             out.append({"tokens": M, "us_per_step": round(us, 2), "us_per_token": round(us / M, 2),
-                        "launches_per_step": 3 * cfg.n_layers, "expected_experts_per_layer": round(uniq, 1),
+                        "launches_per_step": 4 * cfg.n_layers, "expected_experts_per_layer": round(uniq, 1),
                         "bytes_per_step": round(nbytes), "achieved_gbs": round(gbs, 1),
                         "frac_of_measured_hbm": round(gbs / hbm, 4), "device_status": status})
             del g, stack

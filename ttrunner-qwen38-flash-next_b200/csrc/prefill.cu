@@ -669,11 +669,11 @@ __global__ void __launch_bounds__(256) pf_logit_reduce_kernel(const float* __res
 }
 
 // K chunks of the router GEMM for a chunk of T tokens: enough CTAs to cover
-// the SMs, each chunk a multiple of 256 columns.
+// the SMs, each chunk a multiple of 128 columns.
 int router_splits(int T, int E, int D) {
     const int tiles = ((T + kRtM - 1) / kRtM) * ((E + 1 + kRtN - 1) / kRtN);
     int S = 1;
-    while (S * 2 * tiles <= 2 * 148 && D % (S * 2 * 256) == 0) S *= 2;
+    while (S * 2 * tiles <= 2 * 148 && D % (S * 2 * 128) == 0) S *= 2;
     return S;
 }
 
