@@ -758,12 +758,17 @@ int qmoe_moe_block_formats(const void* x, int x_dtype, int n_tokens, const qmoe_
                 fmt_row_bytes(f->sh_down, dims->sh_inter_local) == 0 || !w->sh_gate_up || !w->sh_down)))
         return QMOE_ERR_INVALID_ARG;
     if (dims->inter % 32 || (sh && dims->sh_inter_local % 32)) return QMOE_ERR_UNSUPPORTED;
+    if (!aligned(w->gate_up, 16) || !aligned(w->down, 16) || (sh && (!aligned(w->sh_gate_up, 16) ||
+                                                                     !aligned(w->sh_down, 16))))
+        return QMOE_ERR_ALIGNMENT;
     Ws ws;
     QMOE_TRY(get_ws(workspace, workspace_bytes, dims, n_tokens, &ws));
     cudaStream_t s = (cudaStream_t)stream;
-    QMOE_TRY(run_route(x, x_dtype, n_tokens, w, dims, ws.ids(), ws.weights(), ws.shared(), ws, s));
+    int* xconv = (int*)ws.act();
+    QMOE_TRY(run_route(x, x_dtype, n_tokens, w, dims, ws.ids(), ws.weights(), ws.shared(), ws, s, 0, 0, xconv));
     return cuda_status(launch_fmt_experts(x, x_dtype == QMOE_ACT_F32, n_tokens, *dims, *f, *w, ws.ids(),
-                                          ws.weights(), ws.shared(), ws.h(), ws.L.h_stride, out, ws.status(), s));
+                                          ws.weights(), ws.shared(), ws.h(), ws.L.h_stride, xconv, out,
+                                          ws.status(), s));
 }
 
 int qmoe_prefill_max_tokens(void) { return prefill_max_tokens(); }

@@ -7,7 +7,6 @@
 
 #include <map>
 #include <mutex>
-#include <utility>
 
 #include "../../include/qmoe_b200.h"
 #include "iq4xs.cuh"
@@ -194,8 +193,8 @@ size_t fmt_row_bytes(int fmt, int64_t n);
 cudaError_t launch_fmt_dequant(int fmt, const uint8_t* raw, int64_t n_values, float* out, cudaStream_t s);
 cudaError_t launch_fmt_experts(const void* x, int x_f32, int M, const qmoe_dims& d, const qmoe_formats& f,
                                const qmoe_layer_weights& w, const int32_t* ids, const float* weights,
-                               const float* shared_logit, float* h, int h_stride, float* out, int* status,
-                               cudaStream_t s);
+                               const float* shared_logit, float* h, int h_stride, const int* xconv, float* out,
+                               int* status, cudaStream_t s);
 
 // The hyper-connection mixer (hc.cu).
 size_t hc_workspace_bytes(int M, int hc, int rank);

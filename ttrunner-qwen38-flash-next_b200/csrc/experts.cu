@@ -682,6 +682,264 @@ __global__ void __launch_bounds__(kWarps * 32, 3) down_rows_kernel(ExpertArgs a)
     }
 }
 
+// ---------------------------------------------------------------------------
+// The checkpoint's other expert formats (IQ3_S, IQ4_NL, Q8_0; IQ4_XS too) on
+// the same integer core: each 32-value sub-block becomes eight int8x4 words
+// in the core's pair order (values j and j + 16 side by side, as the block
+// floating-point activation pairs them) and one fp32 scale, then dp2a against
+// the activation.  IQ4_NL codes are laid out as one IQ4_XS sub-block (the
+// same codebook); Q8_0 bytes are the values; IQ3_S grid bytes (odd, 1..15)
+// take their signs as (g ^ m) + (m & 1) per byte, never carrying.
+
+#define QMOE_IQ3S_GRID_DEF __device__ uint32_t g_iq3s_grid_core[512]
+#include "iq3s_grid.inc"
+#undef QMOE_IQ3S_GRID_DEF
+
+struct FmtSel {
+    int gu, dn, sgu, sdn;          // GGML types
+    int gu_rb, dn_rb, sgu_rb, sdn_rb;  // bytes per row
+};
+
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return *reinterpret_cast<const unsigned short*>(p); }
+// four bytes at a 2-byte aligned address
+__device__ __forceinline__ uint32_t ld_w16(const uint8_t* p) { return ld_u16(p) | (ld_u16(p + 2) << 16); }
+
+// Natural-order words N[n] (values 4n .. 4n+3) -> the core's (lo, hi) words.
+__device__ __forceinline__ void pair_order(const uint32_t (&N)[8], uint32_t (&lo)[4], uint32_t (&hi)[4]) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        lo[w] = qmoe_prmt(N[w], N[w + 4], 0x5140u);  // values 4w, 4w+16, 4w+1, 4w+17
+        hi[w] = qmoe_prmt(N[w], N[w + 4], 0x7362u);  // 4w+2, 4w+18, 4w+3, 4w+19
+    }
+}
+
+// Four unsigned grid bytes with sign bits s4 (bit k: byte k negative).
+__device__ __forceinline__ uint32_t signed_bytes(uint32_t g, uint32_t s4) {
+    const uint32_t m01 = (s4 * 0x00204081u) & 0x01010101u;
+    return (g ^ (m01 * 0xFFu)) + m01;
+}
+
+// Sub-block sb of a row in `fmt` as core words and its scale (gguf/quants.py
+// IQ4_XS 112-129, IQ4_NL 101-109, Q8_0 33-37, IQ3_S 132-165).
+__device__ __forceinline__ float fmt_words(int fmt, const uint8_t* row, int sb, const uint32_t* grid,
+                                           uint32_t (&lo)[4], uint32_t (&hi)[4]) {
+    if (fmt == QMOE_FMT_IQ4_XS) {
+        const uint8_t* blk = row + (sb >> 3) * QMOE_SB_BYTES;
+        const int ib = sb & 7;
+        const uint2 h = ldg2(blk), q0 = ldg2(blk + 8 + 16 * ib), q1 = ldg2(blk + 16 + 16 * ib);
+        qmoe_lut8(q0.x, lo[0], hi[0]);
+        qmoe_lut8(q0.y, lo[1], hi[1]);
+        qmoe_lut8(q1.x, lo[2], hi[2]);
+        qmoe_lut8(q1.y, lo[3], hi[3]);
+        return qmoe_half_bits_to_float((uint16_t)(h.x & 0xFFFFu)) * (float)(qmoe_iq4xs_ls(h.x, h.y, ib) - 32);
+    }
+    if (fmt == QMOE_FMT_IQ4_NL) {
+        const uint8_t* blk = row + sb * 18;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) qmoe_lut8(ld_w16(blk + 2 + 4 * w), lo[w], hi[w]);
+        return qmoe_half_bits_to_float((uint16_t)ld_u16(blk));
+    }
+    uint32_t N[8];
+    if (fmt == QMOE_FMT_Q8_0) {
+        const uint8_t* blk = row + sb * 34;
+#pragma unroll
+        for (int n = 0; n < 8; ++n) N[n] = ld_w16(blk + 2 + 4 * n);
+        pair_order(N, lo, hi);
+        return qmoe_half_bits_to_float((uint16_t)ld_u16(blk));
+    }
+    // IQ3_S
+    const uint8_t* blk = row + (sb >> 3) * 110;
+    const int ib32 = sb & 7;
+    const uint32_t qs01 = ld_w16(blk + 2 + 8 * ib32), qs23 = ld_w16(blk + 6 + 8 * ib32);
+    const uint32_t h = blk[66 + ib32];
+    const uint32_t sg = ld_w16(blk + 74 + 4 * ib32);
+    const int sc = (blk[106 + ib32 / 2] >> (4 * (ib32 % 2))) & 0xF;
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const uint32_t qw = l < 2 ? qs01 : qs23;
+        const int sh = (l & 1) * 16;
+        const uint32_t i1 = ((qw >> sh) & 0xFFu) | ((h << (8 - 2 * l)) & 256u);
+        const uint32_t i2 = ((qw >> (sh + 8)) & 0xFFu) | ((h << (7 - 2 * l)) & 256u);
+        const uint32_t s8 = (sg >> (8 * l)) & 0xFFu;
+        N[2 * l] = signed_bytes(grid[i1], s8 & 0xFu);
+        N[2 * l + 1] = signed_bytes(grid[i2], s8 >> 4);
+    }
+    pair_order(N, lo, hi);
+    return qmoe_half_bits_to_float((uint16_t)ld_u16(blk)) * (1.0f + 2.0f * (float)sc);
+}
+
+// gate|up + SwiGLU on formatted weights: gateup_kernel's plan and task
+// layout (warp per row pair of a distinct expert; x converted by the route
+// launch), each row pair's sub-blocks decoded once for all its tokens.
+template <int MAXM, int SBL>
+__global__ void __launch_bounds__(kWarps * 32) fmt_gateup_kernel(ExpertArgs a, FmtSel f) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ Plan plan;
+    __shared__ uint32_t s_grid[512];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int D = a.D, M = a.M;
+    const int nsb = D >> 5;
+    int* xq = reinterpret_cast<int*>(smem);
+    float* xs = reinterpret_cast<float*>(xq + (size_t)M * nsb * 16);
+    int* owner = reinterpret_cast<int*>(xs + (size_t)M * nsb);
+    for (int i = tid; i < 512; i += blockDim.x) s_grid[i] = g_iq3s_grid_core[i];
+    build_plan(a, plan, owner);
+    {
+        const int n16 = M * nsb * 68 / 16;
+        const uint4* src = reinterpret_cast<const uint4*>(a.xconv);
+        uint4* dst = reinterpret_cast<uint4*>(smem);
+        constexpr int U = 8;
+        for (int i0 = tid; i0 < n16; i0 += blockDim.x * U) {
+            uint4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (i0 + u * (int)blockDim.x < n16) v[u] = __ldcg(src + i0 + u * blockDim.x);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (i0 + u * (int)blockDim.x < n16) dst[i0 + u * blockDim.x] = v[u];
+        }
+    }
+    __syncthreads();
+
+    const int n_routed = plan.n;
+    const int has_sh = (a.sh_gate_up != nullptr && a.sh_I_loc > 0) ? 1 : 0;
+    const int T = n_routed * a.I_loc + has_sh * a.sh_I_loc;
+    const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
+    for (int t = gw; t < T; t += nw) {
+        const uint8_t *grow, *urow;
+        int u, r, fmt;
+        if (t < n_routed * a.I_loc) {
+            u = t / a.I_loc;
+            r = t - u * a.I_loc;
+            grow = a.gate_up + (size_t)plan.expert[u] * a.gu_expert_bytes + (size_t)r * f.gu_rb;
+            urow = grow + (size_t)a.I_loc * f.gu_rb;
+            fmt = f.gu;
+        } else {
+            u = n_routed;
+            r = t - n_routed * a.I_loc;
+            grow = a.sh_gate_up + (size_t)r * f.sgu_rb;
+            urow = grow + (size_t)a.sh_I_loc * f.sgu_rb;
+            fmt = f.sgu;
+        }
+        uint32_t glo[SBL][4], ghi[SBL][4], ulo[SBL][4], uhi[SBL][4];
+        float dg[SBL], du[SBL];
+#pragma unroll
+        for (int i = 0; i < SBL; ++i) {
+            const int b = lane + 32 * i;
+            if (b < nsb) {
+                dg[i] = fmt_words(fmt, grow, b, s_grid, glo[i], ghi[i]);
+                du[i] = fmt_words(fmt, urow, b, s_grid, ulo[i], uhi[i]);
+            } else {
+                dg[i] = du[i] = 0.0f;
+            }
+        }
+        const uint32_t tmask = (u < n_routed) ? plan.mask[u] : ((M >= 32) ? 0xffffffffu : ((1u << M) - 1u));
+        for (uint32_t mm = tmask; mm; mm &= mm - 1u) {
+            const int m = __ffs(mm) - 1;
+            float accg = 0.0f, accu = 0.0f;
+#pragma unroll
+            for (int i = 0; i < SBL; ++i) {
+                const int b = lane + 32 * i;
+                if (b >= nsb) continue;
+                int xp[16];
+                const int4* src = reinterpret_cast<const int4*>(xq + ((size_t)m * nsb + b) * 16);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const int4 w4 = src[v];
+                    xp[4 * v] = w4.x;
+                    xp[4 * v + 1] = w4.y;
+                    xp[4 * v + 2] = w4.z;
+                    xp[4 * v + 3] = w4.w;
+                }
+                const float st = xs[m * nsb + b];
+                accg = fmaf(dg[i] * st, (float)subblock_dot_lut(glo[i], ghi[i], xp), accg);
+                accu = fmaf(du[i] * st, (float)subblock_dot_lut(ulo[i], uhi[i], xp), accu);
+            }
+            const float g = warp_sum(accg);
+            const float uu = warp_sum(accu);
+            if (lane == 0) {
+                const int slot = (u < n_routed) ? plan.slot[u][m] : a.k;
+                a.h[((size_t)m * (a.k + 1) + slot) * a.h_stride + r] = silu(g) * uu;
+            }
+        }
+    }
+}
+
+// down + combine on formatted weights: down_kernel's layout (warp per output
+// row, lanes over (unit, sub-block) pairs, h in block floating point), each
+// pair decoded once for all the unit's tokens.
+template <int MAXM>
+__global__ void __launch_bounds__(kWarps * 32) fmt_down_kernel(ExpertArgs a, FmtSel f) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ DownShared sh;
+    __shared__ uint32_t s_grid[512];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int M = a.M, K1 = a.k + 1;
+    const int I_max = a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc;
+    const int nsbh = I_max >> 5;
+    int* hq = reinterpret_cast<int*>(smem);
+    float* hs = reinterpret_cast<float*>(hq + (size_t)M * K1 * nsbh * 16);
+    int* owner = reinterpret_cast<int*>(hs + (size_t)M * K1 * nsbh);
+    for (int i = tid; i < 512; i += blockDim.x) s_grid[i] = g_iq3s_grid_core[i];
+    down_prologue(a, sh, hq, hs, owner);
+    const Plan& plan = sh.plan;
+    const int has_sh = (a.sh_down != nullptr && a.sh_I_loc > 0) ? 1 : 0;
+    const int nsb_r = a.I_loc >> 5, nsb_s = a.sh_I_loc >> 5;
+    const int n_routed = plan.n;
+    const int P = n_routed * nsb_r + has_sh * nsb_s;
+    const uint32_t all = (M >= 32) ? 0xffffffffu : ((1u << M) - 1u);
+    const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
+    for (int j = gw; j < a.D; j += nw) {
+        float acc[MAXM];
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
+        for (int p = lane; p < P; p += 32) {
+            int u, t, fmt;
+            const uint8_t* row;
+            if (p < n_routed * nsb_r) {
+                u = p / nsb_r;
+                t = p - u * nsb_r;
+                row = a.down + (size_t)plan.expert[u] * a.dn_expert_bytes + (size_t)j * f.dn_rb;
+                fmt = f.dn;
+            } else {
+                u = n_routed;
+                t = p - n_routed * nsb_r;
+                row = a.sh_down + (size_t)j * f.sdn_rb;
+                fmt = f.sdn;
+            }
+            uint32_t lo[4], hi[4];
+            const float dl = fmt_words(fmt, row, t, s_grid, lo, hi);
+            for (uint32_t mm = u < n_routed ? plan.mask[u] : all; mm; mm &= mm - 1u) {
+                const int m = __ffs(mm) - 1;
+                const int s = (u < n_routed) ? plan.slot[u][m] : a.k;
+                const size_t hb = ((size_t)m * K1 + s) * nsbh + t;
+                int xp[16];
+                const int4* src = reinterpret_cast<const int4*>(hq + hb * 16);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const int4 w4 = src[v];
+                    xp[4 * v] = w4.x;
+                    xp[4 * v + 1] = w4.y;
+                    xp[4 * v + 2] = w4.z;
+                    xp[4 * v + 3] = w4.w;
+                }
+                const float fs = sh.w[m][s] * dl * hs[hb];
+                const float S = (float)subblock_dot_lut(lo, hi, xp);
+#pragma unroll
+                for (int q = 0; q < MAXM; ++q)
+                    if (q == m) acc[q] = fmaf(fs, S, acc[q]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+            if (m < M) {
+                const float v = warp_sum(acc[m]);
+                if (lane == 0) a.out[(size_t)m * a.D + j] = v;
+            }
+        }
+    }
+}
+
 template <typename K>
 cudaError_t launch_with_smem(K kernel, unsigned grid, size_t smem, const ExpertArgs& a,
                              cudaStream_t s) {
@@ -776,6 +1034,94 @@ cudaError_t launch_down(const ExpertArgs& a, cudaStream_t s) {
     if (a.M <= 4) return launch_down_m<4>(a, s);
     if (a.M <= 8) return launch_down_m<8>(a, s);
     return launch_down_m<16>(a, s);
+}
+
+// The block's expert stages on formatted weights (x already converted by the
+// route launch into `xconv`).
+cudaError_t launch_fmt_experts(const void* x, int x_f32, int M, const qmoe_dims& d, const qmoe_formats& fm,
+                               const qmoe_layer_weights& w, const int32_t* ids, const float* weights,
+                               const float* shared_logit, float* h, int h_stride, const int* xconv, float* out,
+                               int* status, cudaStream_t s) {
+    ExpertArgs a{};
+    a.x = x;
+    a.x_f32 = x_f32;
+    a.M = M;
+    a.D = d.hidden;
+    a.k = d.top_k;
+    a.e_lo = 0;
+    a.e_hi = d.n_experts;
+    a.E = d.n_experts;
+    a.ids = ids;
+    a.weights = weights;
+    a.shared_logit = d.sh_inter_local > 0 ? shared_logit : nullptr;
+    a.gate_up = (const uint8_t*)w.gate_up;
+    a.I_loc = d.inter;
+    a.sh_gate_up = d.sh_inter_local > 0 ? (const uint8_t*)w.sh_gate_up : nullptr;
+    a.sh_I_loc = d.sh_inter_local;
+    a.h = h;
+    a.h_stride = h_stride;
+    a.xconv = xconv;
+    a.down = (const uint8_t*)w.down;
+    a.sh_down = d.sh_inter_local > 0 ? (const uint8_t*)w.sh_down : nullptr;
+    a.out = out;
+    a.status = status;
+    FmtSel f{};
+    f.gu = fm.gate_up;
+    f.dn = fm.down;
+    f.sgu = fm.sh_gate_up;
+    f.sdn = fm.sh_down;
+    f.gu_rb = (int)fmt_row_bytes(fm.gate_up, d.hidden);
+    f.dn_rb = (int)fmt_row_bytes(fm.down, d.inter);
+    f.sgu_rb = d.sh_inter_local > 0 ? (int)fmt_row_bytes(fm.sh_gate_up, d.hidden) : 0;
+    f.sdn_rb = d.sh_inter_local > 0 ? (int)fmt_row_bytes(fm.sh_down, d.sh_inter_local) : 0;
+    a.gu_expert_bytes = (size_t)2 * d.inter * f.gu_rb;
+    a.dn_expert_bytes = (size_t)d.hidden * f.dn_rb;
+
+    const int nsb = d.hidden >> 5;
+    const size_t smem_g = (size_t)M * nsb * 68 + (size_t)d.n_experts * 4;
+    const long tasks = (long)(M * d.top_k + 1) * (d.inter > d.sh_inter_local ? d.inter : d.sh_inter_local);
+    unsigned grid = (unsigned)((tasks + kWarps - 1) / kWarps);
+    if (M > 1) grid = min(grid, (unsigned)device_sm_count() * 3u);
+    const int sbl = (nsb + 31) / 32;
+    cudaError_t err;
+    auto gu = [&](auto kern) {
+        cudaError_t e = smem_opt_in(reinterpret_cast<const void*>(kern), (int)smem_g);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, kWarps * 32, smem_g, s>>>(a, f);
+        return cudaGetLastError();
+    };
+#define QMOE_FMT_GU(MM)                                               \
+    switch (sbl) {                                                     \
+        case 1: err = gu(fmt_gateup_kernel<MM, 1>); break;             \
+        case 2: err = gu(fmt_gateup_kernel<MM, 2>); break;             \
+        case 3: err = gu(fmt_gateup_kernel<MM, 3>); break;             \
+        default: err = gu(fmt_gateup_kernel<MM, 4>); break;            \
+    }
+    if (M <= 1) { QMOE_FMT_GU(1) } else if (M <= 4) { QMOE_FMT_GU(4) } else if (M <= 8) { QMOE_FMT_GU(8) } else { QMOE_FMT_GU(16) }
+#undef QMOE_FMT_GU
+    if (err != cudaSuccess) return err;
+
+    const int I_max = d.inter > d.sh_inter_local ? d.inter : d.sh_inter_local;
+    const size_t smem_d = (size_t)M * (d.top_k + 1) * (I_max >> 5) * 68 + (size_t)d.n_experts * 4;
+    if (M > 1) {
+        a.hconv = h;
+        a.hconv_stride = h_stride;
+        const int nb = M * (d.top_k + 1) * (I_max >> 5);
+        convert_h_kernel<<<(unsigned)((nb + kWarps - 1) / kWarps), kWarps * 32, 0, s>>>(a);
+        err = cudaGetLastError();
+        if (err != cudaSuccess) return err;
+    }
+    const unsigned grid_d = (unsigned)((d.hidden + kWarps - 1) / kWarps);
+    auto dn = [&](auto kern) {
+        cudaError_t e = smem_opt_in(reinterpret_cast<const void*>(kern), (int)smem_d);
+        if (e != cudaSuccess) return e;
+        kern<<<grid_d, kWarps * 32, smem_d, s>>>(a, f);
+        return cudaGetLastError();
+    };
+    if (M <= 1) return dn(fmt_down_kernel<1>);
+    if (M <= 4) return dn(fmt_down_kernel<4>);
+    if (M <= 8) return dn(fmt_down_kernel<8>);
+    return dn(fmt_down_kernel<16>);
 }
 
 }  // namespace qmoe
