@@ -207,7 +207,13 @@ __global__ void __launch_bounds__(kWarps * 32, (MAXM == 1 || SBL > 2) ? 1 : 3) g
         for (int i = 0; i < SBL; ++i) {
             const int b = lane + 32 * i;
 #pragma unroll
-            for (int p = 0; p < 16; ++p) xr[i][p] = b < nsb ? xq[b * 16 + p] : 0;
+            for (int v = 0; v < 4; ++v) {
+                const int4 w4 = b < nsb ? reinterpret_cast<const int4*>(xq + b * 16)[v] : make_int4(0, 0, 0, 0);
+                xr[i][4 * v] = w4.x;
+                xr[i][4 * v + 1] = w4.y;
+                xr[i][4 * v + 2] = w4.z;
+                xr[i][4 * v + 3] = w4.w;
+            }
             xsr[i] = b < nsb ? xs[b] : 0.0f;
         }
     }
@@ -970,10 +976,10 @@ cudaError_t launch_gateup_m(const ExpertArgs& a, cudaStream_t s) {
     const long tasks = (long)n_units * (a.I_loc > a.sh_I_loc ? a.I_loc : a.sh_I_loc);
     unsigned grid = (unsigned)((tasks + kWarps - 1) / kWarps);
     const int sbl = (nsb + 31) / 32;
-    // Several tokens: every CTA converts all of x and plans all the experts
-    // first, so one wave of resident CTAs takes the row pairs in strides (a
-    // second, partial wave would repeat that work for a few row pairs).
-    if (a.M > 1) grid = min(grid, (unsigned)(device_sm_count() * gateup_resident<MAXM>(sbl, smem)));
+    // Every CTA copies the converted x and plans the experts first, so one
+    // wave of resident CTAs takes the row pairs in strides (a second, partial
+    // wave would repeat that work for a few row pairs).
+    grid = min(grid, (unsigned)(device_sm_count() * gateup_resident<MAXM>(sbl, smem)));
     switch (sbl) {
         case 1: return launch_with_smem(gateup_kernel<MAXM, 1>, grid, smem, a, s);
         case 2: return launch_with_smem(gateup_kernel<MAXM, 2>, grid, smem, a, s);
@@ -988,7 +994,8 @@ cudaError_t launch_down_m(const ExpertArgs& a, cudaStream_t s) {
     const size_t smem = (size_t)a.M * (a.k + 1) * (I_max >> 5) * (16 * 4 + 4) +
                         (size_t)(a.e_hi - a.e_lo) * 4;
     const unsigned grid = (unsigned)((a.D + kWarps - 1) / kWarps);
-    if (a.M > 1 && a.hconv) {
+    if (a.hconv) {
+        // h to block floating point once (not once per CTA), then the CTAs copy it
         const int nb = a.M * (a.k + 1) * (I_max >> 5);
         convert_h_kernel<<<(unsigned)((nb + kWarps - 1) / kWarps), kWarps * 32, 0, s>>>(a);
         cudaError_t err = cudaGetLastError();
