@@ -25,7 +25,7 @@ namespace {
 template <int MAXM, int kRouteWarps>
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
     extern __shared__ __align__(16) float xs[];  // [M][D]
-    __shared__ float s_cv[kRouteWarps][kCandCap];
+    __shared__ __align__(16) float s_cv[kRouteWarps][kCandCap];
     __shared__ int s_ci[kRouteWarps][kCandCap];
     __shared__ float s_sv[kRouteWarps][kMaxTopK];
     __shared__ int s_si[kRouteWarps][kMaxTopK];
@@ -98,6 +98,99 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+
+    if (MAXM == 1 && M == 1 && !a.thr_mode && E > 0 && E % (32 * kRouteWarps) == 0 &&
+        E / (32 * kRouteWarps) <= 8) {
+        // One token: the CTA's warps share it.  Warp w ranks ids w*E/W ..,
+        // keys (p bits << 32 | ~id) with p = exp(l - l_max); each warp's k-th
+        // best lane maximum is a lower bound of the top k (k distinct keys
+        // reach it), so the largest of those bounds, T0, is one too, and only
+        // keys >= T0 (about k to 2k) are ranked: ties go to the lower id as
+        // in warp_topk.
+        __shared__ float s_mx[kRouteWarps];
+        __shared__ unsigned long long s_t[kRouteWarps];
+        __shared__ int s_n;
+        const int npl = E / (32 * kRouteWarps);
+        const int id0 = warp * 32 * npl + lane;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __ldcg(a.logits + id0 + 32 * (j < npl ? j : npl - 1));
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j < npl) {
+                if (v[j] != v[j]) v[j] = -INFINITY;  // NaN ranks last
+                mx = fmaxf(mx, v[j]);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) s_mx[warp] = mx;
+        if (tid == 0) s_n = 0;
+        __syncthreads();
+        float lmax = s_mx[0];
+#pragma unroll
+        for (int w = 1; w < kRouteWarps; ++w) lmax = fmaxf(lmax, s_mx[w]);
+        unsigned long long key[8], best = 0ull;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            key[j] = 0ull;
+            if (j < npl) {
+                const unsigned id = (unsigned)(id0 + 32 * j);
+                key[j] = ((unsigned long long)__float_as_uint(expf(v[j] - lmax)) << 32) | (0xFFFFFFFFu - id);
+                best = key[j] > best ? key[j] : best;
+            }
+        }
+        int gt = 0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) gt += __shfl_sync(0xffffffffu, best, i) > best ? 1 : 0;
+        const unsigned selb = __ballot_sync(0xffffffffu, gt == a.k - 1);
+        const unsigned long long tw = __shfl_sync(0xffffffffu, best, __ffs(selb) - 1);
+        if (lane == 0) s_t[warp] = tw;
+        __syncthreads();
+        unsigned long long t0 = s_t[0];
+#pragma unroll
+        for (int w = 1; w < kRouteWarps; ++w) t0 = s_t[w] > t0 ? s_t[w] : t0;
+        unsigned long long* cand = reinterpret_cast<unsigned long long*>(&s_cv[0][0]);
+        constexpr int kCap = kRouteWarps * kCandCap / 2;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j < npl && key[j] >= t0) {
+                const int pos = atomicAdd(&s_n, 1);
+                if (pos < kCap) cand[pos] = key[j];
+            }
+        }
+        __syncthreads();
+        const int n = s_n;
+        if (warp == 0) {
+            float lm = lmax;
+            if (n <= kCap) {
+                for (int c = lane; c < n; c += 32) {
+                    const unsigned long long ck = cand[c];
+                    int r = 0;
+                    for (int j = 0; j < n; ++j) r += cand[j] > ck ? 1 : 0;
+                    if (r < a.k) {
+                        s_sv[0][r] = __uint_as_float((unsigned)(ck >> 32));
+                        s_si[0][r] = (int)(0xFFFFFFFFu - (unsigned)ck);
+                    }
+                }
+                __syncwarp();
+            } else {  // long runs of ties: the one-warp selection
+                lm = warp_topk(a.logits, E, a.k, s_cv[0], s_ci[0], s_sv[0], s_si[0]);
+            }
+            const float e = lane < a.k ? s_sv[0][lane] : 0.0f;
+            const float sum = warp_sum(e);
+            if (lane < a.k) {
+                if (!(fabsf(lm) <= 3.0e38f)) record_status(a.status, QMOE_ERR_NOT_FINITE);
+                a.ids[lane] = s_si[0][lane];
+                a.weights[lane] = e / sum;
+            }
+            if (lane == 0 && a.shared_logit) a.shared_logit[0] = a.gate_vec ? __ldcg(a.logits + E) : 0.0f;
+        }
+        __syncthreads();
+        if (tid == 0) *a.counter = 0u;
+        return;
+    }
 
     for (int m = warp; m < M; m += kRouteWarps) {
         const float* lg = a.logits + (size_t)m * (E + 1);
