@@ -5,8 +5,9 @@ importing the reference, bitwise) and against the oracle's C restatement on ever
 loads (IQ3_S gate|up, IQ4_NL down, IQ3_S / Q8_0 shared expert; tt/plan.py:90-103) against the
 reference's `_moe` (reference/model.py:387-417) and the oracle at the checkpoint's dimensions.
 
-Tolerance of the block: relative max error 1e-2 of max |out| (fp32 dots against the reference's
-fp32 matmuls; the measured error is near 1e-6)."""
+Tolerance of the block: relative max error 1e-2 of max |out| (the block runs on the integer core:
+int8 weight words against x and h in block floating point, int16 mantissas per 32 values, then
+fp32 accumulation, against the reference's fp32 matmuls)."""
 
 from __future__ import annotations
 
