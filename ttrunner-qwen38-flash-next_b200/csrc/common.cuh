@@ -338,6 +338,39 @@ __device__ __forceinline__ int warp_block_fp(float v, float* step) {
     return (q & 0xFFFF) | (hi << 16);
 }
 
+// warp_block_fp for N blocks at once (v[i]: this lane's value of block i),
+// the same arithmetic step by step for every block before the next step, so
+// the blocks' warp reductions and shuffles are in flight together instead of
+// one block's chain after another's.
+template <int N>
+__device__ __forceinline__ void warp_block_fp_n(const float (&v)[N], int (&pw)[N], float (&step)[N]) {
+    unsigned mb[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) mb[i] = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v[i])));
+    int q[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const int E = (int)(mb[i] >> 23);
+        q[i] = 0;
+        step[i] = 0.0f;
+        if (E >= 255) {
+            step[i] = __uint_as_float(0x7fc00000u);
+        } else if (E >= 1) {
+            const int k = 140 - E;
+            const int k1 = k >> 1, k2 = k - k1;
+            const float s1 = __uint_as_float((unsigned)(127 + k1) << 23);
+            const float s2 = __uint_as_float((unsigned)(127 + k2) << 23);
+            q[i] = __float_as_int(fmaf(v[i] * s1, s2, 12582912.0f)) - 0x4B400000;
+            step[i] = E >= 14 ? __uint_as_float((unsigned)(E - 13) << 23) : __uint_as_float(1u << (E + 9));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const int hi = __shfl_down_sync(0xffffffffu, q[i], 16);
+        pw[i] = (q[i] & 0xFFFF) | (hi << 16);
+    }
+}
+
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 __device__ __forceinline__ float sigmoid(float z) { return 1.0f / (1.0f + expf(-z)); }
 

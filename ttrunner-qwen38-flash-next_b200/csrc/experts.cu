@@ -113,7 +113,8 @@ __device__ void build_plan(const ExpertArgs& a, Plan& p, int* owner /* smem [E] 
 
 // Convert n 32-value blocks to block floating point, one warp per block, with
 // NB blocks' loads issued per warp before any conversion (one memory round
-// trip per NB * kWarps blocks instead of one per block).
+// trip per NB * kWarps blocks instead of one per block) and the NB blocks'
+// reductions and shuffles issued together.
 // load(b, lane) -> float: value `lane` of block b; store(b, lane, pair, step).
 template <int NB, typename LoadF, typename StoreF>
 __device__ __forceinline__ void convert_blocks(int n, LoadF load, StoreF store) {
@@ -125,14 +126,13 @@ __device__ __forceinline__ void convert_blocks(int n, LoadF load, StoreF store) 
             const int b = b0 + i * kWarps;
             v[i] = b < n ? load(b, lane) : 0.0f;
         }
+        int pw[NB];
+        float st[NB];
+        warp_block_fp_n<NB>(v, pw, st);
 #pragma unroll
         for (int i = 0; i < NB; ++i) {
             const int b = b0 + i * kWarps;
-            if (b < n) {
-                float st;
-                const int pw = warp_block_fp(v[i], &st);
-                store(b, lane, pw, st);
-            }
+            if (b < n) store(b, lane, pw[i], st[i]);
         }
     }
 }
