@@ -406,8 +406,10 @@ int qmoe_dequant_f32(int format, const void* blocks, int64_t n_values, float* ou
  * out as the IQ4_XS ones are (gate_up [E][2I rows], down [E][D rows], rows of
  * qmoe_format_row_bytes bytes).  Unsharded dims only (the whole expert range
  * and intermediate width); shared expert optional (sh_inter_local = 0).
- * Routing is the exact top-k; each 32-value block is decoded with the
- * reference's arithmetic and dotted in fp32.  out [M, hidden] fp32. */
+ * Routing is the exact top-k; each 32-value sub-block becomes int8 words and
+ * a scale (the codebook or grid values, signs applied) dotted with x and h in
+ * block floating point, as the IQ4_XS path does.  Every weight tensor 16-byte
+ * aligned (QMOE_ERR_ALIGNMENT otherwise).  out [M, hidden] fp32. */
 int qmoe_moe_block_formats(const void* x, int x_dtype, int n_tokens, const qmoe_layer_weights* w,
                            const qmoe_dims* dims, const qmoe_formats* formats, float* out,
                            void* workspace, size_t workspace_bytes, void* stream);
