@@ -156,3 +156,34 @@ def test_prefill_small_groups_both_paths(pkg, oracle, c1, T):
     assert oracle.max_rel_err(tc.cpu().numpy(), ref["out"]) <= TOL
     assert oracle.max_rel_err(gv.cpu().numpy(), ref["out"]) <= TOL
     assert oracle.max_rel_err(gv.cpu().numpy(), tc.cpu().numpy()) <= TOL
+
+
+def test_prefill_pipeline_trace_opt_in(pkg, c1):
+    """qmoe_prefill_trace: off by default; when on, CTA 0 of the grouped GEMM stamps its
+    pipeline clock per A slot into workspace bytes 256 .. 4351 (the MMA thread's waits and
+    issues of the first slots non-zero and ordered); the output is the same either way, up to the
+    order of the scatter-adds."""
+    hl, dl, layer = c1
+    lib = pkg._lib.lib
+    x = _x(256, seed=77).cuda()
+    prev_small = lib.qmoe_prefill_small_group_max(0)
+    try:
+        assert lib.qmoe_prefill_trace(-1) == 0
+        ws = pkg.moe.prefill_workspace_for(layer.dims, 256, x.device)
+        ws.buf[256:256 + 64 * 64].zero_()
+        plain = layer.prefill(x).clone()
+        torch.cuda.synchronize()
+        assert int(ws.buf[256:256 + 64 * 64].count_nonzero()) == 0
+        assert lib.qmoe_prefill_trace(1) == 0
+        traced = layer.prefill(x).clone()
+        torch.cuda.synchronize()
+        tr = ws.buf[256:256 + 64 * 64].view(torch.int64).view(64, 8).cpu().numpy()
+    finally:
+        lib.qmoe_prefill_trace(0)
+        lib.qmoe_prefill_small_group_max(prev_small)
+    assert lib.qmoe_prefill_trace(-1) == 0
+    ws.raise_if_error("prefill")
+    # slot 0: MMA thread past its wait (event 1), MMAs issued (event 3)
+    assert tr[0, 1] > 0 and tr[0, 3] >= tr[0, 1]
+    # the same result up to the order of the scatter-adds (float atomics from several CTAs)
+    assert float((plain - traced).abs().max()) <= 1e-5 * float(plain.abs().max())
