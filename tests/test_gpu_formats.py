@@ -139,3 +139,28 @@ def test_formats_rejects_bad_arguments(pkg, small_layer):
     out = torch.empty(64, dtype=torch.float32, device="cuda")
     assert pkg._lib.lib.qmoe_dequant_f32(99, raw.data_ptr(), 32, out.data_ptr(), None) != 0
     assert pkg._lib.lib.qmoe_dequant_f32(8, raw.data_ptr(), 33, out.data_ptr(), None) != 0
+
+
+@pytest.mark.parametrize("formats", [(21, 8, 21, 8), (20, 20, 20, 20), (8, 8, 8, 8), (23, 21, 8, 20)],
+                         ids=["iq3s-q8_0", "iq4nl", "q8_0", "mixed"])
+def test_block_other_format_mixes_match_oracle(pkg, oracle, formats):
+    """Other mixes the block accepts: the checkpoint's first layers (Q8_0 down), all IQ4_NL, all
+    Q8_0, and a mix with IQ3_S down rows; seeded bytes, the oracle decoding the same bytes."""
+    E, D, I, Ish = 64, 512, 256, 256
+    fg, fd, fsg, fsd = formats
+    seed = 50 + fg + fd
+    lay = {
+        "formats": formats,
+        "gate_up": oracle.synth_format_bytes(fg, seed, 1, E * 2 * I, D, 2e-4).reshape(E, 2 * I, -1),
+        "down": oracle.synth_format_bytes(fd, seed, 2, E * D, I, 2e-4).reshape(E, D, -1),
+        "sh_gate_up": oracle.synth_format_bytes(fsg, seed, 3, 2 * Ish, D, 2e-4),
+        "sh_down": oracle.synth_format_bytes(fsd, seed, 4, D, Ish, 2e-4),
+        "router": oracle.synth_f32(seed, 5, E * D, 0.02).reshape(E, D),
+        "gate_vec": oracle.synth_f32(seed, 6, D, 0.02),
+    }
+    d = _layer_dev(lay)
+    for m in (1, 5):
+        x = (torch.randn(m, D, generator=torch.Generator().manual_seed(seed + m)) * 0.5).to(torch.bfloat16)
+        out = _run(pkg, d, x, 10)
+        assert np.isfinite(out).all()
+        assert _rel(out, _oracle_block(oracle, lay, x, 10)) < TOL
