@@ -23,6 +23,7 @@ from .moe import (
     route_topk,
     shared_expert,
 )
+from .gguf_load import CheckpointMoE, GGUFCheckpoint, load_moe_layer, moe_layer_bytes
 from .hc import gated_residual_mix, reinject
 from .stack import MoEStack
 from .weights import (
@@ -43,4 +44,8 @@ __all__ = [
     "reinject",
     "dequant",
     "moe_block_formats",
+    "GGUFCheckpoint",
+    "CheckpointMoE",
+    "load_moe_layer",
+    "moe_layer_bytes",
 ]
