@@ -115,3 +115,44 @@ def test_checkpoint_layer_on_gpu_matches_oracle(pkg, oracle, ckpt_files, layer_b
         out = moe(x.cuda().reshape(1, 1, m, D)).float().cpu().numpy().reshape(m, D)
         ref = oracle.moe_forward(x.float().numpy(), src, 10)["out"]
         assert np.abs(out - ref).max() / np.abs(ref).max() < 1e-2
+
+
+def test_reader_metadata_types_and_alignment(pkg, tmp_path):
+    """Every scalar type, strings, arrays and a non-default `general.alignment` (the tensor-data
+    section starts at the next multiple of it), against the gguf package's reader."""
+    path = tmp_path / "meta.gguf"
+    w = gguf.GGUFWriter(str(path), "qwen4exp")
+    w.add_custom_alignment(64)
+    w.add_uint8("k.u8", 200)
+    w.add_int8("k.i8", -5)
+    w.add_uint16("k.u16", 60000)
+    w.add_int16("k.i16", -30000)
+    w.add_uint32("k.u32", 4000000000)
+    w.add_int32("k.i32", -2000000000)
+    w.add_float32("k.f32", 0.5)
+    w.add_bool("k.bool", True)
+    w.add_uint64("k.u64", 2 ** 40)
+    w.add_int64("k.i64", -(2 ** 40))
+    w.add_float64("k.f64", 0.25)
+    w.add_string("k.str", "héllo")
+    w.add_array("k.arr_i32", [1, -2, 3])
+    w.add_array("k.arr_f32", [0.5, 1.5])
+    w.add_tensor("t.a", np.arange(12, dtype=np.float32).reshape(3, 4))
+    w.add_tensor("t.b", np.arange(8, dtype=np.float32))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    with pkg.GGUFCheckpoint(path) as ck:
+        m = ck.metadata
+        assert (m["k.u8"], m["k.i8"], m["k.u16"], m["k.i16"]) == (200, -5, 60000, -30000)
+        assert (m["k.u32"], m["k.i32"], m["k.u64"], m["k.i64"]) == (4000000000, -2000000000, 2 ** 40, -(2 ** 40))
+        assert (m["k.f32"], m["k.f64"], m["k.bool"], m["k.str"]) == (0.5, 0.25, True, "héllo")
+        assert m["k.arr_i32"] == [1, -2, 3] and m["k.arr_f32"] == [0.5, 1.5]
+        assert m["general.alignment"] == 64
+        assert ck._data[0] % 64 == 0
+        assert np.array_equal(ck.raw("t.a").view(np.float32).reshape(3, 4), np.arange(12, dtype=np.float32).reshape(3, 4))
+        assert np.array_equal(ck.raw("t.b").view(np.float32), np.arange(8, dtype=np.float32))
+        r = gguf.GGUFReader(str(path))
+        for t in r.tensors:
+            assert ck._data[0] + ck.tensors[t.name].offset == int(t.data_offset)

@@ -164,3 +164,16 @@ def test_block_other_format_mixes_match_oracle(pkg, oracle, formats):
         out = _run(pkg, d, x, 10)
         assert np.isfinite(out).all()
         assert _rel(out, _oracle_block(oracle, lay, x, 10)) < TOL
+
+
+def test_formats_rejects_misaligned_weights(pkg, small_layer):
+    """Weight tensors must start 16-byte aligned: an offset view is refused before any launch."""
+    d = _layer_dev(small_layer)
+    x = torch.zeros(1, 512, dtype=torch.bfloat16, device="cuda")
+    flat = torch.zeros(d["down"].numel() + 2, dtype=torch.uint8, device="cuda")
+    shifted = flat[2:].view(d["down"].shape)   # 2 bytes off a 256-byte boundary
+    shifted.copy_(d["down"])
+    with pytest.raises(RuntimeError) as e:
+        pkg.moe_block_formats(x, d["router"], d["gate_vec"], d["gate_up"], shifted, d["sh_gate_up"], d["sh_down"],
+                              d["formats"], 10)
+    assert e.value.status == pkg._lib.QMOE_ERR_ALIGNMENT
