@@ -156,3 +156,54 @@ def test_reader_metadata_types_and_alignment(pkg, tmp_path):
         r = gguf.GGUFReader(str(path))
         for t in r.tensors:
             assert ck._data[0] + ck.tensors[t.name].offset == int(t.data_offset)
+
+
+def _write_iq4xs_layers(path, pkg, cfg, n_layers, seed):
+    qt = gguf.GGMLQuantizationType
+    w = gguf.GGUFWriter(str(path), "qwen4exp")
+    w.add_uint32("qwen4exp.expert_used_count", cfg.top_k)
+    hls = []
+    for L in range(n_layers):
+        hl = pkg.synth_host_layer(cfg, layer=L, seed=seed, all_experts=True)
+        hls.append(hl)
+        gu = np.stack([hl.expert(e)[0] for e in range(cfg.n_experts)])
+        dn = np.stack([hl.expert(e)[1] for e in range(cfg.n_experts)])
+        p = f"blk.{L}."
+        w.add_tensor(p + "ffn_gate_inp.weight", np.ascontiguousarray(hl.router))
+        w.add_tensor(p + "ffn_gate_inp_shexp.weight", np.ascontiguousarray(hl.gate_vec))
+        w.add_tensor(p + "ffn_gate_exps.weight", np.ascontiguousarray(gu[:, :cfg.inter]), raw_dtype=qt.IQ4_XS)
+        w.add_tensor(p + "ffn_up_exps.weight", np.ascontiguousarray(gu[:, cfg.inter:]), raw_dtype=qt.IQ4_XS)
+        w.add_tensor(p + "ffn_down_exps.weight", np.ascontiguousarray(dn), raw_dtype=qt.IQ4_XS)
+        w.add_tensor(p + "ffn_gate_shexp.weight", np.ascontiguousarray(hl.sh_gate_up[:cfg.shared_inter]),
+                     raw_dtype=qt.IQ4_XS)
+        w.add_tensor(p + "ffn_up_shexp.weight", np.ascontiguousarray(hl.sh_gate_up[cfg.shared_inter:]),
+                     raw_dtype=qt.IQ4_XS)
+        w.add_tensor(p + "ffn_down_shexp.weight", np.ascontiguousarray(hl.sh_down), raw_dtype=qt.IQ4_XS)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return hls
+
+
+@pytest.mark.gpu
+def test_iq4xs_checkpoint_runs_the_stack(pkg, tmp_path):
+    """An all-IQ4_XS checkpoint: its layers as DeviceLayers (bytes equal to the generator's), the
+    stack over two of them equal to the layer-by-layer chain of MoELayer calls."""
+    cfg = pkg.MoEConfig(hidden=512, inter=256, n_experts=64, top_k=10, shared_inter=256)
+    path = tmp_path / "iq4xs.gguf"
+    hls = _write_iq4xs_layers(path, pkg, cfg, 2, seed=17)
+    with pkg.GGUFCheckpoint(path) as ck:
+        stack = pkg.load_moe_stack(ck, [0, 1], max_tokens=4)
+        dls = [pkg.gguf_load.device_layer(pkg.moe_layer_bytes(ck, L)) for L in range(2)]
+    ref_dls = [pkg.upload_host_layer(h) for h in hls]
+    for a, b in zip(dls, ref_dls):
+        for key in ("router", "gate_vec", "gate_up", "down", "sh_gate_up", "sh_down"):
+            assert torch.equal(getattr(a, key), getattr(b, key)), key
+    x = (torch.randn(3, 512, generator=torch.Generator().manual_seed(4)) * 0.5).to(torch.bfloat16).cuda()
+    out = stack.decode(x).clone()
+    y = x
+    for dl in ref_dls:
+        y = pkg.MoELayer(dl)(y, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert float((out - y).abs().max()) <= 1e-5 * float(y.abs().max())

@@ -23,7 +23,7 @@ from .moe import (
     route_topk,
     shared_expert,
 )
-from .gguf_load import CheckpointMoE, GGUFCheckpoint, load_moe_layer, moe_layer_bytes
+from .gguf_load import CheckpointMoE, GGUFCheckpoint, load_moe_layer, load_moe_stack, moe_layer_bytes
 from .hc import gated_residual_mix, reinject
 from .stack import MoEStack
 from .weights import (
@@ -48,4 +48,5 @@ __all__ = [
     "CheckpointMoE",
     "load_moe_layer",
     "moe_layer_bytes",
+    "load_moe_stack",
 ]

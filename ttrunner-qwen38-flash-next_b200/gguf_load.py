@@ -284,3 +284,34 @@ def load_moe_layer(ckpt: GGUFCheckpoint, layer: int, device: str | torch.device 
                    top_k: int | None = None) -> CheckpointMoE:
     """Layer `layer`'s MoE block from a checkpoint, on `device`."""
     return CheckpointMoE(moe_layer_bytes(ckpt, layer), device, top_k)
+
+
+def device_layer(lb: MoELayerBytes, device: str | torch.device = "cuda", top_k: int | None = None):
+    """An all-IQ4_XS checkpoint layer as the library's DeviceLayer (unsharded), so the IQ4_XS paths
+    (MoELayer, and MoEStack's single launch over many layers) run it."""
+    from .config import MoEConfig, Shard
+    from .weights import DeviceLayer
+
+    if lb.formats != (IQ4_XS,) * 4:
+        raise ValueError(f"formats {lb.formats}: the IQ4_XS paths need every expert tensor IQ4_XS")
+    k = top_k if top_k is not None else lb.top_k
+    if k is None:
+        raise ValueError("top_k: not in the checkpoint's metadata, pass it")
+    dev = torch.device(device)
+
+    def up(a):
+        return None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    cfg = MoEConfig(hidden=lb.hidden, inter=lb.inter, n_experts=lb.n_experts, top_k=k, shared_inter=lb.shared_inter)
+    return DeviceLayer(cfg=cfg, shard=Shard(), router=up(lb.router), gate_vec=up(lb.gate_vec),
+                       gate_up=up(lb.gate_up), down=up(lb.down), sh_gate_up=up(lb.sh_gate_up),
+                       sh_down=up(lb.sh_down))
+
+
+def load_moe_stack(ckpt: GGUFCheckpoint, layers: list[int], device: str | torch.device = "cuda",
+                   top_k: int | None = None, max_tokens: int = 16):
+    """Consecutive checkpoint layers whose experts are all IQ4_XS as one MoEStack (the 48-layer
+    decode as one launch per step, `qmoe_stack_decode`)."""
+    from .stack import MoEStack
+
+    return MoEStack([device_layer(moe_layer_bytes(ckpt, L), device, top_k) for L in layers], max_tokens=max_tokens)
